@@ -1,0 +1,352 @@
+"""Benchmark of the sparse-voxel hot path on B200 (one JSON line on rank 0).
+
+Workload ``res4_c128`` (the residual-stack configuration): seeded sine-surface
+voxels on a 256^3 grid (364,846 active voxels), four residual blocks
+(LayerNorm -> SiLU -> submanifold conv 3x3x3 -> SiLU -> conv -> +skip) at
+C = 128 with fp16 state and ggml Q8_0 weights.  One step = rebuild the
+topology (hash + 27-tap neighbour map, as the refiner does on every refine
+pass) and run the four blocks (8 sparse convs).
+
+    value = active voxels x sparse convs per step / step time   (device-resident inputs)
+    e2e   = the same, through the C ABI with host buffers: the step's coordinates and
+            features are copied from pinned host memory and the result copied back
+            inside the timed region.
+
+``--impl reference`` times the reference's own CPU implementation (mogecpp
+src/sparse.cpp + ggml CPU backend, compiled from the reference sources into
+oracle/_ref/) on a bounded voxel sample of the same workload.
+
+Multi-GPU (torchrun): each rank runs the workload on its own GPU (independent
+replicas; per-GPU work is fixed, "scaling": "weak"); timing is the max over
+ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+C_CH = 128
+N_BLOCKS = 4
+CONVS_PER_STEP = 2 * N_BLOCKS
+METRIC = "active voxels/s per sparse conv"
+WORKLOAD = "res4_c128"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def workload_inputs():
+    from mogecpp_b200 import synth
+    coords = synth.res4_c128_coords()
+    n = coords.shape[0]
+    x0 = synth.features(2, n, C_CH).astype(np.float16)
+    blocks = []
+    for b in range(N_BLOCKS):
+        rng = np.random.default_rng(1000 + b)
+        blocks.append(dict(norm_w=(1 + 0.1 * rng.standard_normal(C_CH)).astype(np.float32),
+                           norm_b=(0.1 * rng.standard_normal(C_CH)).astype(np.float32),
+                           w1=synth.conv_weight(2000 + 2 * b, C_CH, C_CH),
+                           b1=(0.05 * rng.standard_normal(C_CH)).astype(np.float32),
+                           w2=synth.conv_weight(2001 + 2 * b, C_CH, C_CH),
+                           b2=(0.05 * rng.standard_normal(C_CH)).astype(np.float32)))
+    return coords, x0, blocks
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clocks_setting"}
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"msc_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 4:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+                mask = int(parts[3], 16)
+            except ValueError:
+                continue
+            for bit, name in self.REASONS.items():
+                if mask & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_sample(coords, x0, blocks, target_s: float, n_threads: int):
+    """Times the reference CPU res-block stack on the first voxels of the
+    (b, z, y, x)-ordered set (a z-slab), sized to about target_s per run."""
+    from oracle.oracle import Oracle, Reference, W_Q8_0
+    try:
+        R = Reference(n_threads=n_threads)
+        kind = "reference"
+    except FileNotFoundError:
+        R = None
+        kind = "port"
+    ns = min(coords.shape[0], 4096)
+    for _ in range(3):
+        sub = coords[:ns]
+        if R is not None:
+            nbr = R.make_level(sub)
+            _, sec = R.res_stack(x0[:ns].astype(np.float32), nbr, blocks, W_Q8_0, iters=1)
+        else:
+            O = Oracle()
+            nbr = O.make_level(sub)
+            t0 = time.perf_counter()
+            h = x0[:ns].astype(np.float32)
+            for b in blocks:
+                h = O.res_block(h, nbr, b, W_Q8_0)
+            sec = time.perf_counter() - t0
+        if sec >= 0.5 * target_s or ns == coords.shape[0]:
+            break
+        ns = int(min(coords.shape[0], ns * max(2.0, target_s / max(sec, 1e-3))))
+    return R, kind, ns, sec
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    coords, x0, blocks = workload_inputs()
+    threads = os.cpu_count() or 1
+    from oracle.oracle import W_Q8_0
+    per_step = min(8.0, 150.0 / max(1, args.steps + args.warmup))
+    R, kind, ns, _ = cpu_reference_sample(coords, x0, blocks, per_step, threads)
+    sub = coords[:ns]
+    times = []
+    if R is not None:
+        nbr = R.make_level(sub)
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            R.res_stack(x0[:ns].astype(np.float32), nbr, blocks, W_Q8_0, iters=1)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+    else:
+        from oracle.oracle import Oracle
+        O = Oracle()
+        nbr = O.make_level(sub)
+        threads = 1
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            h = x0[:ns].astype(np.float32)
+            for b in blocks:
+                h = O.res_block(h, nbr, b, W_Q8_0)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+    t = sum(times) / len(times)
+    value = ns * CONVS_PER_STEP / t
+    sample = f"first {ns} of {coords.shape[0]} voxels in (b,z,y,x) order (a z-slab), 4 res blocks, Q8_0"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 x fp32 (ggml CPU)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "voxels": int(ns), "channels": C_CH, "blocks": N_BLOCKS},
+            "cpu_baseline": {"value": value, "unit": "voxels/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    from mogecpp_b200 import synth
+    from mogecpp_b200.sparse import SparseCudaExecutor
+
+    ex = SparseCudaExecutor(local)
+    coords, x0, blocks_np = workload_inputs()
+    n = coords.shape[0]
+    dev = torch.device("cuda", local)
+    coords_d = torch.from_numpy(coords).to(dev)
+    x0_d = torch.from_numpy(x0).to(dev)
+    x_d = torch.empty_like(x0_d)
+    blocks = []
+    for b in blocks_np:
+        blocks.append(dict(norm_w=torch.from_numpy(b["norm_w"]).to(dev), norm_b=torch.from_numpy(b["norm_b"]).to(dev),
+                           b1=torch.from_numpy(b["b1"]).to(dev), b2=torch.from_numpy(b["b2"]).to(dev),
+                           w1=ex.prepare_weight(torch.from_numpy(synth.quantize_q8_0(b["w1"])).to(dev), "q8_0",
+                                                C_CH, C_CH, 27),
+                           w2=ex.prepare_weight(torch.from_numpy(synth.quantize_q8_0(b["w2"])).to(dev), "q8_0",
+                                                C_CH, C_CH, 27)))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        nbr = ex.make_level(coords_d)
+        for blk in blocks:
+            ex.res_block(x_d, nbr, blk)
+        return nbr
+
+    # warm-up (also validates device status once)
+    for _ in range(args.warmup):
+        x_d.copy_(x0_d)
+        nbr = step()
+    ex.check()
+    e_pairs = int((nbr < n).sum().item())
+
+    # ---- device-resident timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ex.profile(True)
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            x_d.copy_(x0_d)
+            flush.fill_(i & 0xff)  # L2 flush between steps (outside the events)
+            ev[i][0].record()
+            step()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+    ex.profile(False)
+    prof = ex.profile_read()
+    ex.check()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    t_ms = sum(step_ms) / len(step_ms)
+    if world > 1:
+        t = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+        dist.barrier()
+    value = world * n * CONVS_PER_STEP / (t_ms * 1e-3)
+
+    # ---- end to end through the C ABI with host buffers
+    h_coords = torch.from_numpy(coords).pin_memory()
+    h_x = torch.from_numpy(x0).pin_memory()
+    h_out = torch.empty_like(h_x).pin_memory()
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.fill_(i & 0xff)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        coords_d.copy_(h_coords, non_blocking=True)
+        x_d.copy_(h_x, non_blocking=True)
+        step()
+        h_out.copy_(x_d, non_blocking=True)
+        b.record()
+        b.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(a.elapsed_time(b))
+    ex.check()
+    e2e_t = sum(e2e_ms) / len(e2e_ms)
+    if world > 1:
+        t = torch.tensor([e2e_t], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_t = float(t.item())
+
+    # ---- roofline of the dominant kernel (tensor-core sparse conv)
+    peak_tf, peak_hbm, peak_src = load_peaks()
+    conv_launches, conv_ms = prof.get("conv_tc", (0, 0.0))
+    flops_per_launch = 2.0 * C_CH * C_CH * e_pairs
+    achieved = flops_per_launch / (conv_ms / max(conv_launches, 1) * 1e-3) / 1e12 if conv_launches else None
+    kernels_per_family = {"make_level": 3, "conv_tc": 1, "act_prepare": 1}
+    launches = sum(kernels_per_family.get(k, 1) * v[0] for k, v in prof.items())
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            R, kind, ns, sec = cpu_reference_sample(coords, x0, blocks_np, 6.0, os.cpu_count() or 1)
+            cpu = {"value": ns * CONVS_PER_STEP / sec, "unit": "voxels/s",
+                   "cores": (os.cpu_count() or 1) if kind == "reference" else 1, "kind": kind,
+                   "sample": f"first {ns} voxels in (b,z,y,x) order (a z-slab), one 4-block stack run"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0 x fp16 (exact fp16 hi/lo split on tcgen05, fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "voxels": n, "valid_pairs": e_pairs, "channels": C_CH,
+                       "blocks": N_BLOCKS, "convs_per_step": CONVS_PER_STEP, "grid": 256,
+                       "step": "make_level + 4 res blocks", "l2": "flushed between steps (256 MiB write)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "e2e": {"value": world * n * CONVS_PER_STEP / (e2e_t * 1e-3), "unit": "voxels/s",
+                    "h2d_bytes_per_step": int(coords.nbytes + x0.nbytes), "d2h_bytes_per_step": int(x0.nbytes),
+                    "ms_per_step": e2e_t},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": (achieved / peak_tf) if achieved else None, "traffic": None,
+                         "kernel": "conv_tc (Q8_0, C=128)", "peak_source": peak_src,
+                         "flops_per_launch": flops_per_launch,
+                         "avg_launch_ms": conv_ms / max(conv_launches, 1)},
+            "effective_tflops_per_conv": achieved,
+            "kernel_ms_per_step": {k: v[1] / args.steps for k, v in prof.items()},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

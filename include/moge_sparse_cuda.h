@@ -1,0 +1,183 @@
+/* moge_sparse_cuda.h - C ABI of the B200 (sm_100a) sparse-voxel path.
+ *
+ * Drop-in device executor for the sparse refiner of mogecpp (moge-ggml
+ * 0.4.2).  Every entry point returns 0 on success or a negative MSC_E_* code
+ * and leaves a message in the calling thread's msc_last_error(), the same
+ * contract as the reference's C API guard (src/moge_c.cpp:20, :65-75) and
+ * moge_last_error() (include/moge_ggml/moge_c.h:80).  No C++ exception
+ * crosses this boundary.
+ *
+ * Memory: all tensors are caller-owned device pointers (the reference keeps
+ * them in ggml backend buffers, src/sparse.cpp:541-558); scratch is passed in
+ * as a caller-owned workspace whose size the *_workspace_bytes queries give.
+ * Streams are cudaStream_t passed as void* (NULL = legacy default stream).
+ * Calls are asynchronous on the stream except where noted ("syncs").
+ *
+ * Layouts (identical to the reference's):
+ *   coords     int32 [n][4] rows (x, y, z, b), 16-byte aligned; x = image
+ *              row, y = image column, z = depth bin (Coord3,
+ *              src/sparse.cpp:69-74) plus the sample index b (the reference
+ *              has no batch field; b keeps samples apart).  0 <= x,y,z < 2^19,
+ *              0 <= b < 127.  Voxel index = row position.
+ *   features   [n][c] row-major (ggml [C, N], ne0 = C), dtype MSC_F32/F16/BF16.
+ *   nbr        int32 [n][27], tap v = (dx+1)*9 + (dy+1)*3 + (dz+1), missing = n
+ *              (SparseLevel::neighbors, src/sparse.cpp:132-137).
+ *   pool_rows  int32 [8][np] slot-major, missing = nfine; inv_count f32 [np];
+ *              up_rows int32 [nfine] (Transition, src/sparse.cpp:139-147).
+ *   weights    packed [cout][27*cin] (cin fastest; "*.weight.mogg_sparse27",
+ *              tools/convert_moge.py:339-349) or linear [cout][cin], as
+ *              MSC_W_F32 floats, MSC_W_F16 halves or MSC_W_Q8_0 ggml
+ *              block_q8_0 rows {fp16 d; int8 qs[32]}.
+ */
+#ifndef MOGE_SPARSE_CUDA_H
+#define MOGE_SPARSE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MSC_ABI_VERSION 1
+
+/* error codes */
+#define MSC_OK 0
+#define MSC_E_INVALID (-1)     /* bad argument, shape or alignment */
+#define MSC_E_UNSUPPORTED (-2) /* shape/dtype combination not built */
+#define MSC_E_CUDA (-3)        /* CUDA runtime error */
+#define MSC_E_DEVICE (-4)      /* device-side failure (bad coordinate, hash full, timeout, ...) */
+#define MSC_E_WORKSPACE (-5)   /* workspace too small */
+
+/* feature dtypes */
+#define MSC_F32 0
+#define MSC_F16 1
+#define MSC_BF16 2
+
+/* weight types (ggml_type values) */
+#define MSC_W_F32 0
+#define MSC_W_F16 1
+#define MSC_W_Q8_0 8
+
+/* device status bits (msc_check) */
+#define MSC_DEV_TIMEOUT 0x1u
+#define MSC_DEV_HASH_FULL 0x2u
+#define MSC_DEV_BAD_COORD 0x4u
+#define MSC_DEV_DUP_COORD 0x8u
+#define MSC_DEV_POOL_OVERFLOW 0x10u
+#define MSC_DEV_BAD_INDEX 0x20u
+
+typedef struct msc_context* msc_ctx_t;
+
+/* Library ABI version (MSC_ABI_VERSION). */
+int msc_abi_version(void);
+
+/* Thread-local message of the last failed call on this thread.
+ * Replaces: moge_last_error (include/moge_ggml/moge_c.h:80). */
+const char* msc_last_error(void);
+
+/* Creates an executor bound to a CUDA device (allocates its 4-byte device
+ * status word).  Mirrors SparseMetalExecutor::create (src/sparse_metal.hpp:21-30):
+ * fails with MSC_E_UNSUPPORTED when the device is not sm_100. */
+int msc_create(int device, msc_ctx_t* out);
+int msc_destroy(msc_ctx_t ctx);
+
+/* Syncs the stream, reads and clears the device status word; returns
+ * MSC_E_DEVICE if any failure bit was set (bits in *bits when non-NULL).
+ * MSC_DEV_DUP_COORD alone is informational (duplicates resolve to the first
+ * index, as FlatCoordMap::emplace does) and does not fail.  Syncs. */
+int msc_check(msc_ctx_t ctx, void* stream, uint32_t* bits);
+
+/* ---------------------------------------------------------------- topology */
+
+/* Workspace bytes for msc_make_level / msc_downsample over n voxels. */
+size_t msc_topology_workspace_bytes(int64_t n);
+
+/* Submanifold neighbour map.
+ * Replaces: make_level (src/sparse.cpp:238-272). */
+int msc_make_level(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr, void* ws, size_t ws_bytes,
+                   void* stream);
+
+/* Stride-2 transition: parent coords [np][4] (capacity n rows), np (device
+ * int32), pool_rows (capacity 8*n, written [8][np]), inv_count, up_rows.
+ * If np_host is non-NULL the call syncs and stores np there; device failures
+ * (duplicate coordinates, which the reference's serial slot numbering does
+ * not define on the GPU) are then reported by the return code.
+ * Replaces: downsample (src/sparse.cpp:312-357) with factor 2. */
+int msc_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev,
+                   int32_t* pool_rows, float* inv_count, int32_t* up_rows, int64_t* np_host, void* ws,
+                   size_t ws_bytes, void* stream);
+
+/* ----------------------------------------------------------------- weights */
+
+/* Bytes of a prepared-weight blob (tensor-core layout). */
+size_t msc_weight_blob_bytes(int wtype, int cin, int cout, int ntaps);
+
+/* Converts packed weights (ntaps = 27 for sparse27 conv weights, 1 for a
+ * linear [cout][cin]) into the blob consumed by the conv / linear calls.
+ * Replaces: the WeightStore upload of "*.weight.mogg_sparse27" tensors
+ * (src/dense.cpp:198-270). */
+int msc_weight_prepare(msc_ctx_t ctx, int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
+                       size_t blob_bytes, void* stream);
+
+/* ----------------------------------------------------------------- operators
+ * Arithmetic follows ggml's mul_mat for the weight type: F32 weights use fp32
+ * products, F16 weights round activations to fp16, Q8_0 weights quantise
+ * activations to Q8_0 per 32 channels (ggml's x86 quantiser) and sum
+ * fp16(d_a)*fp16(d_w)*int_dot per block.  Accumulation is fp32. */
+
+/* Workspace bytes for msc_sparse_conv / msc_linear / msc_res_block /
+ * msc_pool_down / msc_nearest_up on n rows of c channels. */
+size_t msc_op_workspace_bytes(int64_t n, int c);
+
+/* y = sparse_conv(x) + bias.  cin, cout in {64, 128}.
+ * Replaces: sparse_conv (src/sparse.cpp:579-627). */
+int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                    const void* blob, const float* bias, void* y, int y_dtype, void* ws, size_t ws_bytes,
+                    void* stream);
+
+/* y = W x + bias per row.  Replaces: linear (src/sparse.cpp:515-518). */
+int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const void* blob, const float* bias,
+               void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream);
+
+/* In place: x = x + conv2(SiLU(conv1(SiLU(LayerNorm(x))))), LayerNorm eps 1e-6
+ * with affine norm_w / norm_b (either may be NULL).
+ * Replaces: res_block (src/sparse.cpp:629-642) with an identity skip. */
+int msc_res_block(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr, const float* norm_w,
+                  const float* norm_b, const void* blob1, const float* b1, const void* blob2, const float* b2,
+                  void* ws, size_t ws_bytes, void* stream);
+
+/* y [np][cout] = Linear(mean of children).  Replaces: pool_down
+ * (src/sparse.cpp:646-668) with factor 2 (8 slots). */
+int msc_pool_down(msc_ctx_t ctx, const void* x, int x_dtype, int64_t nfine, int c, const int32_t* pool_rows,
+                  const float* inv_count, int64_t np, const void* blob, const float* bias, void* y, int y_dtype,
+                  void* ws, size_t ws_bytes, void* stream);
+
+/* y [nfine][cout] = Linear(x)[up_rows] (+ skip [nfine][cout] when non-NULL).
+ * Replaces: nearest_up (src/sparse.cpp:670-674) and the decoder's skip add
+ * (src/sparse.cpp:1160-1191). */
+int msc_nearest_up(msc_ctx_t ctx, const void* x, int x_dtype, int64_t np, int c, const int32_t* up_rows,
+                   int64_t nfine, const void* blob, const float* bias, const void* skip, int skip_dtype, void* y,
+                   int y_dtype, void* ws, size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------ tracing */
+
+typedef struct {
+    char name[32];      /* kernel family: conv_tc, linear_tc, act_prepare, make_level, ... */
+    int64_t launches;
+    double total_ms;    /* summed CUDA-event durations on the launching stream */
+} msc_profile_entry;
+
+/* Enables / disables per-launch CUDA-event timing of this context's kernels.
+ * Replaces: MOGE_OP_PROFILE's per-node eval callback (src/profiling.hpp:50-71). */
+int msc_profile_enable(msc_ctx_t ctx, int enable);
+
+/* Aggregates the recorded launches per kernel family into out[0..capacity)
+ * and clears them; *count = number of families.  Syncs on the events. */
+int msc_profile_read(msc_ctx_t ctx, msc_profile_entry* out, int capacity, int* count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOGE_SPARSE_CUDA_H */

@@ -1,0 +1,512 @@
+// extern "C" boundary of the sparse-voxel path (include/moge_sparse_cuda.h).
+//
+// Error contract mirrors the reference C API (src/moge_c.cpp:20, :65-75):
+// every call runs inside guard(), which converts exceptions into a negative
+// status and a thread-local message; nothing throws across the boundary.
+#include "conv.h"
+#include "ops.h"
+#include "topology.h"
+
+#include "../../include/moge_sparse_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+#include <cstring>
+
+struct msc_context {
+    int device = 0;
+    uint32_t* status = nullptr;  // device status word
+    struct Blob {
+        int wtype, cin, cout, ntaps, planes;
+        size_t bytes;
+    };
+    std::mutex mu;
+    std::unordered_map<const void*, Blob> blobs;
+    // kernel profiling (msc_profile_*): one event pair per launch
+    struct Rec {
+        const char* name;
+        cudaEvent_t a, b;
+    };
+    bool prof = false;
+    std::vector<Rec> recs;
+    std::vector<cudaEvent_t> pool;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+struct Failure : std::runtime_error {
+    int code;
+    Failure(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Failure(code, msg); }
+
+void cuda_ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fail(MSC_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <class F>
+int guard(F&& f) {
+    try {
+        f();
+        return MSC_OK;
+    } catch (const Failure& e) {
+        g_err = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return MSC_E_INVALID;
+    } catch (...) {
+        g_err = "unknown error";
+        return MSC_E_INVALID;
+    }
+}
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+cudaEvent_t take_event(msc_ctx_t ctx) {
+    if (!ctx->pool.empty()) {
+        cudaEvent_t e = ctx->pool.back();
+        ctx->pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) fail(MSC_E_CUDA, "cudaEventCreate failed");
+    return e;
+}
+
+// Brackets one kernel launch with CUDA events when profiling is enabled
+// (the counterpart of the reference's MOGE_OP_PROFILE per-node callback,
+// src/profiling.hpp:50-71).
+struct ProfScope {
+    msc_ctx_t ctx;
+    cudaStream_t st;
+    cudaEvent_t b = nullptr;
+    const char* name;
+    cudaEvent_t a = nullptr;
+    ProfScope(msc_ctx_t c, const char* n, cudaStream_t s) : ctx(c), st(s), name(n) {
+        if (ctx->prof) {
+            a = take_event(ctx);
+            cudaEventRecord(a, st);
+        }
+    }
+    ~ProfScope() {
+        if (a) {
+            b = take_event(ctx);
+            cudaEventRecord(b, st);
+            ctx->recs.push_back({name, a, b});
+        }
+    }
+};
+
+void need(bool cond, const char* msg) {
+    if (!cond) fail(MSC_E_INVALID, msg);
+}
+
+void need_dtype(int dt, const char* what) {
+    if (dt != MSC_F32 && dt != MSC_F16 && dt != MSC_BF16) fail(MSC_E_INVALID, std::string("bad dtype for ") + what);
+}
+
+void need_aligned(const void* p, size_t a, const char* what) {
+    if (reinterpret_cast<uintptr_t>(p) % a) fail(MSC_E_INVALID, std::string(what) + " is not " + std::to_string(a) + "-byte aligned");
+}
+
+void need_ctx(msc_ctx_t ctx) {
+    if (!ctx) fail(MSC_E_INVALID, "null context");
+    int dev = -1;
+    cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev != ctx->device) fail(MSC_E_INVALID, "context belongs to device " + std::to_string(ctx->device) +
+                                                  " but the current device is " + std::to_string(dev));
+}
+
+msc_context::Blob blob_info(msc_ctx_t ctx, const void* blob) {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    auto it = ctx->blobs.find(blob);
+    if (it == ctx->blobs.end()) fail(MSC_E_INVALID, "weight blob was not prepared by this context");
+    return it->second;
+}
+
+int act_mode(int wtype, int x_dtype) {
+    if (wtype == MSC_W_Q8_0) return msc::ACT_Q8;
+    if (wtype == MSC_W_F16) return msc::ACT_FP16;
+    return x_dtype == MSC_F16 ? msc::ACT_FP16 : msc::ACT_SPLIT;
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+cudaError_t act_prepare(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int c, int ln, const float* gamma,
+                        const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st) {
+    ProfScope ps(ctx, "act_prepare", st);
+    return msc::launch_act_prepare(x, x_dtype, n, c, ln, gamma, beta, eps, silu, mode, planes, st);
+}
+
+void need_ws(size_t have, size_t want) {
+    if (have < want)
+        fail(MSC_E_WORKSPACE, "workspace too small: " + std::to_string(have) + " < " + std::to_string(want));
+}
+
+void run_conv(msc_ctx_t ctx, const void* planes, int na, int64_t n, int cin, const int32_t* nbr,
+              const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
+              int res_dtype, void* y, int y_dtype, cudaStream_t st) {
+    msc::ConvArgs a{};
+    a.planes = planes;
+    a.na = na;
+    a.n = n;
+    a.cin = cin;
+    a.nbr = nbr;
+    a.blob = blob;
+    a.wplanes = b.planes;
+    a.cout = b.cout;
+    a.ntaps = b.ntaps;
+    a.bias = bias;
+    a.silu_out = silu_out;
+    a.residual = residual;
+    a.res_dtype = res_dtype;
+    a.y = y;
+    a.y_dtype = y_dtype;
+    a.status = ctx->status;
+    ProfScope ps(ctx, nbr ? "conv_tc" : "linear_tc", st);
+    cuda_ok(msc::launch_conv(a, st), "conv launch");
+}
+
+void check_conv_shape(const msc_context::Blob& b, int cin, int ntaps) {
+    if (b.cin != cin) fail(MSC_E_INVALID, "weight cin " + std::to_string(b.cin) + " != input channels " + std::to_string(cin));
+    if (b.ntaps != ntaps) fail(MSC_E_INVALID, "weight has " + std::to_string(b.ntaps) + " taps, expected " + std::to_string(ntaps));
+    if (!msc::conv_supported(b.cin, b.cout))
+        fail(MSC_E_UNSUPPORTED, "conv/linear shape " + std::to_string(b.cin) + "->" + std::to_string(b.cout) +
+                                    " not built (channels must be 64 or 128)");
+}
+
+}  // namespace
+
+extern "C" {
+
+int msc_abi_version(void) { return MSC_ABI_VERSION; }
+
+const char* msc_last_error(void) { return g_err.c_str(); }
+
+int msc_create(int device, msc_ctx_t* out) {
+    return guard([&] {
+        need(out != nullptr, "null output pointer");
+        cudaDeviceProp prop{};
+        cuda_ok(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10 || prop.minor != 0)
+            fail(MSC_E_UNSUPPORTED, "device " + std::to_string(device) + " is sm_" + std::to_string(prop.major) +
+                                        std::to_string(prop.minor) + "; this library is built for sm_100a");
+        cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+        auto* c = new msc_context();
+        c->device = device;
+        cudaError_t e = cudaMalloc(&c->status, sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+        if (e != cudaSuccess) {
+            if (c->status) cudaFree(c->status);
+            delete c;
+            cuda_ok(e, "status word allocation");
+        }
+        *out = c;
+    });
+}
+
+int msc_destroy(msc_ctx_t ctx) {
+    return guard([&] {
+        if (!ctx) return;
+        if (ctx->status) cudaFree(ctx->status);
+        for (auto& r : ctx->recs) {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+        for (auto e : ctx->pool) cudaEventDestroy(e);
+        delete ctx;
+    });
+}
+
+int msc_check(msc_ctx_t ctx, void* stream, uint32_t* bits) {
+    return guard([&] {
+        need_ctx(ctx);
+        uint32_t h = 0;
+        cuda_ok(cudaMemcpyAsync(&h, ctx->status, sizeof(h), cudaMemcpyDeviceToHost, S(stream)), "status read");
+        cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), S(stream)), "status clear");
+        cuda_ok(cudaStreamSynchronize(S(stream)), "stream sync");
+        if (bits) *bits = h;
+        const uint32_t failing = h & ~MSC_DEV_DUP_COORD;
+        if (failing) {
+            std::string m = "device failure:";
+            if (h & MSC_DEV_TIMEOUT) m += " wait-timeout";
+            if (h & MSC_DEV_HASH_FULL) m += " hash-full";
+            if (h & MSC_DEV_BAD_COORD) m += " coordinate-out-of-range";
+            if (h & MSC_DEV_POOL_OVERFLOW) m += " pool-slot-overflow";
+            if (h & MSC_DEV_BAD_INDEX) m += " index-out-of-range";
+            fail(MSC_E_DEVICE, m);
+        }
+    });
+}
+
+size_t msc_topology_workspace_bytes(int64_t n) { return n < 0 ? 0 : msc::topology_workspace_bytes(n); }
+
+int msc_make_level(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr, void* ws, size_t ws_bytes,
+                   void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        if (n == 0) return;
+        need(coords && nbr && ws, "null pointer");
+        need_aligned(coords, 16, "coords");
+        need_aligned(ws, 16, "workspace");
+        need_ws(ws_bytes, msc::topology_workspace_bytes(n));
+        ProfScope ps(ctx, "make_level", S(stream));
+        cuda_ok(msc::launch_make_level(coords, n, nbr, ws, ctx->status, S(stream)), "make_level launch");
+    });
+}
+
+int msc_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev,
+                   int32_t* pool_rows, float* inv_count, int32_t* up_rows, int64_t* np_host, void* ws,
+                   size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(n >= 0 && n < (int64_t(1) << 31) / 8, "voxel count out of range");
+        need(np_dev != nullptr, "null np pointer");
+        if (n > 0) {
+            need(coords && parent && pool_rows && inv_count && up_rows && ws, "null pointer");
+            need_aligned(coords, 16, "coords");
+            need_aligned(parent, 16, "parent");
+            need_aligned(ws, 16, "workspace");
+            need_ws(ws_bytes, msc::topology_workspace_bytes(n));
+        }
+        {
+            ProfScope ps(ctx, "downsample", S(stream));
+            cuda_ok(msc::launch_downsample(coords, n, parent, np_dev, pool_rows, inv_count, up_rows, ws, ctx->status,
+                                           S(stream)),
+                    "downsample launch");
+        }
+        if (np_host) {
+            int32_t h = 0;
+            cuda_ok(cudaMemcpyAsync(&h, np_dev, sizeof(h), cudaMemcpyDeviceToHost, S(stream)), "np read");
+            uint32_t bits = 0;
+            cuda_ok(cudaMemcpyAsync(&bits, ctx->status, sizeof(bits), cudaMemcpyDeviceToHost, S(stream)), "status read");
+            cuda_ok(cudaStreamSynchronize(S(stream)), "stream sync");
+            *np_host = h;
+            if (bits & MSC_DEV_DUP_COORD) {
+                cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), S(stream)), "status clear");
+                fail(MSC_E_DEVICE, "duplicate voxel coordinates: stride-2 slot numbering needs unique voxels");
+            }
+            if (bits & ~MSC_DEV_DUP_COORD) {
+                cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), S(stream)), "status clear");
+                fail(MSC_E_DEVICE, "device failure in downsample (status bits " + std::to_string(bits) + ")");
+            }
+        }
+    });
+}
+
+size_t msc_weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
+    if ((wtype != MSC_W_F32 && wtype != MSC_W_F16 && wtype != MSC_W_Q8_0) || cin <= 0 || cout <= 0 || ntaps <= 0)
+        return 0;
+    return msc::weight_blob_bytes(wtype, cin, cout, ntaps);
+}
+
+int msc_weight_prepare(msc_ctx_t ctx, int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
+                       size_t blob_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(wtype == MSC_W_F32 || wtype == MSC_W_F16 || wtype == MSC_W_Q8_0, "unknown weight type");
+        need(ntaps == 27 || ntaps == 1, "ntaps must be 27 (sparse conv) or 1 (linear)");
+        need(w && blob, "null pointer");
+        need(cin > 0 && cout > 0, "bad channel counts");
+        if (cin % 64 != 0) fail(MSC_E_UNSUPPORTED, "cin must be a multiple of 64");
+        if (wtype == MSC_W_Q8_0) need(cin % 32 == 0, "Q8_0 rows need cin % 32 == 0");
+        need_aligned(blob, 256, "weight blob");
+        const size_t want = msc::weight_blob_bytes(wtype, cin, cout, ntaps);
+        need_ws(blob_bytes, want);
+        cuda_ok(msc::launch_weight_prepare(wtype, w, cin, cout, ntaps, blob, S(stream)), "weight prepare launch");
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        ctx->blobs[blob] = msc_context::Blob{wtype, cin, cout, ntaps, msc::weight_planes(wtype), want};
+    });
+}
+
+size_t msc_op_workspace_bytes(int64_t n, int c) {
+    if (n < 0 || c <= 0) return 0;
+    return align256(static_cast<size_t>(n) * c * 4) + align256(static_cast<size_t>(n) * c * 4) + 256;
+}
+
+int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                    const void* blob, const float* bias, void* y, int y_dtype, void* ws, size_t ws_bytes,
+                    void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need_dtype(y_dtype, "y");
+        const auto b = blob_info(ctx, blob);
+        check_conv_shape(b, cin, 27);
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        if (n == 0) return;
+        need(x && nbr && y && ws, "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(y, 16, "y");
+        need_aligned(ws, 256, "workspace");
+        const int mode = act_mode(b.wtype, x_dtype);
+        const int na = msc::act_planes(mode);
+        need_ws(ws_bytes, static_cast<size_t>(na) * n * cin * 2);
+        cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
+                "activation prepare");
+        run_conv(ctx, ws, na, n, cin, nbr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
+    });
+}
+
+int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const void* blob, const float* bias,
+               void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need_dtype(y_dtype, "y");
+        const auto b = blob_info(ctx, blob);
+        check_conv_shape(b, cin, 1);
+        need(n >= 0, "negative row count");
+        if (n == 0) return;
+        need(x && y && ws, "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(y, 16, "y");
+        need_aligned(ws, 256, "workspace");
+        const int mode = act_mode(b.wtype, x_dtype);
+        const int na = msc::act_planes(mode);
+        need_ws(ws_bytes, static_cast<size_t>(na) * n * cin * 2);
+        cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
+                "activation prepare");
+        run_conv(ctx, ws, na, n, cin, nullptr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
+    });
+}
+
+int msc_res_block(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr, const float* norm_w,
+                  const float* norm_b, const void* blob1, const float* b1, const void* blob2, const float* b2,
+                  void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        const auto w1 = blob_info(ctx, blob1);
+        const auto w2 = blob_info(ctx, blob2);
+        check_conv_shape(w1, c, 27);
+        check_conv_shape(w2, c, 27);
+        need(w1.cout == c && w2.cout == c, "res_block convs must map c -> c");
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        if (n == 0) return;
+        need(x && nbr && ws, "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(ws, 256, "workspace");
+        const size_t planes_bytes = align256(static_cast<size_t>(n) * c * 4);
+        need_ws(ws_bytes, planes_bytes + static_cast<size_t>(n) * c * 4);
+        void* planes = ws;
+        float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
+        const int m1 = act_mode(w1.wtype, x_dtype);
+        cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
+                "norm1 prepare");
+        run_conv(ctx, planes, msc::act_planes(m1), n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream));
+        const int m2 = act_mode(w2.wtype, MSC_F32);
+        cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
+                "conv2 prepare");
+        run_conv(ctx, planes, msc::act_planes(m2), n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream));
+    });
+}
+
+int msc_pool_down(msc_ctx_t ctx, const void* x, int x_dtype, int64_t nfine, int c, const int32_t* pool_rows,
+                  const float* inv_count, int64_t np, const void* blob, const float* bias, void* y, int y_dtype,
+                  void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need_dtype(y_dtype, "y");
+        const auto b = blob_info(ctx, blob);
+        check_conv_shape(b, c, 1);
+        need(np >= 0 && np <= nfine, "parent count out of range");
+        if (np == 0) return;
+        need(x && pool_rows && inv_count && y && ws, "null pointer");
+        need_aligned(y, 16, "y");
+        need_aligned(ws, 256, "workspace");
+        const size_t pooled_bytes = align256(static_cast<size_t>(np) * c * 4);
+        const int mode = act_mode(b.wtype, MSC_F32);
+        need_ws(ws_bytes, pooled_bytes + static_cast<size_t>(msc::act_planes(mode)) * np * c * 2);
+        float* pooled = static_cast<float*>(ws);
+        void* planes = static_cast<char*>(ws) + pooled_bytes;
+        ProfScope pm(ctx, "pool_mean", S(stream));
+        cuda_ok(msc::launch_pool_mean(x, x_dtype, nfine, c, pool_rows, inv_count, np, pooled, ctx->status, S(stream)),
+                "pool mean");
+        cuda_ok(act_prepare(ctx, pooled, MSC_F32, np, c, 0, nullptr, nullptr, 0.f, 0, mode, planes, S(stream)),
+                "pool prepare");
+        run_conv(ctx, planes, msc::act_planes(mode), np, c, nullptr, b, blob, bias, 0, nullptr, 0, y, y_dtype,
+                 S(stream));
+    });
+}
+
+int msc_nearest_up(msc_ctx_t ctx, const void* x, int x_dtype, int64_t np, int c, const int32_t* up_rows,
+                   int64_t nfine, const void* blob, const float* bias, const void* skip, int skip_dtype, void* y,
+                   int y_dtype, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need_dtype(y_dtype, "y");
+        if (skip) need_dtype(skip_dtype, "skip");
+        const auto b = blob_info(ctx, blob);
+        check_conv_shape(b, c, 1);
+        need(np >= 0 && nfine >= 0, "negative sizes");
+        if (nfine == 0) return;
+        need(np > 0, "upsampling from an empty level");
+        need(x && up_rows && y && ws, "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(ws, 256, "workspace");
+        const int mode = act_mode(b.wtype, x_dtype);
+        const size_t planes_bytes = align256(static_cast<size_t>(msc::act_planes(mode)) * np * c * 2);
+        need_ws(ws_bytes, planes_bytes + static_cast<size_t>(np) * b.cout * 4);
+        void* planes = ws;
+        float* t = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
+        cuda_ok(act_prepare(ctx, x, x_dtype, np, c, 0, nullptr, nullptr, 0.f, 0, mode, planes, S(stream)),
+                "up prepare");
+        run_conv(ctx, planes, msc::act_planes(mode), np, c, nullptr, b, blob, bias, 0, nullptr, 0, t, MSC_F32,
+                 S(stream));
+        ProfScope pg(ctx, "gather_rows", S(stream));
+        cuda_ok(msc::launch_gather_rows(t, np, b.cout, up_rows, nfine, skip, skip_dtype, y, y_dtype, ctx->status,
+                                        S(stream)),
+                "up gather");
+    });
+}
+
+int msc_profile_enable(msc_ctx_t ctx, int enable) {
+    return guard([&] {
+        need_ctx(ctx);
+        ctx->prof = enable != 0;
+    });
+}
+
+int msc_profile_read(msc_ctx_t ctx, msc_profile_entry* out, int capacity, int* count) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(count != nullptr, "null count pointer");
+        std::vector<msc_profile_entry> agg;
+        for (auto& r : ctx->recs) {
+            cuda_ok(cudaEventSynchronize(r.b), "profile event sync");
+            float ms = 0.f;
+            cuda_ok(cudaEventElapsedTime(&ms, r.a, r.b), "profile elapsed time");
+            msc_profile_entry* e = nullptr;
+            for (auto& x : agg)
+                if (std::strncmp(x.name, r.name, sizeof(x.name)) == 0) e = &x;
+            if (!e) {
+                agg.push_back(msc_profile_entry{});
+                e = &agg.back();
+                std::strncpy(e->name, r.name, sizeof(e->name) - 1);
+            }
+            e->launches += 1;
+            e->total_ms += ms;
+            ctx->pool.push_back(r.a);
+            ctx->pool.push_back(r.b);
+        }
+        ctx->recs.clear();
+        *count = static_cast<int>(agg.size());
+        for (int i = 0; i < static_cast<int>(agg.size()) && i < capacity && out; ++i) out[i] = agg[i];
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,206 @@
+// Operand preparation for the tensor-core sparse conv:
+//
+//  * weights: packed [cout][ntaps*cin] (f32, f16 or ggml block_q8_0 rows) ->
+//    blob of 128B-swizzled K-major fp16 tiles [tap][64-ch chunk][plane][cout][64].
+//    f16 weights are one exact plane; f32 and Q8_0 weights (dequantised to
+//    their exact fp32 value d*q) become an exact hi/lo pair after a
+//    power-of-two prescale that puts max|w| near 2^14 (undone in the conv
+//    epilogue).
+//  * activations: [n][c] rows (f32/f16/bf16), optional LayerNorm + SiLU
+//    (mogecpp src/sparse.cpp:520-526, ggml norm_f32 / silu), then
+//      ACT_FP16  round to fp16                      (ggml F16 vec_dot_type)
+//      ACT_SPLIT exact hi/lo fp16 pair of the fp32  (ggml F32 x F32)
+//      ACT_Q8    ggml's x86 Q8_0 quantiser per 32 channels (d = amax/127,
+//                id = 127/amax, round-half-even; ggml-cpu/arch/x86/quants.c:302)
+//                then the exact hi/lo pair of q * fp16(d)  (Q8_0 vec_dot_type)
+#include "common.cuh"
+#include "conv.h"
+
+namespace msc {
+namespace {
+
+struct BlockQ8 {
+    __half d;
+    int8_t qs[32];
+};
+static_assert(sizeof(BlockQ8) == 34, "block_q8_0 is 34 bytes");
+
+__device__ __forceinline__ float weight_value(int wtype, const void* w, int64_t row_len, int o, int64_t k) {
+    if (wtype == WT_F32) return static_cast<const float*>(w)[o * row_len + k];
+    if (wtype == WT_F16) return __half2float(static_cast<const __half*>(w)[o * row_len + k]);
+    const BlockQ8* b = static_cast<const BlockQ8*>(w) + (o * row_len + k) / 32;
+    return static_cast<float>(b->qs[k % 32]) * __half2float(b->d);
+}
+
+__global__ void weight_header_kernel(WeightHeader* h, int wtype, int cin, int cout, int ntaps, int planes) {
+    h->magic = kWeightMagic;
+    h->wtype = wtype;
+    h->cin = cin;
+    h->cout = cout;
+    h->ntaps = ntaps;
+    h->planes = planes;
+    h->oscale = 1.0f;
+    h->amax = 0.0f;
+}
+
+__global__ void weight_amax_kernel(WeightHeader* h, int wtype, const void* w, int64_t row_len, int cout) {
+    float m = 0.0f;
+    const int64_t total = row_len * cout;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        m = fmaxf(m, fabsf(weight_value(wtype, w, row_len, static_cast<int>(i / row_len), i % row_len)));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned*>(&h->amax), __float_as_uint(m));
+}
+
+__device__ __forceinline__ int prescale_exp(float amax) {
+    if (!(amax > 0.0f)) return 0;
+    int e;
+    frexpf(amax, &e);  // amax = f * 2^e, f in [0.5, 1)
+    return 14 - e;     // amax * 2^s in [2^13, 2^14)
+}
+
+__global__ void weight_split_kernel(WeightHeader* h, int wtype, const void* w, int cin, int cout, int ntaps,
+                                    int planes, uint8_t* out) {
+    const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
+    const int64_t total = row_len * cout;
+    const int s = planes == 2 ? prescale_exp(h->amax) : 0;
+    const int kch = cin / 64;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int o = static_cast<int>(i / row_len);
+        const int64_t k = i % row_len;
+        const int t = static_cast<int>(k / cin);
+        const int ci = static_cast<int>(k % cin);
+        const int kc = ci / 64, e = ci % 64;
+        const float v = ldexpf(weight_value(wtype, w, row_len, o, k), s);
+        __half hi, lo;
+        if (planes == 2) {
+            split_f16(v, hi, lo);
+        } else {
+            hi = __float2half_rn(v);
+            lo = __float2half_rn(0.0f);
+        }
+        const int64_t tile = static_cast<int64_t>(t * kch + kc) * planes;
+        const uint32_t off = sw128_offset(o, e >> 3) + (e & 7) * 2;
+        *reinterpret_cast<__half*>(out + (tile + 0) * cout * 128 + off) = hi;
+        if (planes == 2) *reinterpret_cast<__half*>(out + (tile + 1) * cout * 128 + off) = lo;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) h->oscale = ldexpf(1.0f, -s);
+}
+
+// One warp per row; lane l holds channels [l*EPL, (l+1)*EPL).
+template <int C>
+__global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
+                                   const float* beta, float eps, int silu, int mode, __half* planes) {
+    constexpr int EPL = C / 32;
+    const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    float v[EPL];
+    const int64_t base = row * C + lane * EPL;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+        if (x_dtype == DT_F32)
+            v[k] = static_cast<const float*>(x)[base + k];
+        else if (x_dtype == DT_F16)
+            v[k] = __half2float(static_cast<const __half*>(x)[base + k]);
+        else
+            v[k] = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base + k]);
+    }
+    if (ln) {
+        float s = 0.0f;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) s += v[k];
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s / C;
+        float q = 0.0f;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            const float d = v[k] - mean;
+            q = fmaf(d, d, q);
+        }
+        for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        const float scale = 1.0f / sqrtf(q / C + eps);
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            float t = __fmul_rn(v[k] - mean, scale);
+            if (gamma) t = __fmul_rn(t, gamma[lane * EPL + k]);
+            if (beta) t = __fadd_rn(t, beta[lane * EPL + k]);
+            v[k] = t;
+        }
+    }
+    if (silu) {
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) v[k] = silu_f(v[k]);
+    }
+    const int64_t plane = n * C;
+    if (mode == ACT_FP16) {
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) planes[base + k] = __float2half_rn(v[k]);
+        return;
+    }
+    if (mode == ACT_Q8) {
+        // 32-channel blocks span 32/EPL lanes
+        float amax = 0.0f;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) amax = fmaxf(amax, fabsf(v[k]));
+        for (int o = 1; o < 32 / EPL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const float dq = __half2float(__float2half_rn(d));
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            const int q = __float2int_rn(__fmul_rn(v[k], id));
+            v[k] = static_cast<float>(q) * dq;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+        __half hi, lo;
+        split_f16(v[k], hi, lo);
+        planes[base + k] = hi;
+        planes[plane + base + k] = lo;
+    }
+}
+
+}  // namespace
+
+int weight_planes(int wtype) { return wtype == WT_F16 ? 1 : 2; }
+
+size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
+    return sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype)) * ntaps * cin * cout * 2;
+}
+
+cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
+                                  cudaStream_t st) {
+    auto* h = static_cast<WeightHeader*>(blob);
+    const int planes = weight_planes(wtype);
+    const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
+    weight_header_kernel<<<1, 1, 0, st>>>(h, wtype, cin, cout, ntaps, planes);
+    if (planes == 2) weight_amax_kernel<<<148, 256, 0, st>>>(h, wtype, w, row_len, cout);
+    const int64_t total = row_len * cout;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    weight_split_kernel<<<grid, 256, 0, st>>>(h, wtype, w, cin, cout, ntaps, planes,
+                                              static_cast<uint8_t*>(blob) + sizeof(WeightHeader));
+    return cudaGetLastError();
+}
+
+int act_planes(int mode) { return mode == ACT_FP16 ? 1 : 2; }
+
+cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int ln, const float* gamma,
+                               const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const unsigned grid = static_cast<unsigned>((n * 32 + 255) / 256);
+    auto* out = static_cast<__half*>(planes);
+    switch (c) {
+        case 32: act_prepare_kernel<32><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
+        case 64: act_prepare_kernel<64><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
+        case 128: act_prepare_kernel<128><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
+        case 256: act_prepare_kernel<256><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace msc

@@ -1,0 +1,22 @@
+// Host launchers for the topology kernels (topology.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace msc {
+
+// Device scratch needed by launch_make_level / launch_downsample for n voxels.
+size_t topology_workspace_bytes(int64_t n);
+
+// coords: [n][4] int32 (x, y, z, b), 16-byte aligned.  nbr: [n][27] int32.
+cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, void* ws, uint32_t* status,
+                              cudaStream_t st);
+
+// parent: [n][4] capacity; np_dev: one device int32; pool_rows: [8][n]
+// capacity (written slot-major with stride np); inv_count, up_rows: [n].
+cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
+                              float* inv_count, int32_t* up_rows, void* ws, uint32_t* status, cudaStream_t st);
+
+}  // namespace msc

@@ -1,0 +1,78 @@
+"""ctypes binding of ``libmoge_sparse_cuda.so`` (C ABI: include/moge_sparse_cuda.h).
+
+Loading fails loudly when the library has not been built: there is no CPU or
+PyTorch fallback for any operator of this package.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libmoge_sparse_cuda.so")
+
+MSC_OK = 0
+MSC_F32, MSC_F16, MSC_BF16 = 0, 1, 2
+MSC_W_F32, MSC_W_F16, MSC_W_Q8_0 = 0, 1, 8
+DEV_TIMEOUT, DEV_HASH_FULL, DEV_BAD_COORD, DEV_DUP_COORD, DEV_POOL_OVERFLOW, DEV_BAD_INDEX = 1, 2, 4, 8, 16, 32
+
+_vp, _i64, _sz, _i32 = C.c_void_p, C.c_int64, C.c_size_t, C.c_int
+
+# name -> (restype, argtypes); the exported set of the C ABI
+SIGNATURES = {
+    "msc_abi_version": (C.c_int, []),
+    "msc_last_error": (C.c_char_p, []),
+    "msc_create": (C.c_int, [_i32, C.POINTER(_vp)]),
+    "msc_destroy": (C.c_int, [_vp]),
+    "msc_check": (C.c_int, [_vp, _vp, C.POINTER(C.c_uint32)]),
+    "msc_topology_workspace_bytes": (_sz, [_i64]),
+    "msc_make_level": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "msc_downsample": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, C.POINTER(_i64), _vp, _sz, _vp]),
+    "msc_weight_blob_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "msc_weight_prepare": (C.c_int, [_vp, _i32, _vp, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "msc_op_workspace_bytes": (_sz, [_i64, _i32]),
+    "msc_sparse_conv": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
+    "msc_linear": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
+    "msc_res_block": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "msc_pool_down": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
+    "msc_nearest_up": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _sz,
+                                 _vp]),
+    "msc_profile_enable": (C.c_int, [_vp, _i32]),
+    "msc_profile_read": (C.c_int, [_vp, _vp, _i32, C.POINTER(_i32)]),
+}
+
+
+class ProfileEntry(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("launches", C.c_int64), ("total_ms", C.c_double)]
+
+
+class MscError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+_LIB = None
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Loads and types the library; raises if it is missing."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is not built: run `python -m mogecpp_b200.build` "
+                          "(this package has no CPU fallback)")
+    lib = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != MSC_OK:
+        raise MscError(rc, load().msc_last_error().decode())

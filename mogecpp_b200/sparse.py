@@ -1,0 +1,200 @@
+"""Host-side mirror of the reference's sparse operator surface, on the B200 path.
+
+``SparseCudaExecutor`` plays the role of the reference's backend executor
+seam (``SparseMetalExecutor``, src/sparse_metal.hpp:21-52): ``create()`` binds
+a CUDA device and fails on anything but sm_100, and its methods are the
+refiner's operators with the reference's names and argument meaning
+(src/sparse.cpp):
+
+    make_level(coords)                    -> nbr [n, 27]          (:238-272)
+    downsample(coords)                    -> Transition           (:312-357)
+    sparse_conv(x, nbr, w, bias)          -> y [n, cout]          (:579-627)
+    res_block(x, nbr, block)              -> x (in place)         (:629-642)
+    pool_down(x, tr, w, bias)             -> y [np, cout]         (:646-668)
+    nearest_up(x, tr, w, bias, skip)      -> y [nfine, cout]      (:670-674)
+    linear(x, w, bias)                    -> y [n, cout]          (:515-518)
+
+Every call goes through the C ABI of ``libmoge_sparse_cuda.so``; tensors are
+torch CUDA tensors used only as device memory.  Errors raise ``MscError``
+with the library's message, as the reference throws ``std::runtime_error``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import lib as L
+
+_DT = {torch.float32: L.MSC_F32, torch.float16: L.MSC_F16, torch.bfloat16: L.MSC_BF16}
+_WT = {"f32": L.MSC_W_F32, "f16": L.MSC_W_F16, "q8_0": L.MSC_W_Q8_0}
+
+
+def _p(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@dataclass
+class Transition:
+    """Stride-2 maps (reference ``Transition``, src/sparse.cpp:139-147)."""
+    parent: torch.Tensor      # [np, 4] int32 parent coordinates
+    pool_rows: torch.Tensor   # [8, np] int32, slot-major, sentinel nfine
+    inv_count: torch.Tensor   # [np] float32
+    up_rows: torch.Tensor     # [nfine] int32
+    np: int
+    nfine: int
+
+
+@dataclass
+class PreparedWeight:
+    """Weights converted once into the tensor-core blob (``msc_weight_prepare``)."""
+    blob: torch.Tensor
+    wtype: str
+    cin: int
+    cout: int
+    ntaps: int
+
+
+class SparseCudaExecutor:
+    def __init__(self, device: int = 0):
+        self.lib = L.load()
+        self.device = device
+        torch.cuda.set_device(device)
+        h = C.c_void_p()
+        L.check(self.lib.msc_create(device, C.byref(h)))
+        self.ctx = h
+        self._ws = None
+
+    @classmethod
+    def create(cls, device: int = 0) -> "SparseCudaExecutor | None":
+        """Returns None when no sm_100 device is available (as the reference's
+        stub executor does, src/sparse_metal_stub.cpp:18-20)."""
+        try:
+            if not torch.cuda.is_available():
+                return None
+            return cls(device)
+        except (L.MscError, RuntimeError):
+            return None
+
+    def close(self):
+        if self.ctx:
+            self.lib.msc_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---------------------------------------------------------- plumbing
+    def workspace(self, nbytes: int) -> torch.Tensor:
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=f"cuda:{self.device}")
+        return self._ws
+
+    def check(self) -> int:
+        """Syncs the current stream and raises on any device-side failure."""
+        bits = C.c_uint32(0)
+        L.check(self.lib.msc_check(self.ctx, _stream(), C.byref(bits)))
+        return bits.value
+
+    def profile(self, enable: bool = True) -> None:
+        """Starts / stops per-launch CUDA-event timing of this executor's kernels."""
+        L.check(self.lib.msc_profile_enable(self.ctx, int(enable)))
+
+    def profile_read(self) -> dict:
+        """{kernel family: (launches, total ms)} since the last read; syncs."""
+        buf = (L.ProfileEntry * 32)()
+        cnt = C.c_int(0)
+        L.check(self.lib.msc_profile_read(self.ctx, buf, 32, C.byref(cnt)))
+        return {buf[i].name.decode(): (buf[i].launches, buf[i].total_ms) for i in range(min(cnt.value, 32))}
+
+    # ---------------------------------------------------------- topology
+    def make_level(self, coords: torch.Tensor) -> torch.Tensor:
+        n = coords.shape[0]
+        nbr = torch.empty((n, 27), dtype=torch.int32, device=coords.device)
+        wsb = self.lib.msc_topology_workspace_bytes(n)
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_make_level(self.ctx, _p(coords), n, _p(nbr), _p(ws), wsb, _stream()))
+        return nbr
+
+    def downsample(self, coords: torch.Tensor) -> Transition:
+        n = coords.shape[0]
+        dev = coords.device
+        parent = torch.empty((max(n, 1), 4), dtype=torch.int32, device=dev)
+        np_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        pool = torch.empty(8 * max(n, 1), dtype=torch.int32, device=dev)
+        inv = torch.empty(max(n, 1), dtype=torch.float32, device=dev)
+        up = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        wsb = self.lib.msc_topology_workspace_bytes(n)
+        ws = self.workspace(wsb)
+        np_host = C.c_int64(0)
+        L.check(self.lib.msc_downsample(self.ctx, _p(coords), n, _p(parent), _p(np_dev), _p(pool), _p(inv), _p(up),
+                                        C.byref(np_host), _p(ws), wsb, _stream()))
+        m = np_host.value
+        return Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n)
+
+    # ---------------------------------------------------------- weights
+    def prepare_weight(self, w: torch.Tensor, wtype: str, cin: int, cout: int, ntaps: int) -> PreparedWeight:
+        """w: packed [cout, ntaps*cin] float32 / float16, or uint8 block_q8_0 rows."""
+        code = _WT[wtype]
+        nb = self.lib.msc_weight_blob_bytes(code, cin, cout, ntaps)
+        blob = torch.empty(nb, dtype=torch.uint8, device=w.device)
+        L.check(self.lib.msc_weight_prepare(self.ctx, code, _p(w), cin, cout, ntaps, _p(blob), nb, _stream()))
+        return PreparedWeight(blob, wtype, cin, cout, ntaps)
+
+    # ---------------------------------------------------------- operators
+    def sparse_conv(self, x, nbr, w: PreparedWeight, bias=None, out_dtype=torch.float32):
+        n, cin = x.shape
+        y = torch.empty((n, w.cout), dtype=out_dtype, device=x.device)
+        wsb = self.lib.msc_op_workspace_bytes(n, max(cin, w.cout))
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_sparse_conv(self.ctx, _p(x), _DT[x.dtype], n, cin, _p(nbr), _p(w.blob), _p(bias), _p(y),
+                                         _DT[out_dtype], _p(ws), wsb, _stream()))
+        return y
+
+    def linear(self, x, w: PreparedWeight, bias=None, out_dtype=torch.float32):
+        n, cin = x.shape
+        y = torch.empty((n, w.cout), dtype=out_dtype, device=x.device)
+        wsb = self.lib.msc_op_workspace_bytes(n, max(cin, w.cout))
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_linear(self.ctx, _p(x), _DT[x.dtype], n, cin, _p(w.blob), _p(bias), _p(y),
+                                    _DT[out_dtype], _p(ws), wsb, _stream()))
+        return y
+
+    def res_block(self, x, nbr, blk: dict):
+        """In place on x.  blk: norm_w, norm_b, w1 (PreparedWeight), b1, w2, b2."""
+        n, c = x.shape
+        wsb = self.lib.msc_op_workspace_bytes(n, c)
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_res_block(self.ctx, _p(x), _DT[x.dtype], n, c, _p(nbr), _p(blk.get("norm_w")),
+                                       _p(blk.get("norm_b")), _p(blk["w1"].blob), _p(blk.get("b1")),
+                                       _p(blk["w2"].blob), _p(blk.get("b2")), _p(ws), wsb, _stream()))
+        return x
+
+    def pool_down(self, x, tr: Transition, w: PreparedWeight, bias=None, out_dtype=torch.float32):
+        nfine, c = x.shape
+        y = torch.empty((tr.np, w.cout), dtype=out_dtype, device=x.device)
+        wsb = self.lib.msc_op_workspace_bytes(max(tr.np, 1), max(c, w.cout))
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_pool_down(self.ctx, _p(x), _DT[x.dtype], nfine, c, _p(tr.pool_rows), _p(tr.inv_count),
+                                       tr.np, _p(w.blob), _p(bias), _p(y), _DT[out_dtype], _p(ws), wsb, _stream()))
+        return y
+
+    def nearest_up(self, x, tr: Transition, w: PreparedWeight, bias=None, skip=None, out_dtype=torch.float32):
+        np_, c = x.shape
+        y = torch.empty((tr.nfine, w.cout), dtype=out_dtype, device=x.device)
+        wsb = self.lib.msc_op_workspace_bytes(max(np_, 1), max(c, w.cout))
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_nearest_up(self.ctx, _p(x), _DT[x.dtype], np_, c, _p(tr.up_rows), tr.nfine,
+                                        _p(w.blob), _p(bias), _p(skip),
+                                        _DT[skip.dtype] if skip is not None else 0, _p(y), _DT[out_dtype], _p(ws),
+                                        wsb, _stream()))
+        return y

@@ -1,0 +1,121 @@
+"""Residual block, pooling and upsampling against the reference goldens and the
+oracle."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import max_abs, rel_l2
+from gpu_util import TOL_FP16, TOL_FP32, dev, host, weight_tensor
+from mogecpp_b200 import synth
+from oracle.oracle import W_F32, W_Q8_0
+
+pytestmark = pytest.mark.gpu
+WT = {"f32": W_F32, "q8_0": W_Q8_0}
+
+
+def make_block(ex, oracle, raw, tag, c):
+    return dict(norm_w=dev(raw["norm_w"]), norm_b=dev(raw["norm_b"]), b1=dev(raw["b1"]), b2=dev(raw["b2"]),
+                w1=ex.prepare_weight(weight_tensor(oracle, raw["w1"], tag), tag, c, c, 27),
+                w2=ex.prepare_weight(weight_tensor(oracle, raw["w2"], tag), tag, c, c, 27))
+
+
+def raw_block(seed, c):
+    rng = np.random.default_rng(seed)
+    return dict(norm_w=(1 + 0.1 * rng.standard_normal(c)).astype(np.float32),
+                norm_b=(0.1 * rng.standard_normal(c)).astype(np.float32),
+                w1=synth.conv_weight(seed + 1, c, c), b1=(0.05 * rng.standard_normal(c)).astype(np.float32),
+                w2=synth.conv_weight(seed + 2, c, c), b2=(0.05 * rng.standard_normal(c)).astype(np.float32))
+
+
+@pytest.mark.parametrize("tag", ["f32", "q8_0"])
+def test_res_block_matches_reference_golden(ex, oracle, golden_features, tag):
+    f = golden_features
+    raw = {k: f[f"res_{tag}_{k}"].astype(np.float32) for k in ("norm_w", "norm_b", "w1", "b1", "w2", "b2")}
+    x = dev(f["x"].astype(np.float32))
+    ex.res_block(x, dev(f["nbr"]), make_block(ex, oracle, raw, tag, 64))
+    ex.check()
+    y = host(x)
+    if tag == "f32":
+        assert rel_l2(y, f["res_f32_y"]) < TOL_FP32
+    else:
+        assert rel_l2(y, f["res_q8_0_y"]) < TOL_FP16[0]
+        assert max_abs(y, f["res_q8_0_y"]) < TOL_FP16[1]
+
+
+@pytest.mark.parametrize("tag", ["f32", "q8_0"])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16])
+def test_res_block_c128_matches_oracle(ex, oracle, tag, dt):
+    coords = synth.small_coords(80, extent=24, grid=32)
+    nbr = oracle.make_level(coords)
+    x = dev(synth.features(81, coords.shape[0], 128)).to(dt)
+    xin = host(x)
+    raw = raw_block(82, 128)
+    ref = oracle.res_block(xin, nbr, raw, WT[tag])
+    ex.res_block(x, dev(nbr), make_block(ex, oracle, raw, tag, 128))
+    ex.check()
+    y = host(x)
+    if tag == "f32" and dt == torch.float32:
+        assert rel_l2(y, ref) < TOL_FP32
+    else:
+        assert rel_l2(y, ref) < TOL_FP16[0] and max_abs(y, ref) < TOL_FP16[1]
+
+
+def test_four_block_q8_stack_fp16_state(ex, oracle):
+    """The res4_c128 workload's arithmetic on a small surface: four blocks,
+    fp16 state between blocks (the oracle rounds its state the same way)."""
+    coords = synth.small_coords(90, extent=28, grid=32)
+    nbr = oracle.make_level(coords)
+    x = dev(synth.features(91, coords.shape[0], 128)).to(torch.float16)
+    ref = host(x)
+    nbrd = dev(nbr)
+    for b in range(4):
+        raw = raw_block(100 + 10 * b, 128)
+        ex.res_block(x, nbrd, make_block(ex, oracle, raw, "q8_0", 128))
+        ref = oracle.res_block(ref, nbr, raw, W_Q8_0).astype(np.float16).astype(np.float32)
+        ex.check()
+        y = host(x)
+        assert rel_l2(y, ref) < TOL_FP16[0], (b, rel_l2(y, ref))
+        assert max_abs(y, ref) < TOL_FP16[1]
+
+
+def test_pool_and_up_match_reference_golden(ex, oracle, golden_features):
+    f = golden_features
+    tr = ex.downsample(dev(f["coords"]))
+    np.testing.assert_array_equal(host(tr.pool_rows), f["pool_rows"])
+    wp = ex.prepare_weight(weight_tensor(oracle, f["pool_w"].astype(np.float32), "f32"), "f32", 64, 128, 1)
+    yp = ex.pool_down(dev(f["x"].astype(np.float32)), tr, wp, dev(f["pool_b"].astype(np.float32)))
+    ex.check()
+    assert rel_l2(host(yp), f["pool_y"]) < TOL_FP32
+    wu = ex.prepare_weight(weight_tensor(oracle, f["up_w"].astype(np.float32), "f32"), "f32", 128, 64, 1)
+    yu = ex.nearest_up(dev(f["up_x"].astype(np.float32)), tr, wu, dev(f["up_b"].astype(np.float32)))
+    ex.check()
+    assert rel_l2(host(yu), f["up_y"]) < TOL_FP32
+
+
+def test_unet_level_bf16_matches_oracle(ex, oracle):
+    """The unet_c64 workload's level on a small batch-2 set: conv 64 -> pool +
+    linear 64->128 -> conv 128 -> linear 128->64 + nearest up + skip."""
+    coords = np.concatenate([synth.small_coords(120, extent=16, grid=32, b=0),
+                             synth.small_coords(121, extent=16, grid=32, b=1)])
+    cd = dev(coords)
+    nbr = ex.make_level(cd)
+    tr = ex.downsample(cd)
+    pc = host(tr.parent)
+    nbr_c = ex.make_level(tr.parent.contiguous())
+    x = dev(synth.features(122, coords.shape[0], 64)).to(torch.bfloat16)
+    lin = lambda seed, co, ci: (np.random.default_rng(seed).standard_normal((co, ci)) / np.sqrt(ci)).astype(np.float32)
+    w0, wl, w1, wu = synth.conv_weight(123, 64, 64), lin(124, 128, 64), synth.conv_weight(125, 128, 128), lin(126, 64, 128)
+    P = lambda w, ci, co, t: ex.prepare_weight(weight_tensor(oracle, w, "f32"), "f32", ci, co, t)
+    h0 = ex.sparse_conv(x, nbr, P(w0, 64, 64, 27), None, out_dtype=torch.bfloat16)
+    h1 = ex.pool_down(h0, tr, P(wl, 64, 128, 1), None, out_dtype=torch.bfloat16)
+    h2 = ex.sparse_conv(h1, nbr_c, P(w1, 128, 128, 27), None, out_dtype=torch.bfloat16)
+    y = ex.nearest_up(h2, tr, P(wu, 128, 64, 1), None, skip=h0, out_dtype=torch.float32)
+    ex.check()
+    # oracle on the same bf16-rounded intermediates
+    r0 = oracle.sparse_conv(host(x), host(nbr), w0, W_F32)
+    r1 = oracle.pool_down(host(h0), host(tr.pool_rows), host(tr.inv_count), wl, W_F32)
+    r2 = oracle.sparse_conv(host(h1), oracle.make_level(pc), w1, W_F32)
+    ry = oracle.nearest_up(host(h2), host(tr.up_rows), wu, W_F32) + host(h0)
+    for got, ref in ((h0, r0), (h1, r1), (h2, r2)):
+        assert rel_l2(host(got), ref) < 8e-3  # bf16 output rounding
+    assert rel_l2(host(y), ry) < TOL_FP16[0] and max_abs(host(y), ry) < TOL_FP16[1]

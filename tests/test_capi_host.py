@@ -1,0 +1,61 @@
+"""C-ABI library: loads without a GPU, exports every declared symbol, and its
+host-side logic (size queries, argument checks) behaves."""
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "moge_sparse_cuda.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(msc_[a-z_0-9]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from mogecpp_b200 import lib as L
+    lib = L.load()
+    syms = declared_symbols()
+    assert len(syms) >= 15
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    assert set(syms) == set(L.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_abi_version():
+    from mogecpp_b200 import lib as L
+    assert L.load().msc_abi_version() == 1
+
+
+def test_size_queries_are_host_only():
+    from mogecpp_b200 import lib as L
+    lib = L.load()
+    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == 256 + 2 * 27 * 128 * 128 * 2
+    assert lib.msc_weight_blob_bytes(L.MSC_W_F16, 64, 64, 27) == 256 + 27 * 64 * 64 * 2
+    assert lib.msc_weight_blob_bytes(99, 64, 64, 27) == 0
+    assert lib.msc_topology_workspace_bytes(1000) > 2048 * 16
+    assert lib.msc_op_workspace_bytes(1000, 128) >= 1000 * 128 * 8
+
+
+def test_create_fails_cleanly_without_sm100():
+    import ctypes as C
+    import torch
+    from mogecpp_b200 import lib as L
+    if torch.cuda.is_available() and torch.cuda.get_device_capability(0) == (10, 0):
+        pytest.skip("an sm_100 device is present")
+    lib = L.load()
+    h = C.c_void_p()
+    rc = lib.msc_create(0, C.byref(h))
+    assert rc != 0
+    assert lib.msc_last_error().decode()
+
+
+def test_null_context_is_rejected():
+    from mogecpp_b200 import lib as L
+    lib = L.load()
+    rc = lib.msc_make_level(None, None, 0, None, None, 0, None)
+    assert rc == -1
+    assert "context" in lib.msc_last_error().decode()
