@@ -153,13 +153,19 @@ void need_ws(size_t have, size_t want) {
         fail(MSC_E_WORKSPACE, "workspace too small: " + std::to_string(have) + " < " + std::to_string(want));
 }
 
-void run_conv(msc_ctx_t ctx, const void* planes, int na, int64_t n, int cin, const int32_t* nbr,
+void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
               const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
               int res_dtype, void* y, int y_dtype, cudaStream_t st) {
     msc::ConvArgs a{};
     a.planes = planes;
-    a.na = na;
+    a.q8 = mode == msc::ACT_Q8;
+    a.a_scale = a.q8 ? reinterpret_cast<const float*>(static_cast<const char*>(planes) + msc::act_scale_offset(n, cin))
+                     : nullptr;
+    a.na = msc::act_planes(mode);
+    a.n_in = n;
     a.n = n;
+    a.row_begin = 0;
+    a.perm = nullptr;
     a.cin = cin;
     a.nbr = nbr;
     a.blob = blob;
@@ -351,11 +357,10 @@ int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int ci
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
         const int mode = act_mode(b.wtype, x_dtype);
-        const int na = msc::act_planes(mode);
-        need_ws(ws_bytes, static_cast<size_t>(na) * n * cin * 2);
+        need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
-        run_conv(ctx, ws, na, n, cin, nbr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
+        run_conv(ctx, ws, mode, n, cin, nbr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
     });
 }
 
@@ -374,11 +379,10 @@ int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, co
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
         const int mode = act_mode(b.wtype, x_dtype);
-        const int na = msc::act_planes(mode);
-        need_ws(ws_bytes, static_cast<size_t>(na) * n * cin * 2);
+        need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
-        run_conv(ctx, ws, na, n, cin, nullptr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
+        run_conv(ctx, ws, mode, n, cin, nullptr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
     });
 }
 
@@ -405,11 +409,11 @@ int msc_res_block(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const i
         const int m1 = act_mode(w1.wtype, x_dtype);
         cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
                 "norm1 prepare");
-        run_conv(ctx, planes, msc::act_planes(m1), n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream));
+        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream));
         const int m2 = act_mode(w2.wtype, MSC_F32);
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
-        run_conv(ctx, planes, msc::act_planes(m2), n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream));
+        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream));
     });
 }
 
@@ -429,7 +433,7 @@ int msc_pool_down(msc_ctx_t ctx, const void* x, int x_dtype, int64_t nfine, int 
         need_aligned(ws, 256, "workspace");
         const size_t pooled_bytes = align256(static_cast<size_t>(np) * c * 4);
         const int mode = act_mode(b.wtype, MSC_F32);
-        need_ws(ws_bytes, pooled_bytes + static_cast<size_t>(msc::act_planes(mode)) * np * c * 2);
+        need_ws(ws_bytes, pooled_bytes + msc::act_bytes(mode, np, c));
         float* pooled = static_cast<float*>(ws);
         void* planes = static_cast<char*>(ws) + pooled_bytes;
         ProfScope pm(ctx, "pool_mean", S(stream));
@@ -437,7 +441,7 @@ int msc_pool_down(msc_ctx_t ctx, const void* x, int x_dtype, int64_t nfine, int 
                 "pool mean");
         cuda_ok(act_prepare(ctx, pooled, MSC_F32, np, c, 0, nullptr, nullptr, 0.f, 0, mode, planes, S(stream)),
                 "pool prepare");
-        run_conv(ctx, planes, msc::act_planes(mode), np, c, nullptr, b, blob, bias, 0, nullptr, 0, y, y_dtype,
+        run_conv(ctx, planes, mode, np, c, nullptr, b, blob, bias, 0, nullptr, 0, y, y_dtype,
                  S(stream));
     });
 }
@@ -459,13 +463,13 @@ int msc_nearest_up(msc_ctx_t ctx, const void* x, int x_dtype, int64_t np, int c,
         need_aligned(x, 16, "x");
         need_aligned(ws, 256, "workspace");
         const int mode = act_mode(b.wtype, x_dtype);
-        const size_t planes_bytes = align256(static_cast<size_t>(msc::act_planes(mode)) * np * c * 2);
+        const size_t planes_bytes = align256(msc::act_bytes(mode, np, c));
         need_ws(ws_bytes, planes_bytes + static_cast<size_t>(np) * b.cout * 4);
         void* planes = ws;
         float* t = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
         cuda_ok(act_prepare(ctx, x, x_dtype, np, c, 0, nullptr, nullptr, 0.f, 0, mode, planes, S(stream)),
                 "up prepare");
-        run_conv(ctx, planes, msc::act_planes(mode), np, c, nullptr, b, blob, bias, 0, nullptr, 0, t, MSC_F32,
+        run_conv(ctx, planes, mode, np, c, nullptr, b, blob, bias, 0, nullptr, 0, t, MSC_F32,
                  S(stream));
         ProfScope pg(ctx, "gather_rows", S(stream));
         cuda_ok(msc::launch_gather_rows(t, np, b.cout, up_rows, nfine, skip, skip_dtype, y, y_dtype, ctx->status,

@@ -13,7 +13,8 @@ enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2 };
 // weight type codes (ggml order)
 enum WType : int { WT_F32 = 0, WT_F16 = 1, WT_Q8_0 = 8 };
 // activation preparation modes: fp16 rounding (1 plane), exact hi/lo split
-// of the fp32 value (2 planes), Q8_0 quantise then exact split (2 planes).
+// of the fp32 value (2 planes), Q8_0 quantisation (1 plane of int8 codes as
+// fp16 + one fp32 scale per 32 channels).
 enum ActMode : int { ACT_FP16 = 0, ACT_SPLIT = 1, ACT_Q8 = 2 };
 
 // Prepared-weight blob header (first 256 bytes of the blob).
@@ -31,31 +32,43 @@ struct WeightHeader {
 static_assert(sizeof(WeightHeader) == 256, "header is 256 bytes");
 constexpr uint32_t kWeightMagic = 0x4d534357u;  // "WCSM"
 
+// Planes of the prepared weight: Q8_0 -> 1 (codes; per-block scales stored
+// after the planes as fp32 [ntaps][cin/32][cout]); f16 -> 1; f32 -> 2 (hi/lo).
 int weight_planes(int wtype);
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps);
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob, cudaStream_t st);
 
 int act_planes(int mode);
-// x: [n][c] (dtype); planes: [act_planes][n][c] fp16.  Optional LayerNorm
-// (gamma/beta may be null only if ln == 0) and SiLU before preparation.
+// Bytes of the prepared activation operand for n rows of c channels.
+size_t act_bytes(int mode, int64_t n, int c);
+// Q8 mode: the per-block scales follow the code plane at this byte offset.
+size_t act_scale_offset(int64_t n, int c);
+// x: [n][c] (dtype) -> prepared operand (planes [act_planes][n][c] fp16, plus
+// scales in Q8 mode).  Optional LayerNorm (affine gamma/beta, either may be
+// null) and SiLU before preparation.
 cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int ln, const float* gamma,
                                const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st);
 
 struct ConvArgs {
-    const void* planes;      // [na][n][cin] fp16
+    const void* planes;      // [na][n_in][cin] fp16 operand planes (Q8: the int8 codes as fp16)
+    const float* a_scale;    // Q8: [n_in][cin/32] per-block activation scales, else null
     int na;                  // 1 or 2
-    int64_t n;               // rows (voxels) of input and output
+    int q8;                  // ggml Q8_0 x Q8_0 block arithmetic
+    int64_t n_in;            // rows of the input planes (neighbour indices >= n_in are missing)
+    int64_t n;               // output rows processed
+    int64_t row_begin;       // output row k is row_begin + k (when perm is null)
+    const int32_t* perm;     // [n] output rows to process, or null
     int cin;
-    const int32_t* nbr;      // [n][27]; null => linear (row i reads row i)
+    const int32_t* nbr;      // [rows][27] indexed by output row; null => linear (row i reads row i)
     const void* blob;        // prepared weights
     int wplanes;             // planes in blob (1 or 2)
     int cout;
     int ntaps;               // 27 or 1
     const float* bias;       // [cout] or null
     int silu_out;
-    const void* residual;    // [n][cout] or null
+    const void* residual;    // [rows][cout] or null
     int res_dtype;
-    void* y;                 // [n][cout]
+    void* y;                 // [rows][cout]
     int y_dtype;
     uint32_t* status;
 };

@@ -1,172 +1,206 @@
 // Submanifold sparse 3-D convolution (and its 1-tap special case, the
-// per-voxel linear layer) as an implicit gather-GEMM on the sm_100a tensor
-// cores.
+// per-voxel linear layer) as a persistent implicit gather-GEMM on the sm_100a
+// tensor cores.
 //
 // Reference semantics (mogecpp src/sparse.cpp:579-627 sparse_conv):
 //   y[i, :] = sum_t W_t x[nbr[i][t], :] + bias,  nbr sentinel = zero row,
 // with W packed [cout][27*cin] (cin fastest, taps in neighbour-map order).
 //
-// Tile: 128 output voxels (M) x cout (N) accumulated in TMEM (fp32), K loops
-// over (tap, 64-channel chunk) stages; taps with no valid neighbour in the
-// tile are skipped.  Operands are fp16 "planes": A = gathered activation
-// rows (1 plane, or an exact hi/lo pair), B = prepared weights (1 plane or
-// hi/lo pair).  For two-plane operands the MMA sums hi*hi + hi*lo + lo*hi,
-// which reproduces fp32 products of <=22-bit operands to ~2^-22 (used for
-// fp32 weights and for ggml's Q8_0 x Q8_0 block dot products).
+// Tiles of 128 output voxels (M) x cout (N).  K runs over the taps present
+// in the tile (taps with no valid neighbour in any of its rows are skipped)
+// and 64-channel chunks.  Operands are fp16 "planes" in shared memory
+// (128-byte swizzled, K-major):
+//   * Q8 mode (ggml Q8_0 x Q8_0, the path of Q8_0 weights): A = the
+//     activation's int8 codes qa, B = the weight codes qw, both exact small
+//     integers in fp16.  One MMA group per 32-channel block yields the exact
+//     integer block dot product (|sum| < 2^19, so the fp32 accumulator is
+//     exact); drain warps then apply ggml's per-block scale,
+//         acc += (d_a * d_w) * isum      (one fp32 FMA, ggml-cpu x86 quants.c:1308)
+//   * other modes: A and B are one fp16 plane or an exact hi/lo pair
+//     (hi*hi + hi*lo + lo*hi); one MMA group per 64-channel chunk, drained
+//     with an fp32 add.
+// Draining every group keeps each tensor-core accumulation chain to a few
+// MMAs: the tcgen05 fp32 accumulator does not round to nearest, and long
+// chains drift by ~1e-6 relative, which ggml's activation re-quantisation
+// would amplify.
 //
-// Warp roles (160 threads):
-//   warps 0-3  producers: each thread gathers one A row per stage with
-//              16-byte cp.async (sentinel rows zero-filled), thread 0 also
-//              issues the bulk copy of the stage's pre-swizzled B tile;
-//              after the main loop the same warps run the epilogue (TMEM
-//              lane 32w+l = voxel row).
-//   warp 4     TMEM allocation and the single-thread MMA issue loop.
-// smem stages: [A planes][B planes], 128B-swizzled K-major; mbarriers full
-// (128 producer arrivals + 1 tx arrival) and empty (tcgen05.commit).
+// Persistent CTA, one per SM, 21 warps:
+//   warps 0-3   producers: per tile, stage the rows' neighbour lists and the
+//               tap mask; per stage, gather one A row per thread with 16-byte
+//               cp.async (sentinel rows zero-filled); thread 0 bulk-copies
+//               the stage's pre-swizzled B tile.
+//   warp 4      TMEM allocation and the single-thread MMA issue loop.
+//   warps 5-20  drain + epilogue: TMEM lane quarter (warp % 4) x column quarter;
+//               fp32 accumulators in registers, bias / SiLU / residual / store.
+// Pipelines (mbarriers): smem stages full/empty, TMEM accumulator slots
+// acc_full/acc_empty (NACC rotating slots), per-tile tile_ready/tile_free
+// (double-buffered neighbour lists).  Every wait is bounded; a wait that runs
+// out sets MSC_DEV_TIMEOUT and the CTA unwinds.
 #include "common.cuh"
 #include "conv.h"
-
-#include <algorithm>
 
 namespace msc {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 64;                  // fp16 elements per stage row (128 B)
-constexpr int kProducerThreads = 128;
-constexpr int kThreads = kProducerThreads + 32;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int BK = 64;  // fp16 elements per stage row (128 B)
+constexpr int kProducerWarps = 4;
+constexpr int kDrainWarps = 16;
+constexpr int kThreads = 32 * (kProducerWarps + 1 + kDrainWarps);
+constexpr int kProducers = 32 * kProducerWarps;
+constexpr int kDrainers = 32 * kDrainWarps;
+constexpr int kSmemLimit = 227 * 1024;  // max dynamic shared memory per block on sm_100
 
-template <int CIN, int COUT, int NA, int NB>
+template <int CIN, int COUT, int NA, int NB, bool Q8>
 struct Cfg {
     static constexpr int KCH = CIN / BK;
+    static constexpr int NBLK = CIN / 32;
     static constexpr int A_PLANE = BM * BK * 2;
     static constexpr int B_PLANE = COUT * BK * 2;
     static constexpr int STAGE = NA * A_PLANE + NB * B_PLANE;
-    static constexpr int STAGES_FIT = kSmemBudget / STAGE;
-    static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
-    static constexpr int NBR_BYTES = BM * 27 * 4;
-    static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE + NBR_BYTES + 256;
-    static constexpr int TMEM_COLS = COUT < 32 ? 32 : COUT;
+    static constexpr int GPS = Q8 ? 2 : 1;          // accumulator groups per stage
+    static constexpr int KSPG = (BK / 16) / GPS;    // MMA k-steps per group
+    static constexpr int NACC = (512 / COUT) < 4 ? (512 / COUT) : 4;
+    static constexpr int TMEM_COLS = NACC * COUT;
+    static constexpr int COLS = COUT / (kDrainWarps / 4);  // columns per drain thread
+    static constexpr int NBR_BYTES = 2 * BM * 27 * 4;
+    static constexpr int SCALE_BYTES = Q8 ? 27 * NBLK * COUT * 4 : 0;
+    static constexpr int ROWS_BYTES = 2 * BM * 4;
+    static constexpr int BAR_BYTES = 512;
+    static constexpr int FIXED = NBR_BYTES + SCALE_BYTES + ROWS_BYTES + BAR_BYTES;
+    static constexpr int STAGES_FIT = (kSmemLimit - 1024 - FIXED) / STAGE;
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    static constexpr int SMEM = 1024 + STAGES * STAGE + FIXED;
     static_assert(STAGES >= 2, "at least two pipeline stages");
     static_assert(CIN % BK == 0, "cin must be a multiple of 64");
-    static_assert(COUT % 16 == 0 && COUT >= 16 && COUT <= 256, "UMMA N range for M=128");
-    static_assert((COUT & (COUT - 1)) == 0, "TMEM allocation is a power of two");
+    static_assert(COUT % 64 == 0 && COUT <= 256, "cout must be 64..256 in steps of 64");
+    static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
+    static_assert(!Q8 || (NA == 1 && NB == 1), "Q8 mode uses integer code planes");
+    static_assert(SMEM <= kSmemLimit, "shared memory budget");
 };
 
-__device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t idx) {
-    if (dtype == DT_F32) return static_cast<const float*>(p)[idx];
-    if (dtype == DT_F16) return __half2float(static_cast<const __half*>(p)[idx]);
-    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
+struct Smem {
+    uint8_t* stages;
+    int* nbr;        // [2][BM*27]
+    float* scaleB;   // [27][NBLK][COUT] (Q8)
+    int* rows;       // [2][BM]
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* acc_full;
+    uint64_t* acc_empty;
+    uint64_t* tile_ready;  // [2]
+    uint64_t* tile_free;   // [2]
+    uint32_t* wmask;       // [2][kProducerWarps]
+    uint32_t* tmem;
+    int* abort;
+};
+
+// Bounded wait that also gives up once another role has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* abort_flag, uint32_t* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 31u) == 31u) {
+            if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+            if (global_timer_ns() - t0 > kWaitBudgetNs) {
+                atomicExch(abort_flag, 1);
+                set_status(status, MSC_DEV_TIMEOUT);
+                return false;
+            }
+        }
+    }
 }
 
-template <int CIN, int COUT, int NA, int NB>
-__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(ConvArgs a) {
-    using C = Cfg<CIN, COUT, NA, NB>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stage_base = smem;
-    int* s_nbr = reinterpret_cast<int*>(smem + C::STAGES * C::STAGE);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE + C::NBR_BYTES);
-    uint64_t* empty = full + C::STAGES;
-    uint64_t* done = empty + C::STAGES;
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
-    uint32_t* s_mask = s_tmem + 1;
-    int* s_abort = reinterpret_cast<int*>(s_mask + 1);
+__device__ __forceinline__ uint32_t tile_mask(const Smem& S, int buf) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int w = 0; w < kProducerWarps; ++w) m |= S.wmask[buf * kProducerWarps + w];
+    return m;
+}
 
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * BM;
-    const int64_t n = a.n;
-    const int ntaps = a.ntaps;
+__device__ __forceinline__ int64_t tile_row(const ConvArgs& a, int64_t idx) {
+    if (idx >= a.n) return -1;
+    return a.perm ? static_cast<int64_t>(__ldg(a.perm + idx)) : a.row_begin + idx;
+}
 
-    if (tid == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], kProducerThreads + 1);
-            mbar_init(&empty[s], 1);
+// ------------------------------------------------------------------ roles
+
+template <int CIN, int COUT, int NA, int NB, bool Q8>
+__device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
+    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+    const int r = threadIdx.x;  // 0..127: tile row
+    const int warp = r >> 5;
+    const __half* planes = static_cast<const __half*>(a.planes);
+    const uint8_t* wdata = static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader);
+    const int64_t plane_stride = a.n_in * CIN;
+    constexpr int LAG = C::STAGES - 1;
+    int64_t i = 0;        // stages issued
+    int64_t arrived = 0;  // stages whose full barrier this thread has arrived on
+    bool ok = true;
+    int k = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++k) {
+        const int buf = k & 1;
+        if (k >= 2) {
+            // publish every issued stage before blocking on the drainers, who may
+            // still need those stages of an earlier tile
+            cp_async_wait_all();
+            fence_proxy_async();
+            for (; arrived < i; ++arrived) mbar_arrive(&S.full[arrived % C::STAGES]);
+            if (!wait_or_abort(&S.tile_free[buf], ((k >> 1) - 1) & 1, S.abort, a.status)) {
+                ok = false;
+                break;
+            }
         }
-        mbar_init(done, 1);
-        *s_mask = 0;
-        *s_abort = 0;
-        fence_mbar_init();
-    }
-    if (warp == 4) {
-        tmem_alloc(s_tmem, C::TMEM_COLS);
-        tmem_relinquish();
-    }
-    // stage the tile's neighbour rows and build the tap-occupancy mask
-    if (a.nbr) {
-        const int rows = static_cast<int>(n - row0 < BM ? n - row0 : BM);
-        const int* src = a.nbr + row0 * 27;
-        for (int k = tid; k < rows * 27; k += kThreads) s_nbr[k] = __ldg(src + k);
-    }
-    __syncthreads();
-    if (tid < kProducerThreads) {
+        // neighbour list and tap mask of this row
+        const int64_t row = tile_row(a, tile * BM + r);
+        int* nb = S.nbr + buf * BM * 27 + r * 27;
         uint32_t m = 0;
-        if (row0 + tid < n) {
+        if (row >= 0) {
             if (a.nbr) {
+                const int* src = a.nbr + row * 27;
+#pragma unroll
                 for (int t = 0; t < 27; ++t) {
-                    const int j = s_nbr[tid * 27 + t];
-                    if (static_cast<uint64_t>(j) < static_cast<uint64_t>(n)) m |= 1u << t;
+                    const int j = __ldg(src + t);
+                    nb[t] = j;
+                    if (static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in)) m |= 1u << t;
                 }
             } else {
+                nb[0] = static_cast<int>(row);
                 m = 1u;
             }
         }
-        m |= __shfl_xor_sync(0xffffffffu, m, 1);
-        m |= __shfl_xor_sync(0xffffffffu, m, 2);
-        m |= __shfl_xor_sync(0xffffffffu, m, 4);
-        m |= __shfl_xor_sync(0xffffffffu, m, 8);
-        m |= __shfl_xor_sync(0xffffffffu, m, 16);
-        if ((tid & 31) == 0 && m) atomicOr(s_mask, m);
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *s_tmem;
-    const uint32_t mask = *s_mask;
-    const int nst = __popc(mask) * C::KCH;
-
-    const __half* planes = static_cast<const __half*>(a.planes);
-    const uint8_t* wdata = static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader);
-    const int64_t plane_stride = n * CIN;
-    constexpr int LAG = C::STAGES - 1;
-
-    if (tid < kProducerThreads) {
-        // ---------------------------------------------------------- producer
-        const int r = tid;
-        const bool row_ok = row0 + r < n;
-        uint32_t rem = mask;
+        S.rows[buf * BM + r] = static_cast<int>(row);
+        m = __reduce_or_sync(0xffffffffu, m);
+        if ((r & 31) == 0) S.wmask[buf * kProducerWarps + warp] = m;
+        asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
+        mbar_arrive(&S.tile_ready[buf]);
+        uint32_t rem = tile_mask(S, buf);
+        const int nst = __popc(rem) * C::KCH;
         int tap = -1, kc = C::KCH;
-        bool ok = true;
-        for (int i = 0; i < nst; ++i) {
+        for (int st = 0; st < nst; ++st, ++i) {
             if (kc == C::KCH) {
                 tap = __ffs(rem) - 1;
                 rem &= rem - 1;
                 kc = 0;
             }
-            const int s = i % C::STAGES;
-            if (i >= C::STAGES) {
-                if (!mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) {
-                    ok = false;
-                    break;
-                }
+            const int s = static_cast<int>(i % C::STAGES);
+            if (i >= C::STAGES &&
+                !wait_or_abort(&S.empty[s], static_cast<uint32_t>((i / C::STAGES) - 1) & 1, S.abort, a.status)) {
+                ok = false;
+                break;
             }
-            uint8_t* sA = stage_base + s * C::STAGE;
+            uint8_t* sA = S.stages + s * C::STAGE;
             uint8_t* sB = sA + NA * C::A_PLANE;
             if (r == 0) {
-                mbar_arrive_expect_tx(&full[s], NB * C::B_PLANE);
+                mbar_arrive_expect_tx(&S.full[s], NB * C::B_PLANE);
                 bulk_g2s(smem_u32(sB), wdata + static_cast<int64_t>(tap * C::KCH + kc) * NB * C::B_PLANE,
-                         NB * C::B_PLANE, &full[s]);
+                         NB * C::B_PLANE, &S.full[s]);
             }
             int64_t j = -1;
-            if (row_ok) {
-                if (a.nbr) {
-                    const int jj = s_nbr[r * 27 + tap];
-                    if (static_cast<uint64_t>(jj) < static_cast<uint64_t>(n)) j = jj;
-                } else {
-                    j = row0 + r;
-                }
+            if (row >= 0) {
+                const int jj = nb[tap];
+                if (static_cast<uint64_t>(jj) < static_cast<uint64_t>(a.n_in)) j = jj;
             }
             const uint32_t nbytes = j >= 0 ? 16u : 0u;
 #pragma unroll
@@ -177,160 +211,331 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(ConvArgs a) {
                 for (int c = 0; c < 8; ++c) cp_async16(dst + sw128_offset(r, c), src + (j >= 0 ? c * 8 : 0), nbytes);
             }
             cp_async_commit();
-            if (i >= LAG) {
+            if (i + 1 - arrived > LAG) {
                 cp_async_wait<LAG>();
                 fence_proxy_async();
-                mbar_arrive(&full[(i - LAG) % C::STAGES]);
+                mbar_arrive(&S.full[arrived % C::STAGES]);
+                ++arrived;
             }
             ++kc;
         }
-        cp_async_wait_all();
-        if (ok) {
-            fence_proxy_async();
-            for (int i = max(0, nst - LAG); i < nst; ++i) mbar_arrive(&full[i % C::STAGES]);
-        } else {
-            atomicExch(s_abort, 1);
-            set_status(a.status, MSC_DEV_TIMEOUT);
-        }
-    } else if (warp == 4) {
-        // ---------------------------------------------------------- MMA
-        if ((tid & 31) == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM, COUT, 0);
-            bool ok = true;
-            for (int i = 0; i < nst; ++i) {
-                const int s = i % C::STAGES;
-                if (!mbar_wait(&full[s], (i / C::STAGES) & 1)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t aaddr = smem_u32(stage_base + s * C::STAGE);
-                const uint32_t baddr = aaddr + NA * C::A_PLANE;
+    }
+    cp_async_wait_all();
+    if (ok) {
+        fence_proxy_async();
+        for (; arrived < i; ++arrived) mbar_arrive(&S.full[arrived % C::STAGES]);
+    }
+}
+
+template <int CIN, int COUT, int NA, int NB, bool Q8>
+__device__ void mma_issuer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32_t tmem) {
+    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+    constexpr uint32_t idesc = idesc_f16(BM, COUT, 0);
+    int64_t i = 0, g = 0;
+    int k = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
+        const int buf = k & 1;
+        if (!wait_or_abort(&S.tile_ready[buf], (k >> 1) & 1, S.abort, a.status)) return;
+        const int nst = __popc(tile_mask(S, buf)) * C::KCH;
+        for (int st = 0; st < nst; ++st, ++i) {
+            const int s = static_cast<int>(i % C::STAGES);
+            if (!wait_or_abort(&S.full[s], static_cast<uint32_t>(i / C::STAGES) & 1, S.abort, a.status)) return;
+            tc_fence_after();
+            const uint32_t aaddr = smem_u32(S.stages + s * C::STAGE);
+            const uint32_t baddr = aaddr + NA * C::A_PLANE;
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k) {
-                    const uint64_t ah = sdesc_k_sw128(aaddr + k * 32);
-                    const uint64_t bh = sdesc_k_sw128(baddr + k * 32);
-                    umma_f16(tmem, ah, bh, idesc, (i > 0 || k > 0) ? 1u : 0u);
-                    if (NB == 2) umma_f16(tmem, ah, sdesc_k_sw128(baddr + C::B_PLANE + k * 32), idesc, 1u);
-                    if (NA == 2) umma_f16(tmem, sdesc_k_sw128(aaddr + C::A_PLANE + k * 32), bh, idesc, 1u);
+            for (int gg = 0; gg < C::GPS; ++gg, ++g) {
+                const int slot = static_cast<int>(g % C::NACC);
+                if (g >= C::NACC &&
+                    !wait_or_abort(&S.acc_empty[slot], static_cast<uint32_t>((g / C::NACC) - 1) & 1, S.abort,
+                                   a.status))
+                    return;
+                tc_fence_after();
+                const uint32_t d = tmem + static_cast<uint32_t>(slot * COUT);
+#pragma unroll
+                for (int ks = 0; ks < C::KSPG; ++ks) {
+                    const uint32_t off = static_cast<uint32_t>((gg * C::KSPG + ks) * 32);
+                    const uint64_t ah = sdesc_k_sw128(aaddr + off);
+                    const uint64_t bh = sdesc_k_sw128(baddr + off);
+                    umma_f16(d, ah, bh, idesc, ks > 0 ? 1u : 0u);
+                    if (NB == 2) umma_f16(d, ah, sdesc_k_sw128(baddr + C::B_PLANE + off), idesc, 1u);
+                    if (NA == 2) umma_f16(d, sdesc_k_sw128(aaddr + C::A_PLANE + off), bh, idesc, 1u);
                 }
-                umma_commit(&empty[s]);
+                umma_commit(&S.acc_full[slot]);
             }
-            if (ok) {
-                umma_commit(done);
-            } else {
-                atomicExch(s_abort, 1);
-                set_status(a.status, MSC_DEV_TIMEOUT);
-                mbar_arrive(done);  // release the epilogue
-            }
+            umma_commit(&S.empty[s]);
         }
     }
+}
 
-    // -------------------------------------------------------------- epilogue
-    if (tid < kProducerThreads) {
-        const bool ok = mbar_wait(done, 0);
-        if (!ok) set_status(a.status, MSC_DEV_TIMEOUT);
-        tc_fence_after();
-        __syncwarp();
-        const bool valid = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(s_abort) == 0);
-        const int64_t row = row0 + tid;
-        const auto* hdr = static_cast<const WeightHeader*>(a.blob);
-        const float oscale = hdr->oscale;
-#pragma unroll 1
-        for (int c0 = 0; c0 < COUT; c0 += 32) {
-            uint32_t acc[32];
-            if (nst > 0 && valid) {
-                tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, acc);
-                tmem_wait_ld();
-            } else {
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+__device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t idx) {
+    if (dtype == DT_F32) return static_cast<const float*>(p)[idx];
+    if (dtype == DT_F16) return __half2float(static_cast<const __half*>(p)[idx]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
+}
+
+template <int N>
+__device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const float (&v)[N]) {
+    if (dtype == DT_F32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(y) + off);
 #pragma unroll
-                for (int k = 0; k < 32; ++k) acc[k] = 0u;
+        for (int k = 0; k < N / 4; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    } else if (dtype == DT_F16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(y) + off);
+#pragma unroll
+        for (int k = 0; k < N / 8; ++k) {
+            __half2 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
+            dst[k] = *reinterpret_cast<uint4*>(h);
+        }
+    } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + off);
+#pragma unroll
+        for (int k = 0; k < N / 8; ++k) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
+            dst[k] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+}
+
+template <int CIN, int COUT, int NA, int NB, bool Q8>
+__device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32_t tmem) {
+    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+    constexpr int COLS = C::COLS;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = warp & 3;                       // TMEM lane quarter
+    const int part = (warp - kProducerWarps - 1) >> 2;  // column slice
+    const int m = q * 32 + lane;                         // tile row
+    const int c_base = part * COLS;
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    const float oscale = static_cast<const WeightHeader*>(a.blob)->oscale;
+    int64_t g = 0;
+    int k = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
+        const int buf = k & 1;
+        if (!wait_or_abort(&S.tile_ready[buf], (k >> 1) & 1, S.abort, a.status)) return;
+        uint32_t rem = tile_mask(S, buf);
+        const int row = S.rows[buf * BM + m];
+        const int* nb = S.nbr + buf * BM * 27 + m * 27;
+        uint64_t acc[COLS / 2];
+#pragma unroll
+        for (int e = 0; e < COLS / 2; ++e) acc[e] = 0ull;
+        while (rem) {
+            const int tap = __ffs(rem) - 1;
+            rem &= rem - 1;
+            float sa[C::NBLK];
+            if (Q8) {
+                const int j = row >= 0 ? nb[tap] : -1;
+                const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
+#pragma unroll
+                for (int b = 0; b < C::NBLK; ++b) sa[b] = v ? __ldg(a.a_scale + static_cast<int64_t>(j) * C::NBLK + b) : 0.f;
             }
-            if (row < n && valid) {
-                float v[32];
+#pragma unroll 1
+            for (int grp = 0; grp < C::KCH * C::GPS; ++grp, ++g) {
+                const int slot = static_cast<int>(g % C::NACC);
+                if (!wait_or_abort(&S.acc_full[slot], static_cast<uint32_t>(g / C::NACC) & 1, S.abort, a.status))
+                    return;
+                tc_fence_after();
+                // CH columns at a time: load, wait, accumulate; release the slot
+                // after the last load has landed
+                constexpr int CH = COLS < 32 ? COLS : 32;
 #pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    float t = __uint_as_float(acc[k]) * oscale;
-                    if (a.bias) t += __ldg(a.bias + c0 + k);
-                    if (a.silu_out) t = silu_f(t);
-                    if (a.residual) t += load_elem(a.residual, a.res_dtype, row * COUT + c0 + k);
-                    v[k] = t;
-                }
-                if (a.y_dtype == DT_F32) {
-                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.y) + row * COUT + c0);
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-                } else if (a.y_dtype == DT_F16) {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.y) + row * COUT + c0);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        uint4 u;
-                        __half2 h0 = __floats2half2_rn(v[8 * k], v[8 * k + 1]);
-                        __half2 h1 = __floats2half2_rn(v[8 * k + 2], v[8 * k + 3]);
-                        __half2 h2 = __floats2half2_rn(v[8 * k + 4], v[8 * k + 5]);
-                        __half2 h3 = __floats2half2_rn(v[8 * k + 6], v[8 * k + 7]);
-                        u.x = *reinterpret_cast<uint32_t*>(&h0);
-                        u.y = *reinterpret_cast<uint32_t*>(&h1);
-                        u.z = *reinterpret_cast<uint32_t*>(&h2);
-                        u.w = *reinterpret_cast<uint32_t*>(&h3);
-                        dst[k] = u;
+                for (int c = 0; c < COLS; c += CH) {
+                    uint32_t d[CH];
+                    tmem_ld<CH>(tmem + lane_addr + static_cast<uint32_t>(slot * COUT + c_base + c), d);
+                    tmem_wait_ld();
+                    if (c + CH == COLS) {
+                        tc_fence_before();
+                        mbar_arrive(&S.acc_empty[slot]);
                     }
-                } else {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y) + row * COUT + c0);
+                    if (Q8) {
+                        const float4* sb = reinterpret_cast<const float4*>(S.scaleB + (tap * C::NBLK + grp) * COUT + c_base + c);
+                        float sg = sa[0];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        uint4 u;
-                        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * k], v[8 * k + 1]);
-                        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * k + 2], v[8 * k + 3]);
-                        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * k + 4], v[8 * k + 5]);
-                        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * k + 6], v[8 * k + 7]);
-                        u.x = *reinterpret_cast<uint32_t*>(&h0);
-                        u.y = *reinterpret_cast<uint32_t*>(&h1);
-                        u.z = *reinterpret_cast<uint32_t*>(&h2);
-                        u.w = *reinterpret_cast<uint32_t*>(&h3);
-                        dst[k] = u;
+                        for (int b = 1; b < C::NBLK; ++b) sg = grp == b ? sa[b] : sg;
+                        const uint64_t sa2 = pack2(sg, sg);
+#pragma unroll
+                        for (int e = 0; e < CH / 4; ++e) {
+                            const float4 w = sb[e];
+                            const uint64_t s0 = mul2(sa2, pack2(w.x, w.y));
+                            const uint64_t s1 = mul2(sa2, pack2(w.z, w.w));
+                            acc[c / 2 + 2 * e] = fma2(pack2(__uint_as_float(d[4 * e]), __uint_as_float(d[4 * e + 1])), s0,
+                                                      acc[c / 2 + 2 * e]);
+                            acc[c / 2 + 2 * e + 1] = fma2(pack2(__uint_as_float(d[4 * e + 2]), __uint_as_float(d[4 * e + 3])),
+                                                          s1, acc[c / 2 + 2 * e + 1]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < CH / 2; ++e)
+                            acc[c / 2 + e] = add2(acc[c / 2 + e], pack2(__uint_as_float(d[2 * e]), __uint_as_float(d[2 * e + 1])));
                     }
                 }
             }
         }
+        // epilogue for this tile row / column slice
+        if (row >= 0) {
+            constexpr int EC = COLS < 32 ? COLS : 32;
+#pragma unroll
+            for (int c0 = 0; c0 < COLS; c0 += EC) {
+                float v[EC];
+#pragma unroll
+                for (int e = 0; e < EC / 2; ++e) unpack2(acc[c0 / 2 + e], v[2 * e], v[2 * e + 1]);
+#pragma unroll
+                for (int e = 0; e < EC; ++e) {
+                    const int n = c_base + c0 + e;
+                    float t = v[e] * oscale;
+                    if (a.bias) t += __ldg(a.bias + n);
+                    if (a.silu_out) t = silu_f(t);
+                    if (a.residual) t += load_elem(a.residual, a.res_dtype, static_cast<int64_t>(row) * COUT + n);
+                    v[e] = t;
+                }
+                store_row<EC>(a.y, a.y_dtype, static_cast<int64_t>(row) * COUT + c_base + c0, v);
+            }
+        }
+        mbar_arrive(&S.tile_free[buf]);
+    }
+}
+
+template <int CIN, int COUT, int NA, int NB, bool Q8>
+__global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
+    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem S;
+    S.stages = base;
+    uint8_t* p = base + C::STAGES * C::STAGE;
+    S.nbr = reinterpret_cast<int*>(p);
+    p += C::NBR_BYTES;
+    S.scaleB = reinterpret_cast<float*>(p);
+    p += C::SCALE_BYTES;
+    S.rows = reinterpret_cast<int*>(p);
+    p += C::ROWS_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(p);
+    S.full = bars;
+    S.empty = S.full + C::STAGES;
+    S.acc_full = S.empty + C::STAGES;
+    S.acc_empty = S.acc_full + C::NACC;
+    S.tile_ready = S.acc_empty + C::NACC;
+    S.tile_free = S.tile_ready + 2;
+    S.wmask = reinterpret_cast<uint32_t*>(S.tile_free + 2);
+    S.tmem = S.wmask + 2 * kProducerWarps;
+    S.abort = reinterpret_cast<int*>(S.tmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&S.full[s], kProducers + 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        for (int s = 0; s < C::NACC; ++s) {
+            mbar_init(&S.acc_full[s], 1);
+            mbar_init(&S.acc_empty[s], kDrainers);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&S.tile_ready[b], kProducers);
+            mbar_init(&S.tile_free[b], kDrainers);
+        }
+        *S.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kProducerWarps) {
+        tmem_alloc(S.tmem, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (Q8) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader) +
+                                                            static_cast<size_t>(a.ntaps) * C::KCH * C::B_PLANE);
+        float4* dst = reinterpret_cast<float4*>(S.scaleB);
+        const int nsc = (a.ntaps * C::NBLK * COUT) / 4;
+        for (int e = threadIdx.x; e < nsc; e += kThreads) dst[e] = __ldg(src + e);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    tc_fence_after();
+    const uint32_t tmem = *S.tmem;
+    const int64_t ntiles = (a.n + BM - 1) / BM;
+
+    if (warp < kProducerWarps) {
+        producer<CIN, COUT, NA, NB, Q8>(a, S, ntiles);
+    } else if (warp == kProducerWarps) {
+        if ((threadIdx.x & 31) == 0) mma_issuer<CIN, COUT, NA, NB, Q8>(a, S, ntiles, tmem);
+        __syncwarp();
+    } else {
+        drainer<CIN, COUT, NA, NB, Q8>(a, S, ntiles, tmem);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kProducerWarps) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
-template <int CIN, int COUT, int NA, int NB>
+template <int CIN, int COUT, int NA, int NB, bool Q8>
 cudaError_t launch_t(const ConvArgs& a, cudaStream_t st) {
-    using C = Cfg<CIN, COUT, NA, NB>;
-    auto kern = conv_tc_kernel<CIN, COUT, NA, NB>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+    auto kern = conv_tc_kernel<CIN, COUT, NA, NB, Q8>;
+    static int num_sms[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!num_sms[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
-        configured = true;
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        num_sms[dev] = sms;
     }
-    const unsigned grid = static_cast<unsigned>((a.n + BM - 1) / BM);
+    const int64_t ntiles = (a.n + BM - 1) / BM;
+    const unsigned grid = static_cast<unsigned>(ntiles < num_sms[dev] ? ntiles : num_sms[dev]);
     kern<<<grid, kThreads, C::SMEM, st>>>(a);
     return cudaGetLastError();
 }
 
 template <int CIN, int COUT>
 cudaError_t launch_planes(const ConvArgs& a, cudaStream_t st) {
-    if (a.na == 1 && a.wplanes == 1) return launch_t<CIN, COUT, 1, 1>(a, st);
-    if (a.na == 1 && a.wplanes == 2) return launch_t<CIN, COUT, 1, 2>(a, st);
-    if (a.na == 2 && a.wplanes == 1) return launch_t<CIN, COUT, 2, 1>(a, st);
-    if (a.na == 2 && a.wplanes == 2) return launch_t<CIN, COUT, 2, 2>(a, st);
+    if (a.q8) return launch_t<CIN, COUT, 1, 1, true>(a, st);
+    if (a.na == 1 && a.wplanes == 1) return launch_t<CIN, COUT, 1, 1, false>(a, st);
+    if (a.na == 1 && a.wplanes == 2) return launch_t<CIN, COUT, 1, 2, false>(a, st);
+    if (a.na == 2 && a.wplanes == 1) return launch_t<CIN, COUT, 2, 1, false>(a, st);
+    if (a.na == 2 && a.wplanes == 2) return launch_t<CIN, COUT, 2, 2, false>(a, st);
     return cudaErrorInvalidValue;
 }
 
 }  // namespace
 
-bool conv_supported(int cin, int cout) {
-    return (cin == 64 || cin == 128) && (cout == 64 || cout == 128);
-}
+bool conv_supported(int cin, int cout) { return (cin == 64 || cin == 128) && (cout == 64 || cout == 128); }
 
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t st) {
     if (a.n == 0) return cudaSuccess;

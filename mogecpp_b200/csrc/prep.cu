@@ -2,22 +2,27 @@
 //
 //  * weights: packed [cout][ntaps*cin] (f32, f16 or ggml block_q8_0 rows) ->
 //    blob of 128B-swizzled K-major fp16 tiles [tap][64-ch chunk][plane][cout][64].
-//    f16 weights are one exact plane; f32 and Q8_0 weights (dequantised to
-//    their exact fp32 value d*q) become an exact hi/lo pair after a
-//    power-of-two prescale that puts max|w| near 2^14 (undone in the conv
-//    epilogue).
+//    f16 weights are one exact plane; f32 weights become an exact hi/lo pair
+//    after a power-of-two prescale that puts max|w| near 2^14 (undone in the
+//    conv epilogue); Q8_0 weights become one plane of their int8 codes plus
+//    the fp16 block scales as fp32 [tap][cin/32][cout] after the planes.
 //  * activations: [n][c] rows (f32/f16/bf16), optional LayerNorm + SiLU
 //    (mogecpp src/sparse.cpp:520-526, ggml norm_f32 / silu), then
 //      ACT_FP16  round to fp16                      (ggml F16 vec_dot_type)
 //      ACT_SPLIT exact hi/lo fp16 pair of the fp32  (ggml F32 x F32)
 //      ACT_Q8    ggml's x86 Q8_0 quantiser per 32 channels (d = amax/127,
-//                id = 127/amax, round-half-even; ggml-cpu/arch/x86/quants.c:302)
-//                then the exact hi/lo pair of q * fp16(d)  (Q8_0 vec_dot_type)
+//                id = 127/amax, round-half-even; ggml-cpu/arch/x86/quants.c:302):
+//                the int8 codes as one fp16 plane, fp32(fp16(d)) per block
+//                after it (Q8_0 vec_dot_type)
 #include "common.cuh"
 #include "conv.h"
 
 namespace msc {
 namespace {
+
+__host__ __device__ inline size_t scale_offset(int64_t n, int c) {
+    return (static_cast<size_t>(n) * c * 2 + 255) / 256 * 256;
+}
 
 struct BlockQ8 {
     __half d;
@@ -64,7 +69,7 @@ __global__ void weight_split_kernel(WeightHeader* h, int wtype, const void* w, i
                                     int planes, uint8_t* out) {
     const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
     const int64_t total = row_len * cout;
-    const int s = planes == 2 ? prescale_exp(h->amax) : 0;
+    const int s = (planes == 2 && wtype != WT_Q8_0) ? prescale_exp(h->amax) : 0;
     const int kch = cin / 64;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -73,13 +78,23 @@ __global__ void weight_split_kernel(WeightHeader* h, int wtype, const void* w, i
         const int t = static_cast<int>(k / cin);
         const int ci = static_cast<int>(k % cin);
         const int kc = ci / 64, e = ci % 64;
-        const float v = ldexpf(weight_value(wtype, w, row_len, o, k), s);
         __half hi, lo;
-        if (planes == 2) {
-            split_f16(v, hi, lo);
-        } else {
-            hi = __float2half_rn(v);
+        if (wtype == WT_Q8_0) {
+            const BlockQ8* b = static_cast<const BlockQ8*>(w) + (o * row_len + k) / 32;
+            hi = __int2half_rn(b->qs[k % 32]);
             lo = __float2half_rn(0.0f);
+            if (k % 32 == 0) {
+                float* scales = reinterpret_cast<float*>(out + static_cast<int64_t>(ntaps) * cin * cout * 2);
+                scales[(static_cast<int64_t>(t) * (cin / 32) + ci / 32) * cout + o] = __half2float(b->d);
+            }
+        } else {
+            const float v = ldexpf(weight_value(wtype, w, row_len, o, k), s);
+            if (planes == 2) {
+                split_f16(v, hi, lo);
+            } else {
+                hi = __float2half_rn(v);
+                lo = __float2half_rn(0.0f);
+            }
         }
         const int64_t tile = static_cast<int64_t>(t * kch + kc) * planes;
         const uint32_t off = sw128_offset(o, e >> 3) + (e & 7) * 2;
@@ -148,12 +163,13 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         for (int o = 1; o < 32 / EPL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        const float dq = __half2float(__float2half_rn(d));
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) {
-            const int q = __float2int_rn(__fmul_rn(v[k], id));
-            v[k] = static_cast<float>(q) * dq;
+        for (int k = 0; k < EPL; ++k) planes[base + k] = __int2half_rn(__float2int_rn(__fmul_rn(v[k], id)));
+        if ((lane * EPL) % 32 == 0) {
+            float* scales = reinterpret_cast<float*>(reinterpret_cast<char*>(planes) + scale_offset(n, C));
+            scales[row * (C / 32) + lane * EPL / 32] = __half2float(__float2half_rn(d));
         }
+        return;
     }
 #pragma unroll
     for (int k = 0; k < EPL; ++k) {
@@ -166,10 +182,12 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
 
 }  // namespace
 
-int weight_planes(int wtype) { return wtype == WT_F16 ? 1 : 2; }
+int weight_planes(int wtype) { return wtype == WT_F32 ? 2 : 1; }
 
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
-    return sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype)) * ntaps * cin * cout * 2;
+    size_t b = sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype)) * ntaps * cin * cout * 2;
+    if (wtype == WT_Q8_0) b += static_cast<size_t>(ntaps) * (cin / 32) * cout * 4;
+    return b;
 }
 
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
@@ -178,7 +196,7 @@ cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, i
     const int planes = weight_planes(wtype);
     const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
     weight_header_kernel<<<1, 1, 0, st>>>(h, wtype, cin, cout, ntaps, planes);
-    if (planes == 2) weight_amax_kernel<<<148, 256, 0, st>>>(h, wtype, w, row_len, cout);
+    if (wtype == WT_F32) weight_amax_kernel<<<148, 256, 0, st>>>(h, wtype, w, row_len, cout);
     const int64_t total = row_len * cout;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 16));
     weight_split_kernel<<<grid, 256, 0, st>>>(h, wtype, w, cin, cout, ntaps, planes,
@@ -186,7 +204,14 @@ cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, i
     return cudaGetLastError();
 }
 
-int act_planes(int mode) { return mode == ACT_FP16 ? 1 : 2; }
+int act_planes(int mode) { return mode == ACT_SPLIT ? 2 : 1; }
+
+size_t act_scale_offset(int64_t n, int c) { return scale_offset(n, c); }
+
+size_t act_bytes(int mode, int64_t n, int c) {
+    if (mode == ACT_Q8) return scale_offset(n, c) + static_cast<size_t>(n) * (c / 32) * 4;
+    return static_cast<size_t>(act_planes(mode)) * n * c * 2;
+}
 
 cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int ln, const float* gamma,
                                const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st) {
