@@ -32,8 +32,8 @@ struct WeightHeader {
 static_assert(sizeof(WeightHeader) == 256, "header is 256 bytes");
 constexpr uint32_t kWeightMagic = 0x4d534357u;  // "WCSM"
 
-// Planes of the prepared weight: Q8_0 -> 1 (codes; per-block scales stored
-// after the planes as fp32 [ntaps][cin/32][cout]); f16 -> 1; f32 -> 2 (hi/lo).
+// Planes of the prepared weight: f16 -> 1 (exact); f32 and Q8_0 -> 2 (exact
+// hi/lo pair of the prescaled dequantised value).
 int weight_planes(int wtype);
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps);
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob, cudaStream_t st);

@@ -11,11 +11,12 @@
 // and 64-channel chunks.  Operands are fp16 "planes" in shared memory
 // (128-byte swizzled, K-major):
 //   * Q8 mode (ggml Q8_0 x Q8_0, the path of Q8_0 weights): A = the
-//     activation's int8 codes qa, B = the weight codes qw, both exact small
-//     integers in fp16.  One MMA group per 32-channel block yields the exact
-//     integer block dot product (|sum| < 2^19, so the fp32 accumulator is
-//     exact); drain warps then apply ggml's per-block scale,
-//         acc += (d_a * d_w) * isum      (one fp32 FMA, ggml-cpu x86 quants.c:1308)
+//     activation's int8 codes qa (exact in fp16), B = the exact hi/lo pair of
+//     the prescaled weight d_w * qw.  One MMA group per 32-channel block
+//     gives d_w * isum with exact products and a 4-MMA accumulation chain;
+//     the drain warps apply the activation block scale,
+//         acc += d_a * (d_w * isum)      (ggml-cpu x86 quants.c:1308 sums
+//                                          fp16(d_a)*fp16(d_w)*isum per block)
 //   * other modes: A and B are one fp16 plane or an exact hi/lo pair
 //     (hi*hi + hi*lo + lo*hi); one MMA group per 64-channel chunk, drained
 //     with an fp32 add.
@@ -24,13 +25,13 @@
 // chains drift by ~1e-6 relative, which ggml's activation re-quantisation
 // would amplify.
 //
-// Persistent CTA, one per SM, 21 warps:
-//   warps 0-3   producers: per tile, stage the rows' neighbour lists and the
-//               tap mask; per stage, gather one A row per thread with 16-byte
+// Persistent CTA, one per SM, 19 warps:
+//   warps 0-1   producers: per tile, stage the rows' neighbour lists and the
+//               tap mask; per stage, gather two A rows per thread with 16-byte
 //               cp.async (sentinel rows zero-filled); thread 0 bulk-copies
 //               the stage's pre-swizzled B tile.
-//   warp 4      TMEM allocation and the single-thread MMA issue loop.
-//   warps 5-20  drain + epilogue: TMEM lane quarter (warp % 4) x column quarter;
+//   warp 2      TMEM allocation and the single-thread MMA issue loop.
+//   warps 3-18  drain + epilogue: TMEM lane quarter (warp % 4) x column quarter;
 //               fp32 accumulators in registers, bias / SiLU / residual / store.
 // Pipelines (mbarriers): smem stages full/empty, TMEM accumulator slots
 // acc_full/acc_empty (NACC rotating slots), per-tile tile_ready/tile_free
@@ -44,11 +45,12 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // fp16 elements per stage row (128 B)
-constexpr int kProducerWarps = 4;
+constexpr int kProducerWarps = 2;
 constexpr int kDrainWarps = 16;
 constexpr int kThreads = 32 * (kProducerWarps + 1 + kDrainWarps);
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kDrainers = 32 * kDrainWarps;
+constexpr int kRowsPerProducer = BM / kProducers;
 constexpr int kSmemLimit = 227 * 1024;  // max dynamic shared memory per block on sm_100
 
 template <int CIN, int COUT, int NA, int NB, bool Q8>
@@ -64,10 +66,9 @@ struct Cfg {
     static constexpr int TMEM_COLS = NACC * COUT;
     static constexpr int COLS = COUT / (kDrainWarps / 4);  // columns per drain thread
     static constexpr int NBR_BYTES = 2 * BM * 27 * 4;
-    static constexpr int SCALE_BYTES = Q8 ? 27 * NBLK * COUT * 4 : 0;
     static constexpr int ROWS_BYTES = 2 * BM * 4;
     static constexpr int BAR_BYTES = 512;
-    static constexpr int FIXED = NBR_BYTES + SCALE_BYTES + ROWS_BYTES + BAR_BYTES;
+    static constexpr int FIXED = NBR_BYTES + ROWS_BYTES + BAR_BYTES;
     static constexpr int STAGES_FIT = (kSmemLimit - 1024 - FIXED) / STAGE;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int SMEM = 1024 + STAGES * STAGE + FIXED;
@@ -75,14 +76,13 @@ struct Cfg {
     static_assert(CIN % BK == 0, "cin must be a multiple of 64");
     static_assert(COUT % 64 == 0 && COUT <= 256, "cout must be 64..256 in steps of 64");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
-    static_assert(!Q8 || (NA == 1 && NB == 1), "Q8 mode uses integer code planes");
+    static_assert(!Q8 || (NA == 1 && NB == 2), "Q8 mode: integer code plane x exact weight pair");
     static_assert(SMEM <= kSmemLimit, "shared memory budget");
 };
 
 struct Smem {
     uint8_t* stages;
     int* nbr;        // [2][BM*27]
-    float* scaleB;   // [27][NBLK][COUT] (Q8)
     int* rows;       // [2][BM]
     uint64_t* full;
     uint64_t* empty;
@@ -129,8 +129,8 @@ __device__ __forceinline__ int64_t tile_row(const ConvArgs& a, int64_t idx) {
 template <int CIN, int COUT, int NA, int NB, bool Q8>
 __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
     using C = Cfg<CIN, COUT, NA, NB, Q8>;
-    const int r = threadIdx.x;  // 0..127: tile row
-    const int warp = r >> 5;
+    const int t0 = threadIdx.x;  // 0..kProducers-1; owns tile rows t0 + u*kProducers
+    const int warp = t0 >> 5;
     const __half* planes = static_cast<const __half*>(a.planes);
     const uint8_t* wdata = static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader);
     const int64_t plane_stride = a.n_in * CIN;
@@ -152,27 +152,31 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
                 break;
             }
         }
-        // neighbour list and tap mask of this row
-        const int64_t row = tile_row(a, tile * BM + r);
-        int* nb = S.nbr + buf * BM * 27 + r * 27;
+        // neighbour lists and tap mask of this thread's rows
         uint32_t m = 0;
-        if (row >= 0) {
-            if (a.nbr) {
-                const int* src = a.nbr + row * 27;
 #pragma unroll
-                for (int t = 0; t < 27; ++t) {
-                    const int j = __ldg(src + t);
-                    nb[t] = j;
-                    if (static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in)) m |= 1u << t;
+        for (int u = 0; u < kRowsPerProducer; ++u) {
+            const int r = t0 + u * kProducers;
+            const int64_t row = tile_row(a, tile * BM + r);
+            int* nb = S.nbr + buf * BM * 27 + r * 27;
+            if (row >= 0) {
+                if (a.nbr) {
+                    const int* src = a.nbr + row * 27;
+#pragma unroll 9
+                    for (int t = 0; t < 27; ++t) {
+                        const int j = __ldg(src + t);
+                        nb[t] = j;
+                        if (static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in)) m |= 1u << t;
+                    }
+                } else {
+                    nb[0] = static_cast<int>(row);
+                    m = 1u;
                 }
-            } else {
-                nb[0] = static_cast<int>(row);
-                m = 1u;
             }
+            S.rows[buf * BM + r] = static_cast<int>(row);
         }
-        S.rows[buf * BM + r] = static_cast<int>(row);
         m = __reduce_or_sync(0xffffffffu, m);
-        if ((r & 31) == 0) S.wmask[buf * kProducerWarps + warp] = m;
+        if ((t0 & 31) == 0) S.wmask[buf * kProducerWarps + warp] = m;
         asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
         mbar_arrive(&S.tile_ready[buf]);
         uint32_t rem = tile_mask(S, buf);
@@ -192,23 +196,28 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
             }
             uint8_t* sA = S.stages + s * C::STAGE;
             uint8_t* sB = sA + NA * C::A_PLANE;
-            if (r == 0) {
+            if (t0 == 0) {
                 mbar_arrive_expect_tx(&S.full[s], NB * C::B_PLANE);
                 bulk_g2s(smem_u32(sB), wdata + static_cast<int64_t>(tap * C::KCH + kc) * NB * C::B_PLANE,
                          NB * C::B_PLANE, &S.full[s]);
             }
-            int64_t j = -1;
-            if (row >= 0) {
-                const int jj = nb[tap];
-                if (static_cast<uint64_t>(jj) < static_cast<uint64_t>(a.n_in)) j = jj;
-            }
-            const uint32_t nbytes = j >= 0 ? 16u : 0u;
 #pragma unroll
-            for (int p = 0; p < NA; ++p) {
-                const __half* src = j >= 0 ? planes + p * plane_stride + j * CIN + kc * BK : planes;
-                const uint32_t dst = smem_u32(sA + p * C::A_PLANE);
+            for (int u = 0; u < kRowsPerProducer; ++u) {
+                const int r = t0 + u * kProducers;
+                int64_t j = -1;
+                if (S.rows[buf * BM + r] >= 0) {
+                    const int jj = S.nbr[buf * BM * 27 + r * 27 + tap];
+                    if (static_cast<uint64_t>(jj) < static_cast<uint64_t>(a.n_in)) j = jj;
+                }
+                const uint32_t nbytes = j >= 0 ? 16u : 0u;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) cp_async16(dst + sw128_offset(r, c), src + (j >= 0 ? c * 8 : 0), nbytes);
+                for (int p = 0; p < NA; ++p) {
+                    const __half* src = j >= 0 ? planes + p * plane_stride + j * CIN + kc * BK : planes;
+                    const uint32_t dst = smem_u32(sA + p * C::A_PLANE);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        cp_async16(dst + sw128_offset(r, c), src + (j >= 0 ? c * 8 : 0), nbytes);
+                }
             }
             cp_async_commit();
             if (i + 1 - arrived > LAG) {
@@ -348,17 +357,25 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
         uint64_t acc[COLS / 2];
 #pragma unroll
         for (int e = 0; e < COLS / 2; ++e) acc[e] = 0ull;
+        // activation block scales of this row, fetched one tap ahead
+        float sa[C::NBLK], sa_next[C::NBLK];
+        auto fetch_scales = [&](int tap, float (&dst)[C::NBLK]) {
+            const int j = (row >= 0 && tap >= 0) ? nb[tap] : -1;
+            const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
+#pragma unroll
+            for (int b = 0; b < C::NBLK; ++b)
+                dst[b] = v ? __ldg(a.a_scale + static_cast<int64_t>(j) * C::NBLK + b) : 0.f;
+        };
+        if (Q8) fetch_scales(rem ? __ffs(rem) - 1 : -1, sa_next);
         while (rem) {
             const int tap = __ffs(rem) - 1;
             rem &= rem - 1;
-            float sa[C::NBLK];
             if (Q8) {
-                const int j = row >= 0 ? nb[tap] : -1;
-                const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
 #pragma unroll
-                for (int b = 0; b < C::NBLK; ++b) sa[b] = v ? __ldg(a.a_scale + static_cast<int64_t>(j) * C::NBLK + b) : 0.f;
+                for (int b = 0; b < C::NBLK; ++b) sa[b] = sa_next[b];
+                fetch_scales(rem ? __ffs(rem) - 1 : -1, sa_next);
             }
-#pragma unroll 1
+#pragma unroll
             for (int grp = 0; grp < C::KCH * C::GPS; ++grp, ++g) {
                 const int slot = static_cast<int>(g % C::NACC);
                 if (!wait_or_abort(&S.acc_full[slot], static_cast<uint32_t>(g / C::NACC) & 1, S.abort, a.status))
@@ -377,21 +394,11 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                         mbar_arrive(&S.acc_empty[slot]);
                     }
                     if (Q8) {
-                        const float4* sb = reinterpret_cast<const float4*>(S.scaleB + (tap * C::NBLK + grp) * COUT + c_base + c);
-                        float sg = sa[0];
+                        const uint64_t s2 = pack2(sa[grp], sa[grp]);
 #pragma unroll
-                        for (int b = 1; b < C::NBLK; ++b) sg = grp == b ? sa[b] : sg;
-                        const uint64_t sa2 = pack2(sg, sg);
-#pragma unroll
-                        for (int e = 0; e < CH / 4; ++e) {
-                            const float4 w = sb[e];
-                            const uint64_t s0 = mul2(sa2, pack2(w.x, w.y));
-                            const uint64_t s1 = mul2(sa2, pack2(w.z, w.w));
-                            acc[c / 2 + 2 * e] = fma2(pack2(__uint_as_float(d[4 * e]), __uint_as_float(d[4 * e + 1])), s0,
-                                                      acc[c / 2 + 2 * e]);
-                            acc[c / 2 + 2 * e + 1] = fma2(pack2(__uint_as_float(d[4 * e + 2]), __uint_as_float(d[4 * e + 3])),
-                                                          s1, acc[c / 2 + 2 * e + 1]);
-                        }
+                        for (int e = 0; e < CH / 2; ++e)
+                            acc[c / 2 + e] =
+                                fma2(pack2(__uint_as_float(d[2 * e]), __uint_as_float(d[2 * e + 1])), s2, acc[c / 2 + e]);
                     } else {
 #pragma unroll
                         for (int e = 0; e < CH / 2; ++e)
@@ -434,8 +441,6 @@ __global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
     uint8_t* p = base + C::STAGES * C::STAGE;
     S.nbr = reinterpret_cast<int*>(p);
     p += C::NBR_BYTES;
-    S.scaleB = reinterpret_cast<float*>(p);
-    p += C::SCALE_BYTES;
     S.rows = reinterpret_cast<int*>(p);
     p += C::ROWS_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
@@ -469,13 +474,6 @@ __global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
     if (warp == kProducerWarps) {
         tmem_alloc(S.tmem, C::TMEM_COLS);
         tmem_relinquish();
-    }
-    if (Q8) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader) +
-                                                            static_cast<size_t>(a.ntaps) * C::KCH * C::B_PLANE);
-        float4* dst = reinterpret_cast<float4*>(S.scaleB);
-        const int nsc = (a.ntaps * C::NBLK * COUT) / 4;
-        for (int e = threadIdx.x; e < nsc; e += kThreads) dst[e] = __ldg(src + e);
     }
     tc_fence_before();
     __syncthreads();
@@ -525,7 +523,7 @@ cudaError_t launch_t(const ConvArgs& a, cudaStream_t st) {
 
 template <int CIN, int COUT>
 cudaError_t launch_planes(const ConvArgs& a, cudaStream_t st) {
-    if (a.q8) return launch_t<CIN, COUT, 1, 1, true>(a, st);
+    if (a.q8) return launch_t<CIN, COUT, 1, 2, true>(a, st);
     if (a.na == 1 && a.wplanes == 1) return launch_t<CIN, COUT, 1, 1, false>(a, st);
     if (a.na == 1 && a.wplanes == 2) return launch_t<CIN, COUT, 1, 2, false>(a, st);
     if (a.na == 2 && a.wplanes == 1) return launch_t<CIN, COUT, 2, 1, false>(a, st);

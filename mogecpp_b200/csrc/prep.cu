@@ -2,10 +2,10 @@
 //
 //  * weights: packed [cout][ntaps*cin] (f32, f16 or ggml block_q8_0 rows) ->
 //    blob of 128B-swizzled K-major fp16 tiles [tap][64-ch chunk][plane][cout][64].
-//    f16 weights are one exact plane; f32 weights become an exact hi/lo pair
-//    after a power-of-two prescale that puts max|w| near 2^14 (undone in the
-//    conv epilogue); Q8_0 weights become one plane of their int8 codes plus
-//    the fp16 block scales as fp32 [tap][cin/32][cout] after the planes.
+//    f16 weights are one exact plane; f32 weights and Q8_0 weights (their
+//    exact dequantised value q * fp16(d)) become an exact hi/lo pair after a
+//    power-of-two prescale that puts max|w| near 2^14 (undone in the conv
+//    epilogue).
 //  * activations: [n][c] rows (f32/f16/bf16), optional LayerNorm + SiLU
 //    (mogecpp src/sparse.cpp:520-526, ggml norm_f32 / silu), then
 //      ACT_FP16  round to fp16                      (ggml F16 vec_dot_type)
@@ -69,7 +69,7 @@ __global__ void weight_split_kernel(WeightHeader* h, int wtype, const void* w, i
                                     int planes, uint8_t* out) {
     const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
     const int64_t total = row_len * cout;
-    const int s = (planes == 2 && wtype != WT_Q8_0) ? prescale_exp(h->amax) : 0;
+    const int s = planes == 2 ? prescale_exp(h->amax) : 0;
     const int kch = cin / 64;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -79,22 +79,12 @@ __global__ void weight_split_kernel(WeightHeader* h, int wtype, const void* w, i
         const int ci = static_cast<int>(k % cin);
         const int kc = ci / 64, e = ci % 64;
         __half hi, lo;
-        if (wtype == WT_Q8_0) {
-            const BlockQ8* b = static_cast<const BlockQ8*>(w) + (o * row_len + k) / 32;
-            hi = __int2half_rn(b->qs[k % 32]);
-            lo = __float2half_rn(0.0f);
-            if (k % 32 == 0) {
-                float* scales = reinterpret_cast<float*>(out + static_cast<int64_t>(ntaps) * cin * cout * 2);
-                scales[(static_cast<int64_t>(t) * (cin / 32) + ci / 32) * cout + o] = __half2float(b->d);
-            }
+        const float v = ldexpf(weight_value(wtype, w, row_len, o, k), s);
+        if (planes == 2) {
+            split_f16(v, hi, lo);
         } else {
-            const float v = ldexpf(weight_value(wtype, w, row_len, o, k), s);
-            if (planes == 2) {
-                split_f16(v, hi, lo);
-            } else {
-                hi = __float2half_rn(v);
-                lo = __float2half_rn(0.0f);
-            }
+            hi = __float2half_rn(v);
+            lo = __float2half_rn(0.0f);
         }
         const int64_t tile = static_cast<int64_t>(t * kch + kc) * planes;
         const uint32_t off = sw128_offset(o, e >> 3) + (e & 7) * 2;
@@ -182,12 +172,10 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
 
 }  // namespace
 
-int weight_planes(int wtype) { return wtype == WT_F32 ? 2 : 1; }
+int weight_planes(int wtype) { return wtype == WT_F16 ? 1 : 2; }
 
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
-    size_t b = sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype)) * ntaps * cin * cout * 2;
-    if (wtype == WT_Q8_0) b += static_cast<size_t>(ntaps) * (cin / 32) * cout * 4;
-    return b;
+    return sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype)) * ntaps * cin * cout * 2;
 }
 
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
@@ -196,7 +184,7 @@ cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, i
     const int planes = weight_planes(wtype);
     const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
     weight_header_kernel<<<1, 1, 0, st>>>(h, wtype, cin, cout, ntaps, planes);
-    if (wtype == WT_F32) weight_amax_kernel<<<148, 256, 0, st>>>(h, wtype, w, row_len, cout);
+    if (planes == 2) weight_amax_kernel<<<148, 256, 0, st>>>(h, wtype, w, row_len, cout);
     const int64_t total = row_len * cout;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 16));
     weight_split_kernel<<<grid, 256, 0, st>>>(h, wtype, w, cin, cout, ntaps, planes,

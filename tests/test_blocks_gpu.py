@@ -61,21 +61,33 @@ def test_res_block_c128_matches_oracle(ex, oracle, tag, dt):
 
 
 def test_four_block_q8_stack_fp16_state(ex, oracle):
-    """The res4_c128 workload's arithmetic on a small surface: four blocks,
-    fp16 state between blocks (the oracle rounds its state the same way)."""
+    """The res4_c128 workload's arithmetic on a small surface: four blocks with
+    fp16 state between blocks.
+
+    Each block is checked against the oracle run on that block's actual fp16
+    input, at the full tolerance.  The four-block chain is compared with the
+    oracle's own chain (same fp16 rounding of the state) at a looser bound:
+    ggml's activation re-quantisation turns last-bit summation-order
+    differences into one-step code flips that compound over blocks.  On this
+    input the reference's own CPU code and the oracle (both exact up to
+    summation order) already differ by rel-L2 6.1e-4 / 1.26e-3 and max-abs
+    0.0098 / 0.0137 after three / four blocks, so the chain bound is 3e-3."""
     coords = synth.small_coords(90, extent=28, grid=32)
     nbr = oracle.make_level(coords)
     x = dev(synth.features(91, coords.shape[0], 128)).to(torch.float16)
-    ref = host(x)
+    chain = host(x)
     nbrd = dev(nbr)
     for b in range(4):
         raw = raw_block(100 + 10 * b, 128)
+        xin = host(x)
         ex.res_block(x, nbrd, make_block(ex, oracle, raw, "q8_0", 128))
-        ref = oracle.res_block(ref, nbr, raw, W_Q8_0).astype(np.float16).astype(np.float32)
         ex.check()
         y = host(x)
+        ref = oracle.res_block(xin, nbr, raw, W_Q8_0)
         assert rel_l2(y, ref) < TOL_FP16[0], (b, rel_l2(y, ref))
-        assert max_abs(y, ref) < TOL_FP16[1]
+        assert max_abs(y, ref) < TOL_FP16[1], (b, max_abs(y, ref))
+        chain = oracle.res_block(chain, nbr, raw, W_Q8_0).astype(np.float16).astype(np.float32)
+        assert rel_l2(y, chain) < 3e-3, (b, rel_l2(y, chain))
 
 
 def test_pool_and_up_match_reference_golden(ex, oracle, golden_features):
