@@ -134,8 +134,8 @@ msc_context::Blob blob_info(msc_ctx_t ctx, const void* blob) {
     return it->second;
 }
 
-int act_mode(int wtype, int x_dtype) {
-    if (wtype == MSC_W_Q8_0) return msc::ACT_Q8;
+int act_mode(int wtype, int x_dtype, int cin) {
+    if (wtype == MSC_W_Q8_0) return msc::weight_is_i8(wtype, cin) ? msc::ACT_Q8I : msc::ACT_Q8;
     if (wtype == MSC_W_F16) return msc::ACT_FP16;
     return x_dtype == MSC_F16 ? msc::ACT_FP16 : msc::ACT_SPLIT;
 }
@@ -158,8 +158,10 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
               int res_dtype, void* y, int y_dtype, cudaStream_t st) {
     msc::ConvArgs a{};
     a.planes = planes;
-    a.q8 = mode == msc::ACT_Q8;
-    a.a_scale = a.q8 ? reinterpret_cast<const float*>(static_cast<const char*>(planes) + msc::act_scale_offset(n, cin))
+    a.q8 = mode == msc::ACT_Q8 || mode == msc::ACT_Q8I;
+    a.i8 = mode == msc::ACT_Q8I;
+    a.a_scale = a.q8 ? reinterpret_cast<const float*>(static_cast<const char*>(planes) +
+                                                      msc::act_scale_offset(mode, n, cin))
                      : nullptr;
     a.na = msc::act_planes(mode);
     a.n_in = n;
@@ -332,7 +334,7 @@ int msc_weight_prepare(msc_ctx_t ctx, int wtype, const void* w, int cin, int cou
         need_ws(blob_bytes, want);
         cuda_ok(msc::launch_weight_prepare(wtype, w, cin, cout, ntaps, blob, S(stream)), "weight prepare launch");
         std::lock_guard<std::mutex> lk(ctx->mu);
-        ctx->blobs[blob] = msc_context::Blob{wtype, cin, cout, ntaps, msc::weight_planes(wtype), want};
+        ctx->blobs[blob] = msc_context::Blob{wtype, cin, cout, ntaps, msc::weight_planes(wtype, cin), want};
     });
 }
 
@@ -356,7 +358,7 @@ int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int ci
         need_aligned(x, 16, "x");
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
-        const int mode = act_mode(b.wtype, x_dtype);
+        const int mode = act_mode(b.wtype, x_dtype, b.cin);
         need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
@@ -378,7 +380,7 @@ int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, co
         need_aligned(x, 16, "x");
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
-        const int mode = act_mode(b.wtype, x_dtype);
+        const int mode = act_mode(b.wtype, x_dtype, b.cin);
         need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
@@ -406,11 +408,11 @@ int msc_res_block(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const i
         need_ws(ws_bytes, planes_bytes + static_cast<size_t>(n) * c * 4);
         void* planes = ws;
         float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
-        const int m1 = act_mode(w1.wtype, x_dtype);
+        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin);
         cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
                 "norm1 prepare");
         run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream));
-        const int m2 = act_mode(w2.wtype, MSC_F32);
+        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin);
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
         run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream));
@@ -432,7 +434,7 @@ int msc_pool_down(msc_ctx_t ctx, const void* x, int x_dtype, int64_t nfine, int 
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
         const size_t pooled_bytes = align256(static_cast<size_t>(np) * c * 4);
-        const int mode = act_mode(b.wtype, MSC_F32);
+        const int mode = act_mode(b.wtype, MSC_F32, b.cin);
         need_ws(ws_bytes, pooled_bytes + msc::act_bytes(mode, np, c));
         float* pooled = static_cast<float*>(ws);
         void* planes = static_cast<char*>(ws) + pooled_bytes;
@@ -462,7 +464,7 @@ int msc_nearest_up(msc_ctx_t ctx, const void* x, int x_dtype, int64_t np, int c,
         need(x && up_rows && y && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(ws, 256, "workspace");
-        const int mode = act_mode(b.wtype, x_dtype);
+        const int mode = act_mode(b.wtype, x_dtype, b.cin);
         const size_t planes_bytes = align256(msc::act_bytes(mode, np, c));
         need_ws(ws_bytes, planes_bytes + static_cast<size_t>(np) * b.cout * 4);
         void* planes = ws;

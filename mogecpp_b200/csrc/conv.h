@@ -13,9 +13,9 @@ enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2 };
 // weight type codes (ggml order)
 enum WType : int { WT_F32 = 0, WT_F16 = 1, WT_Q8_0 = 8 };
 // activation preparation modes: fp16 rounding (1 plane), exact hi/lo split
-// of the fp32 value (2 planes), Q8_0 quantisation (1 plane of int8 codes as
-// fp16 + one fp32 scale per 32 channels).
-enum ActMode : int { ACT_FP16 = 0, ACT_SPLIT = 1, ACT_Q8 = 2 };
+// of the fp32 value (2 planes), Q8_0 quantisation (1 plane of the int8 codes
+// as fp16, or ACT_Q8I as int8, + one fp32 scale per 32 channels).
+enum ActMode : int { ACT_FP16 = 0, ACT_SPLIT = 1, ACT_Q8 = 2, ACT_Q8I = 3 };
 
 // Prepared-weight blob header (first 256 bytes of the blob).
 struct WeightHeader {
@@ -32,17 +32,20 @@ struct WeightHeader {
 static_assert(sizeof(WeightHeader) == 256, "header is 256 bytes");
 constexpr uint32_t kWeightMagic = 0x4d534357u;  // "WCSM"
 
-// Planes of the prepared weight: f16 -> 1 (exact); f32 and Q8_0 -> 2 (exact
-// hi/lo pair of the prescaled dequantised value).
-int weight_planes(int wtype);
+// Prepared weight layouts: f16 -> one exact fp16 plane; f32 and Q8_0 with
+// cin != 128 -> exact hi/lo fp16 pair of the prescaled dequantised value;
+// Q8_0 with cin == 128 -> int8 code tiles followed by the fp32 block scales
+// [ntaps][cin/32][cout] (the kind::i8 path).
+bool weight_is_i8(int wtype, int cin);
+int weight_planes(int wtype, int cin);
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps);
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob, cudaStream_t st);
 
 int act_planes(int mode);
 // Bytes of the prepared activation operand for n rows of c channels.
 size_t act_bytes(int mode, int64_t n, int c);
-// Q8 mode: the per-block scales follow the code plane at this byte offset.
-size_t act_scale_offset(int64_t n, int c);
+// Q8 modes: the per-block scales follow the code plane at this byte offset.
+size_t act_scale_offset(int mode, int64_t n, int c);
 // x: [n][c] (dtype) -> prepared operand (planes [act_planes][n][c] fp16, plus
 // scales in Q8 mode).  Optional LayerNorm (affine gamma/beta, either may be
 // null) and SiLU before preparation.
@@ -54,6 +57,7 @@ struct ConvArgs {
     const float* a_scale;    // Q8: [n_in][cin/32] per-block activation scales, else null
     int na;                  // 1 or 2
     int q8;                  // ggml Q8_0 x Q8_0 block arithmetic
+    int i8;                  // Q8 with int8 code planes (kind::i8 MMA; cin 128)
     int64_t n_in;            // rows of the input planes (neighbour indices >= n_in are missing)
     int64_t n;               // output rows processed
     int64_t row_begin;       // output row k is row_begin + k (when perm is null)

@@ -8,18 +8,20 @@
 //
 // Tiles of 128 output voxels (M) x cout (N).  K runs over the taps present
 // in the tile (taps with no valid neighbour in any of its rows are skipped)
-// and 64-channel chunks.  Operands are fp16 "planes" in shared memory
-// (128-byte swizzled, K-major):
-//   * Q8 mode (ggml Q8_0 x Q8_0, the path of Q8_0 weights): A = the
-//     activation's int8 codes qa (exact in fp16), B = the exact hi/lo pair of
-//     the prescaled weight d_w * qw.  One MMA group per 32-channel block
-//     gives d_w * isum with exact products and a 4-MMA accumulation chain;
-//     the drain warps apply the activation block scale,
-//         acc += d_a * (d_w * isum)      (ggml-cpu x86 quants.c:1308 sums
-//                                          fp16(d_a)*fp16(d_w)*isum per block)
-//   * other modes: A and B are one fp16 plane or an exact hi/lo pair
-//     (hi*hi + hi*lo + lo*hi); one MMA group per 64-channel chunk, drained
-//     with an fp32 add.
+// and 128-byte operand rows.  Operands sit in shared memory 128-byte
+// swizzled, K-major.  Three arithmetic kinds:
+//   * KIND_Q8I (ggml Q8_0 weights, cin = 128): A = the activation's int8
+//     Q8_0 codes, B = the weight's int8 codes; one kind::i8 MMA per
+//     32-channel block gives the exact int32 block dot product isum; the
+//     drain warps apply ggml's per-block scale
+//         acc += (d_a * d_w) * isum       (ggml-cpu x86 quants.c:1308)
+//   * KIND_Q8F (ggml Q8_0 weights, cin = 64): A = the int8 codes as fp16,
+//     B = the exact hi/lo fp16 pair of the prescaled weight d_w * q_w; one
+//     MMA group per 32-channel block gives d_w * isum exactly (4-MMA chain),
+//     the drain applies d_a.
+//   * KIND_F (f32 / f16 weights): A and B are one fp16 plane or an exact
+//     hi/lo pair (hi*hi + hi*lo + lo*hi); one MMA group per 64-channel chunk,
+//     drained with an fp32 add.
 // Draining every group keeps each tensor-core accumulation chain to a few
 // MMAs: the tcgen05 fp32 accumulator does not round to nearest, and long
 // chains drift by ~1e-6 relative, which ggml's activation re-quantisation
@@ -27,16 +29,18 @@
 //
 // Persistent CTA, one per SM, 19 warps:
 //   warps 0-1   producers: per tile, stage the rows' neighbour lists and the
-//               tap mask; per stage, gather two A rows per thread with 16-byte
-//               cp.async (sentinel rows zero-filled); thread 0 bulk-copies
-//               the stage's pre-swizzled B tile.
+//               tap mask; per stage, gather the 128 A rows with coalesced
+//               16-byte cp.async (8 lanes per 128-byte row, swizzled straight
+//               into the UMMA layout; sentinel rows zero-filled); thread 0
+//               bulk-copies the stage's pre-swizzled B tile.
 //   warp 2      TMEM allocation and the single-thread MMA issue loop.
 //   warps 3-18  drain + epilogue: TMEM lane quarter (warp % 4) x column quarter;
 //               fp32 accumulators in registers, bias / SiLU / residual / store.
 // Pipelines (mbarriers): smem stages full/empty, TMEM accumulator slots
 // acc_full/acc_empty (NACC rotating slots), per-tile tile_ready/tile_free
-// (double-buffered neighbour lists).  Every wait is bounded; a wait that runs
-// out sets MSC_DEV_TIMEOUT and the CTA unwinds.
+// (double-buffered neighbour lists).  Taps are visited in a per-tile rotated
+// order.  Every wait is bounded; a wait that runs out sets MSC_DEV_TIMEOUT
+// and the CTA unwinds.
 #include "common.cuh"
 #include "conv.h"
 
@@ -44,7 +48,6 @@ namespace msc {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 64;  // fp16 elements per stage row (128 B)
 constexpr int kProducerWarps = 2;
 constexpr int kDrainWarps = 16;
 constexpr int kThreads = 32 * (kProducerWarps + 1 + kDrainWarps);
@@ -53,37 +56,48 @@ constexpr int kDrainers = 32 * kDrainWarps;
 constexpr int kRowsPerProducer = BM / kProducers;
 constexpr int kSmemLimit = 227 * 1024;  // max dynamic shared memory per block on sm_100
 
-template <int CIN, int COUT, int NA, int NB, bool Q8>
+enum Kind : int { KIND_F = 0, KIND_Q8F = 1, KIND_Q8I = 2 };
+
+template <int CIN, int COUT, int NA, int NB, int KIND>
 struct Cfg {
-    static constexpr int KCH = CIN / BK;
-    static constexpr int NBLK = CIN / 32;
-    static constexpr int A_PLANE = BM * BK * 2;
-    static constexpr int B_PLANE = COUT * BK * 2;
+    static constexpr int ELEM = KIND == KIND_Q8I ? 1 : 2;   // bytes per A/B element
+    static constexpr int ROW_BYTES = CIN * ELEM;             // one activation row
+    static constexpr int KCH = ROW_BYTES / 128;              // 128-byte chunks per tap
+    static constexpr int NBLK = CIN / 32;                    // Q8_0 blocks per tap
+    static constexpr int A_PLANE = BM * 128;
+    static constexpr int B_PLANE = COUT * 128;
     static constexpr int STAGE = NA * A_PLANE + NB * B_PLANE;
-    static constexpr int GPS = Q8 ? 2 : 1;          // accumulator groups per stage
-    static constexpr int KSPG = (BK / 16) / GPS;    // MMA k-steps per group
+    // accumulator groups per stage and MMA k-steps (32 bytes of K) per group
+    static constexpr int GPS = KIND == KIND_Q8I ? 4 : (KIND == KIND_Q8F ? 2 : 1);
+    static constexpr int KSPG = 4 / GPS;
     static constexpr int NACC = (512 / COUT) < 4 ? (512 / COUT) : 4;
     static constexpr int TMEM_COLS = NACC * COUT;
     static constexpr int COLS = COUT / (kDrainWarps / 4);  // columns per drain thread
     static constexpr int NBR_BYTES = 2 * BM * 27 * 4;
     static constexpr int ROWS_BYTES = 2 * BM * 4;
+    static constexpr int SB_BYTES = KIND == KIND_Q8I ? 27 * NBLK * COUT * 4 : 0;  // weight block scales
     static constexpr int BAR_BYTES = 512;
-    static constexpr int FIXED = NBR_BYTES + ROWS_BYTES + BAR_BYTES;
+    static constexpr int FIXED = NBR_BYTES + ROWS_BYTES + SB_BYTES + BAR_BYTES;
     static constexpr int STAGES_FIT = (kSmemLimit - 1024 - FIXED) / STAGE;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int SMEM = 1024 + STAGES * STAGE + FIXED;
+    // gather groups a producer keeps in flight; at least one stage of slack
+    // between the stage being published and the stage being refilled
+    static constexpr int LAG = STAGES >= 4 ? STAGES - 2 : 1;
     static_assert(STAGES >= 2, "at least two pipeline stages");
-    static_assert(CIN % BK == 0, "cin must be a multiple of 64");
+    static_assert(ROW_BYTES % 128 == 0, "activation rows must be whole 128-byte chunks");
     static_assert(COUT % 64 == 0 && COUT <= 256, "cout must be 64..256 in steps of 64");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
-    static_assert(!Q8 || (NA == 1 && NB == 2), "Q8 mode: integer code plane x exact weight pair");
+    static_assert(KIND != KIND_Q8F || (NA == 1 && NB == 2), "Q8F: code plane x exact weight pair");
+    static_assert(KIND != KIND_Q8I || (NA == 1 && NB == 1 && CIN == 128), "Q8I: int8 planes, cin 128");
     static_assert(SMEM <= kSmemLimit, "shared memory budget");
 };
 
 struct Smem {
     uint8_t* stages;
-    int* nbr;        // [2][BM*27]
+    int* nbr;        // [2][BM*27], missing neighbour = -1
     int* rows;       // [2][BM]
+    float* sB;       // [27][NBLK][COUT] weight block scales (Q8I)
     uint64_t* full;
     uint64_t* empty;
     uint64_t* acc_full;
@@ -119,24 +133,62 @@ __device__ __forceinline__ uint32_t tile_mask(const Smem& S, int buf) {
     return m;
 }
 
+// Taps are visited in a per-tile rotated order so that the CTAs, which all
+// stream the same small weight tensor, do not request the same weight tile
+// from L2 at the same moment.  rot_mask() rotates the tap mask so that bit 0
+// is tap `r`; rot_tap() maps a rotated bit back to the tap.
+__device__ __forceinline__ int tap_rotation(int64_t tile, int ntaps) {
+    return ntaps == 27 ? static_cast<int>(tile % 27) : 0;
+}
+__device__ __forceinline__ uint32_t rot_mask(uint32_t m, int r) {
+    return r ? ((m >> r) | (m << (27 - r))) & 0x7ffffffu : m;
+}
+__device__ __forceinline__ int rot_tap(int bit, int r) {
+    const int t = bit + r;
+    return t >= 27 ? t - 27 : t;
+}
+
 __device__ __forceinline__ int64_t tile_row(const ConvArgs& a, int64_t idx) {
     if (idx >= a.n) return -1;
     return a.perm ? static_cast<int64_t>(__ldg(a.perm + idx)) : a.row_begin + idx;
 }
 
+// D[tmem] (+)= A * B^T, kind::i8 (signed int8 operands, int32 accumulator).
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Instruction descriptor for kind::i8: signed int8 A and B (format 1), int32
+// accumulator (format 2), both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 // ------------------------------------------------------------------ roles
 
-template <int CIN, int COUT, int NA, int NB, bool Q8>
+template <int CIN, int COUT, int NA, int NB, int KIND>
 __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
-    using C = Cfg<CIN, COUT, NA, NB, Q8>;
-    const int t0 = threadIdx.x;  // 0..kProducers-1; owns tile rows t0 + u*kProducers
+    using C = Cfg<CIN, COUT, NA, NB, KIND>;
+    const int t0 = threadIdx.x;  // 0..kProducers-1
     const int warp = t0 >> 5;
-    const __half* planes = static_cast<const __half*>(a.planes);
+    const int lane = t0 & 31;
+    const int chunk = lane & 7;            // 16-byte chunk of a 128-byte row
+    const int rsub = lane >> 3;            // row within a group of 4
+    constexpr int kRowsPerWarp = BM / kProducerWarps;
+    constexpr int kCopies = kRowsPerWarp / 4;  // cp.async per lane per plane per stage
+    const uint8_t* planes = static_cast<const uint8_t*>(a.planes);
     const uint8_t* wdata = static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader);
-    const int64_t plane_stride = a.n_in * CIN;
-    constexpr int LAG = C::STAGES - 1;
+    const int64_t plane_bytes = a.n_in * C::ROW_BYTES;
+    constexpr int LAG = C::LAG;
     int64_t i = 0;        // stages issued
-    int64_t arrived = 0;  // stages whose full barrier this thread has arrived on
+    int64_t arrived = 0;  // stages this thread has published (arrived on full)
     bool ok = true;
     int k = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++k) {
@@ -152,7 +204,7 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
                 break;
             }
         }
-        // neighbour lists and tap mask of this thread's rows
+        // neighbour lists and tap mask of this thread's rows (t0, t0+64)
         uint32_t m = 0;
 #pragma unroll
         for (int u = 0; u < kRowsPerProducer; ++u) {
@@ -165,26 +217,32 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
 #pragma unroll 9
                     for (int t = 0; t < 27; ++t) {
                         const int j = __ldg(src + t);
-                        nb[t] = j;
-                        if (static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in)) m |= 1u << t;
+                        const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
+                        nb[t] = v ? j : -1;
+                        if (v) m |= 1u << t;
                     }
                 } else {
                     nb[0] = static_cast<int>(row);
                     m = 1u;
                 }
+            } else {
+#pragma unroll 9
+                for (int t = 0; t < 27; ++t) nb[t] = -1;
             }
             S.rows[buf * BM + r] = static_cast<int>(row);
         }
         m = __reduce_or_sync(0xffffffffu, m);
-        if ((t0 & 31) == 0) S.wmask[buf * kProducerWarps + warp] = m;
+        if (lane == 0) S.wmask[buf * kProducerWarps + warp] = m;
         asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
         mbar_arrive(&S.tile_ready[buf]);
-        uint32_t rem = tile_mask(S, buf);
+        const int rot = tap_rotation(tile, a.ntaps);
+        uint32_t rem = rot_mask(tile_mask(S, buf), rot);
         const int nst = __popc(rem) * C::KCH;
         int tap = -1, kc = C::KCH;
+        const int* nbw = S.nbr + buf * BM * 27 + (warp * kRowsPerWarp + rsub) * 27;
         for (int st = 0; st < nst; ++st, ++i) {
             if (kc == C::KCH) {
-                tap = __ffs(rem) - 1;
+                tap = rot_tap(__ffs(rem) - 1, rot);
                 rem &= rem - 1;
                 kc = 0;
             }
@@ -201,22 +259,19 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
                 bulk_g2s(smem_u32(sB), wdata + static_cast<int64_t>(tap * C::KCH + kc) * NB * C::B_PLANE,
                          NB * C::B_PLANE, &S.full[s]);
             }
+            // coalesced gather: 8 lanes per 128-byte row, 4 rows per instruction
 #pragma unroll
-            for (int u = 0; u < kRowsPerProducer; ++u) {
-                const int r = t0 + u * kProducers;
-                int64_t j = -1;
-                if (S.rows[buf * BM + r] >= 0) {
-                    const int jj = S.nbr[buf * BM * 27 + r * 27 + tap];
-                    if (static_cast<uint64_t>(jj) < static_cast<uint64_t>(a.n_in)) j = jj;
-                }
+            for (int q = 0; q < kCopies; ++q) {
+                const int r = warp * kRowsPerWarp + rsub + 4 * q;
+                const int j = nbw[(4 * q) * 27 + tap];
                 const uint32_t nbytes = j >= 0 ? 16u : 0u;
+                const uint32_t dst = smem_u32(sA) + sw128_offset(r, chunk);
 #pragma unroll
                 for (int p = 0; p < NA; ++p) {
-                    const __half* src = j >= 0 ? planes + p * plane_stride + j * CIN + kc * BK : planes;
-                    const uint32_t dst = smem_u32(sA + p * C::A_PLANE);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        cp_async16(dst + sw128_offset(r, c), src + (j >= 0 ? c * 8 : 0), nbytes);
+                    const uint8_t* src =
+                        j >= 0 ? planes + p * plane_bytes + static_cast<int64_t>(j) * C::ROW_BYTES + kc * 128 + chunk * 16
+                               : planes;
+                    cp_async16(dst + p * C::A_PLANE, src, nbytes);
                 }
             }
             cp_async_commit();
@@ -236,10 +291,10 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
     }
 }
 
-template <int CIN, int COUT, int NA, int NB, bool Q8>
+template <int CIN, int COUT, int NA, int NB, int KIND>
 __device__ void mma_issuer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32_t tmem) {
-    using C = Cfg<CIN, COUT, NA, NB, Q8>;
-    constexpr uint32_t idesc = idesc_f16(BM, COUT, 0);
+    using C = Cfg<CIN, COUT, NA, NB, KIND>;
+    constexpr uint32_t idesc = KIND == KIND_Q8I ? idesc_i8(BM, COUT) : idesc_f16(BM, COUT, 0);
     int64_t i = 0, g = 0;
     int k = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
@@ -266,9 +321,13 @@ __device__ void mma_issuer(const ConvArgs& a, const Smem& S, int64_t ntiles, uin
                     const uint32_t off = static_cast<uint32_t>((gg * C::KSPG + ks) * 32);
                     const uint64_t ah = sdesc_k_sw128(aaddr + off);
                     const uint64_t bh = sdesc_k_sw128(baddr + off);
-                    umma_f16(d, ah, bh, idesc, ks > 0 ? 1u : 0u);
-                    if (NB == 2) umma_f16(d, ah, sdesc_k_sw128(baddr + C::B_PLANE + off), idesc, 1u);
-                    if (NA == 2) umma_f16(d, sdesc_k_sw128(aaddr + C::A_PLANE + off), bh, idesc, 1u);
+                    if (KIND == KIND_Q8I) {
+                        umma_i8(d, ah, bh, idesc, ks > 0 ? 1u : 0u);
+                    } else {
+                        umma_f16(d, ah, bh, idesc, ks > 0 ? 1u : 0u);
+                        if (NB == 2) umma_f16(d, ah, sdesc_k_sw128(baddr + C::B_PLANE + off), idesc, 1u);
+                        if (NA == 2) umma_f16(d, sdesc_k_sw128(aaddr + C::A_PLANE + off), bh, idesc, 1u);
+                    }
                 }
                 umma_commit(&S.acc_full[slot]);
             }
@@ -288,11 +347,6 @@ __device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
 __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     uint64_t r;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
 __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
@@ -334,13 +388,22 @@ __device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const
     }
 }
 
-template <int CIN, int COUT, int NA, int NB, bool Q8>
+// Magic-number conversion of an int32 in (-2^22, 2^22) to fp32: the integer
+// added to the bits of 1.5*2^23 lands in the mantissa, so subtracting
+// 1.5*2^23 afterwards is exact.
+constexpr int kMagicBits = 0x4B400000;
+constexpr float kMagic = 12582912.0f;
+
+template <int CIN, int COUT, int NA, int NB, int KIND>
 __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32_t tmem) {
-    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+    using C = Cfg<CIN, COUT, NA, NB, KIND>;
+    constexpr bool Q8 = KIND != KIND_F;
     constexpr int COLS = C::COLS;
+    // TMEM columns per load: 16 for the int8 path keeps its drain in registers
+    constexpr int CH = (COLS < 32 || KIND == KIND_Q8I) ? 16 : 32;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int q = warp & 3;                       // TMEM lane quarter
+    const int q = warp & 3;                              // TMEM lane quarter
     const int part = (warp - kProducerWarps - 1) >> 2;  // column slice
     const int m = q * 32 + lane;                         // tile row
     const int c_base = part * COLS;
@@ -351,7 +414,8 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
         const int buf = k & 1;
         if (!wait_or_abort(&S.tile_ready[buf], (k >> 1) & 1, S.abort, a.status)) return;
-        uint32_t rem = tile_mask(S, buf);
+        const int rot = tap_rotation(tile, a.ntaps);
+        uint32_t rem = rot_mask(tile_mask(S, buf), rot);
         const int row = S.rows[buf * BM + m];
         const int* nb = S.nbr + buf * BM * 27 + m * 27;
         uint64_t acc[COLS / 2];
@@ -361,29 +425,34 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
         float sa[C::NBLK], sa_next[C::NBLK];
         auto fetch_scales = [&](int tap, float (&dst)[C::NBLK]) {
             const int j = (row >= 0 && tap >= 0) ? nb[tap] : -1;
-            const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
 #pragma unroll
             for (int b = 0; b < C::NBLK; ++b)
-                dst[b] = v ? __ldg(a.a_scale + static_cast<int64_t>(j) * C::NBLK + b) : 0.f;
+                dst[b] = j >= 0 ? __ldg(a.a_scale + static_cast<int64_t>(j) * C::NBLK + b) : 0.f;
         };
-        if (Q8) fetch_scales(rem ? __ffs(rem) - 1 : -1, sa_next);
+        if (Q8) fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
         while (rem) {
-            const int tap = __ffs(rem) - 1;
+            const int tap = rot_tap(__ffs(rem) - 1, rot);
             rem &= rem - 1;
             if (Q8) {
 #pragma unroll
                 for (int b = 0; b < C::NBLK; ++b) sa[b] = sa_next[b];
-                fetch_scales(rem ? __ffs(rem) - 1 : -1, sa_next);
+                fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
             }
-#pragma unroll
+#pragma unroll 1
             for (int grp = 0; grp < C::KCH * C::GPS; ++grp, ++g) {
+                // this group's activation block scale (select chain keeps sa in registers)
+                float sg = 0.f;
+                if (Q8) {
+                    sg = sa[0];
+#pragma unroll
+                    for (int b = 1; b < C::NBLK; ++b) sg = grp == b ? sa[b] : sg;
+                }
                 const int slot = static_cast<int>(g % C::NACC);
                 if (!wait_or_abort(&S.acc_full[slot], static_cast<uint32_t>(g / C::NACC) & 1, S.abort, a.status))
                     return;
                 tc_fence_after();
                 // CH columns at a time: load, wait, accumulate; release the slot
                 // after the last load has landed
-                constexpr int CH = COLS < 32 ? COLS : 32;
 #pragma unroll
                 for (int c = 0; c < COLS; c += CH) {
                     uint32_t d[CH];
@@ -393,8 +462,26 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                         tc_fence_before();
                         mbar_arrive(&S.acc_empty[slot]);
                     }
-                    if (Q8) {
-                        const uint64_t s2 = pack2(sa[grp], sa[grp]);
+                    if (KIND == KIND_Q8I) {
+                        // acc += (d_a * d_w[n]) * isum[n]: (isum * d_a) is rounded once
+                        // by an FMA that also removes the conversion offset, then
+                        // fused into the accumulator with d_w[n]
+                        const uint64_t s2 = pack2(sg, sg);
+                        const uint64_t off2 = pack2(-kMagic * sg, -kMagic * sg);
+                        const float4* sb = reinterpret_cast<const float4*>(
+                            S.sB + (tap * C::NBLK + grp) * COUT + c_base + c);
+#pragma unroll
+                        for (int e = 0; e < CH / 4; ++e) {
+                            const float4 w = sb[e];
+                            const uint64_t f0 = pack2(__int_as_float(static_cast<int>(d[4 * e]) + kMagicBits),
+                                                      __int_as_float(static_cast<int>(d[4 * e + 1]) + kMagicBits));
+                            const uint64_t f1 = pack2(__int_as_float(static_cast<int>(d[4 * e + 2]) + kMagicBits),
+                                                      __int_as_float(static_cast<int>(d[4 * e + 3]) + kMagicBits));
+                            acc[c / 2 + 2 * e] = fma2(fma2(f0, s2, off2), pack2(w.x, w.y), acc[c / 2 + 2 * e]);
+                            acc[c / 2 + 2 * e + 1] = fma2(fma2(f1, s2, off2), pack2(w.z, w.w), acc[c / 2 + 2 * e + 1]);
+                        }
+                    } else if (KIND == KIND_Q8F) {
+                        const uint64_t s2 = pack2(sg, sg);
 #pragma unroll
                         for (int e = 0; e < CH / 2; ++e)
                             acc[c / 2 + e] =
@@ -431,9 +518,11 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
     }
 }
 
-template <int CIN, int COUT, int NA, int NB, bool Q8>
-__global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
-    using C = Cfg<CIN, COUT, NA, NB, Q8>;
+// Register budget: the launch check rounds the warp count up to a multiple of
+// four, so 19 warps are charged as 20 x 32 threads x 96 registers = 61440.
+template <int CIN, int COUT, int NA, int NB, int KIND>
+__global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
+    using C = Cfg<CIN, COUT, NA, NB, KIND>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Smem S;
@@ -443,6 +532,8 @@ __global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
     p += C::NBR_BYTES;
     S.rows = reinterpret_cast<int*>(p);
     p += C::ROWS_BYTES;
+    S.sB = reinterpret_cast<float*>(p);
+    p += C::SB_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
     S.full = bars;
     S.empty = S.full + C::STAGES;
@@ -475,6 +566,14 @@ __global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
         tmem_alloc(S.tmem, C::TMEM_COLS);
         tmem_relinquish();
     }
+    if (KIND == KIND_Q8I) {
+        // weight block scales [ntaps][NBLK][COUT] follow the code tiles
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader) +
+                                                            static_cast<size_t>(a.ntaps) * C::KCH * C::B_PLANE);
+        float4* dst = reinterpret_cast<float4*>(S.sB);
+        const int n4 = a.ntaps * C::NBLK * COUT / 4;
+        for (int e = threadIdx.x; e < n4; e += kThreads) dst[e] = __ldg(src + e);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -482,12 +581,12 @@ __global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
     const int64_t ntiles = (a.n + BM - 1) / BM;
 
     if (warp < kProducerWarps) {
-        producer<CIN, COUT, NA, NB, Q8>(a, S, ntiles);
+        producer<CIN, COUT, NA, NB, KIND>(a, S, ntiles);
     } else if (warp == kProducerWarps) {
-        if ((threadIdx.x & 31) == 0) mma_issuer<CIN, COUT, NA, NB, Q8>(a, S, ntiles, tmem);
+        if ((threadIdx.x & 31) == 0) mma_issuer<CIN, COUT, NA, NB, KIND>(a, S, ntiles, tmem);
         __syncwarp();
     } else {
-        drainer<CIN, COUT, NA, NB, Q8>(a, S, ntiles, tmem);
+        drainer<CIN, COUT, NA, NB, KIND>(a, S, ntiles, tmem);
     }
 
     tc_fence_before();
@@ -498,10 +597,10 @@ __global__ void __maxnreg__(96) conv_tc_kernel(ConvArgs a) {
     }
 }
 
-template <int CIN, int COUT, int NA, int NB, bool Q8>
+template <int CIN, int COUT, int NA, int NB, int KIND>
 cudaError_t launch_t(const ConvArgs& a, cudaStream_t st) {
-    using C = Cfg<CIN, COUT, NA, NB, Q8>;
-    auto kern = conv_tc_kernel<CIN, COUT, NA, NB, Q8>;
+    using C = Cfg<CIN, COUT, NA, NB, KIND>;
+    auto kern = conv_tc_kernel<CIN, COUT, NA, NB, KIND>;
     static int num_sms[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -523,11 +622,16 @@ cudaError_t launch_t(const ConvArgs& a, cudaStream_t st) {
 
 template <int CIN, int COUT>
 cudaError_t launch_planes(const ConvArgs& a, cudaStream_t st) {
-    if (a.q8) return launch_t<CIN, COUT, 1, 2, true>(a, st);
-    if (a.na == 1 && a.wplanes == 1) return launch_t<CIN, COUT, 1, 1, false>(a, st);
-    if (a.na == 1 && a.wplanes == 2) return launch_t<CIN, COUT, 1, 2, false>(a, st);
-    if (a.na == 2 && a.wplanes == 1) return launch_t<CIN, COUT, 2, 1, false>(a, st);
-    if (a.na == 2 && a.wplanes == 2) return launch_t<CIN, COUT, 2, 2, false>(a, st);
+    if (a.q8) {
+        if constexpr (CIN == 128) {
+            if (a.i8) return launch_t<CIN, COUT, 1, 1, KIND_Q8I>(a, st);
+        }
+        return a.i8 ? cudaErrorInvalidValue : launch_t<CIN, COUT, 1, 2, KIND_Q8F>(a, st);
+    }
+    if (a.na == 1 && a.wplanes == 1) return launch_t<CIN, COUT, 1, 1, KIND_F>(a, st);
+    if (a.na == 1 && a.wplanes == 2) return launch_t<CIN, COUT, 1, 2, KIND_F>(a, st);
+    if (a.na == 2 && a.wplanes == 1) return launch_t<CIN, COUT, 2, 1, KIND_F>(a, st);
+    if (a.na == 2 && a.wplanes == 2) return launch_t<CIN, COUT, 2, 2, KIND_F>(a, st);
     return cudaErrorInvalidValue;
 }
 

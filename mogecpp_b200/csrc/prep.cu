@@ -2,18 +2,19 @@
 //
 //  * weights: packed [cout][ntaps*cin] (f32, f16 or ggml block_q8_0 rows) ->
 //    blob of 128B-swizzled K-major fp16 tiles [tap][64-ch chunk][plane][cout][64].
-//    f16 weights are one exact plane; f32 weights and Q8_0 weights (their
-//    exact dequantised value q * fp16(d)) become an exact hi/lo pair after a
-//    power-of-two prescale that puts max|w| near 2^14 (undone in the conv
-//    epilogue).
+//    f16 weights are one exact plane; f32 weights and Q8_0 weights with
+//    cin = 64 (their exact dequantised value q * fp16(d)) become an exact
+//    hi/lo pair after a power-of-two prescale that puts max|w| near 2^14
+//    (undone in the conv epilogue); Q8_0 weights with cin = 128 keep their
+//    int8 codes ([tap][cout][128] swizzled) plus fp32(fp16(d)) block scales.
 //  * activations: [n][c] rows (f32/f16/bf16), optional LayerNorm + SiLU
 //    (mogecpp src/sparse.cpp:520-526, ggml norm_f32 / silu), then
 //      ACT_FP16  round to fp16                      (ggml F16 vec_dot_type)
 //      ACT_SPLIT exact hi/lo fp16 pair of the fp32  (ggml F32 x F32)
 //      ACT_Q8    ggml's x86 Q8_0 quantiser per 32 channels (d = amax/127,
 //                id = 127/amax, round-half-even; ggml-cpu/arch/x86/quants.c:302):
-//                the int8 codes as one fp16 plane, fp32(fp16(d)) per block
-//                after it (Q8_0 vec_dot_type)
+//                the int8 codes as one fp16 plane (ACT_Q8I: as int8),
+//                fp32(fp16(d)) per block after it (Q8_0 vec_dot_type)
 #include "common.cuh"
 #include "conv.h"
 
@@ -94,6 +95,30 @@ __global__ void weight_split_kernel(WeightHeader* h, int wtype, const void* w, i
     if (blockIdx.x == 0 && threadIdx.x == 0) h->oscale = ldexpf(1.0f, -s);
 }
 
+// Q8_0 weights for the kind::i8 path: int8 codes into 128-byte swizzled rows
+// (one tile of cout rows per tap), block scales as fp32 [tap][block][cout].
+__global__ void weight_q8i_kernel(const BlockQ8* w, int cin, int cout, int ntaps, uint8_t* out) {
+    const int64_t nblocks = static_cast<int64_t>(cout) * ntaps * (cin / 32);
+    int8_t* codes = reinterpret_cast<int8_t*>(out);
+    float* scales = reinterpret_cast<float*>(out + static_cast<int64_t>(ntaps) * cout * cin);
+    for (int64_t bi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; bi < nblocks;
+         bi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t per_row = static_cast<int64_t>(ntaps) * (cin / 32);
+        const int o = static_cast<int>(bi / per_row);
+        const int64_t rb = bi % per_row;               // block within the packed row
+        const int t = static_cast<int>(rb / (cin / 32));
+        const int b = static_cast<int>(rb % (cin / 32));
+        const BlockQ8 blk = w[bi];
+        int8_t* tile = codes + static_cast<int64_t>(t) * cout * cin;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            const int ci = b * 32 + e;
+            tile[sw128_offset(o, ci >> 4) + (ci & 15)] = blk.qs[e];
+        }
+        scales[(static_cast<int64_t>(t) * (cin / 32) + b) * cout + o] = __half2float(blk.d);
+    }
+}
+
 // One warp per row; lane l holds channels [l*EPL, (l+1)*EPL).
 template <int C>
 __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
@@ -145,7 +170,7 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         for (int k = 0; k < EPL; ++k) planes[base + k] = __float2half_rn(v[k]);
         return;
     }
-    if (mode == ACT_Q8) {
+    if (mode == ACT_Q8 || mode == ACT_Q8I) {
         // 32-channel blocks span 32/EPL lanes
         float amax = 0.0f;
 #pragma unroll
@@ -153,10 +178,17 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         for (int o = 1; o < 32 / EPL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        if (mode == ACT_Q8I) {
+            int8_t* codes = reinterpret_cast<int8_t*>(planes);
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) planes[base + k] = __int2half_rn(__float2int_rn(__fmul_rn(v[k], id)));
+            for (int k = 0; k < EPL; ++k) codes[base + k] = static_cast<int8_t>(__float2int_rn(__fmul_rn(v[k], id)));
+        } else {
+#pragma unroll
+            for (int k = 0; k < EPL; ++k) planes[base + k] = __int2half_rn(__float2int_rn(__fmul_rn(v[k], id)));
+        }
         if ((lane * EPL) % 32 == 0) {
-            float* scales = reinterpret_cast<float*>(reinterpret_cast<char*>(planes) + scale_offset(n, C));
+            float* scales = reinterpret_cast<float*>(reinterpret_cast<char*>(planes) +
+                                                     scale_offset(n, mode == ACT_Q8I ? C / 2 : C));
             scales[row * (C / 32) + lane * EPL / 32] = __half2float(__float2half_rn(d));
         }
         return;
@@ -172,18 +204,30 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
 
 }  // namespace
 
-int weight_planes(int wtype) { return wtype == WT_F16 ? 1 : 2; }
+bool weight_is_i8(int wtype, int cin) { return wtype == WT_Q8_0 && cin == 128; }
+
+int weight_planes(int wtype, int cin) { return (wtype == WT_F16 || weight_is_i8(wtype, cin)) ? 1 : 2; }
 
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
-    return sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype)) * ntaps * cin * cout * 2;
+    if (weight_is_i8(wtype, cin))
+        return sizeof(WeightHeader) + static_cast<size_t>(ntaps) * cin * cout +
+               static_cast<size_t>(ntaps) * (cin / 32) * cout * 4;
+    return sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype, cin)) * ntaps * cin * cout * 2;
 }
 
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
                                   cudaStream_t st) {
     auto* h = static_cast<WeightHeader*>(blob);
-    const int planes = weight_planes(wtype);
+    const int planes = weight_planes(wtype, cin);
     const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
     weight_header_kernel<<<1, 1, 0, st>>>(h, wtype, cin, cout, ntaps, planes);
+    if (weight_is_i8(wtype, cin)) {
+        const int64_t nblocks = row_len / 32 * cout;
+        const unsigned grid = static_cast<unsigned>(std::min<int64_t>((nblocks + 255) / 256, 148 * 16));
+        weight_q8i_kernel<<<grid, 256, 0, st>>>(static_cast<const BlockQ8*>(w), cin, cout, ntaps,
+                                                static_cast<uint8_t*>(blob) + sizeof(WeightHeader));
+        return cudaGetLastError();
+    }
     if (planes == 2) weight_amax_kernel<<<148, 256, 0, st>>>(h, wtype, w, row_len, cout);
     const int64_t total = row_len * cout;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 16));
@@ -194,10 +238,11 @@ cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, i
 
 int act_planes(int mode) { return mode == ACT_SPLIT ? 2 : 1; }
 
-size_t act_scale_offset(int64_t n, int c) { return scale_offset(n, c); }
+size_t act_scale_offset(int mode, int64_t n, int c) { return scale_offset(n, mode == ACT_Q8I ? c / 2 : c); }
 
 size_t act_bytes(int mode, int64_t n, int c) {
-    if (mode == ACT_Q8) return scale_offset(n, c) + static_cast<size_t>(n) * (c / 32) * 4;
+    if (mode == ACT_Q8 || mode == ACT_Q8I)
+        return act_scale_offset(mode, n, c) + static_cast<size_t>(n) * (c / 32) * 4;
     return static_cast<size_t>(act_planes(mode)) * n * c * 2;
 }
 

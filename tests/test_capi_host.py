@@ -33,7 +33,8 @@ def test_abi_version():
 def test_size_queries_are_host_only():
     from mogecpp_b200 import lib as L
     lib = L.load()
-    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == 256 + 2 * 27 * 128 * 128 * 2
+    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == 256 + 27 * 128 * 128 + 27 * 4 * 128 * 4
+    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 64, 64, 27) == 256 + 2 * 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(L.MSC_W_F32, 64, 64, 27) == 256 + 2 * 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(L.MSC_W_F16, 64, 64, 27) == 256 + 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(99, 64, 64, 27) == 0
