@@ -98,6 +98,20 @@ size_t msc_topology_workspace_bytes(int64_t n);
 int msc_make_level(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr, void* ws, size_t ws_bytes,
                    void* stream);
 
+/* Neighbour map that allocates nothing, for callers that cannot allocate
+ * device memory (a host runtime whose device memory belongs to another
+ * allocator and offers no scratch, or latency-critical code that must not
+ * call cudaMalloc because it can synchronise the device).  Same result as
+ * msc_make_level; the hash table lives in a 16 MiB array compiled into the
+ * library (held by every GPU that loads it until the process exits), so
+ * n <= 524288 voxels; larger n fails with MSC_E_INVALID.  No context:
+ * device-side failure bits go to *status (a caller-owned device word, may be
+ * NULL).  The first call on a device looks up the array's device address
+ * with that device current; make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised.
+ * No counterpart in the reference. */
+int msc_make_level_noalloc(const int32_t* coords, int64_t n, int32_t* nbr, uint32_t* status, void* stream);
+
 /* Stride-2 transition: parent coords [np][4] (capacity n rows), np (device
  * int32), pool_rows (capacity 8*n, written [8][np]), inv_count, up_rows.
  * If np_host is non-NULL the call syncs and stores np there; device failures

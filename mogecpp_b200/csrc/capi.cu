@@ -195,6 +195,11 @@ void check_conv_shape(const msc_context::Blob& b, int cin, int ntaps) {
 
 }  // namespace
 
+namespace msc {
+// Records the calling thread's error message (for entry points in other files).
+void set_last_error(const std::string& msg) { g_err = msg; }
+}  // namespace msc
+
 extern "C" {
 
 int msc_abi_version(void) { return MSC_ABI_VERSION; }

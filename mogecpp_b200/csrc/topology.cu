@@ -323,6 +323,23 @@ cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, vo
     return cudaGetLastError();
 }
 
+size_t topology_table_bytes(int64_t n) { return table_capacity(n) * sizeof(Slot); }
+
+cudaError_t launch_make_level_in_table(const int32_t* coords, int64_t n, int32_t* nbr, void* table,
+                                       size_t table_bytes, uint32_t* status, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const uint64_t cap = table_capacity(n);
+    if (cap * sizeof(Slot) > table_bytes) return cudaErrorInvalidValue;
+    Slot* t = static_cast<Slot*>(table);
+    table_clear_kernel<<<static_cast<unsigned>((cap + 255) / 256), 256, 0, st>>>(t, cap);
+    const auto* c4 = reinterpret_cast<const int4*>(coords);
+    insert_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(c4, static_cast<int>(n), t, cap - 1,
+                                                                          status);
+    neighbor_kernel<<<static_cast<unsigned>((n + kMapVox - 1) / kMapVox), 27 * kMapVox, 0, st>>>(
+        c4, static_cast<int>(n), t, cap - 1, nbr);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
                               float* inv_count, int32_t* up_rows, void* ws, uint32_t* status, cudaStream_t st) {
     if (n == 0) {

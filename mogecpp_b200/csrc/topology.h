@@ -14,6 +14,12 @@ size_t topology_workspace_bytes(int64_t n);
 cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, void* ws, uint32_t* status,
                               cudaStream_t st);
 
+// Bytes of the hash table make_level uses for n voxels, and make_level with
+// that table supplied directly (table_bytes >= topology_table_bytes(n)).
+size_t topology_table_bytes(int64_t n);
+cudaError_t launch_make_level_in_table(const int32_t* coords, int64_t n, int32_t* nbr, void* table,
+                                       size_t table_bytes, uint32_t* status, cudaStream_t st);
+
 // parent: [n][4] capacity; np_dev: one device int32; pool_rows: [8][n]
 // capacity (written slot-major with stride np); inv_count, up_rows: [n].
 cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,

@@ -28,6 +28,7 @@ SIGNATURES = {
     "msc_check": (C.c_int, [_vp, _vp, C.POINTER(C.c_uint32)]),
     "msc_topology_workspace_bytes": (_sz, [_i64]),
     "msc_make_level": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "msc_make_level_noalloc": (C.c_int, [_vp, _i64, _vp, _vp, _vp]),
     "msc_downsample": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, C.POINTER(_i64), _vp, _sz, _vp]),
     "msc_weight_blob_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "msc_weight_prepare": (C.c_int, [_vp, _i32, _vp, _i32, _i32, _i32, _vp, _sz, _vp]),
