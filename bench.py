@@ -5,7 +5,9 @@ voxels on a 256^3 grid (364,846 active voxels), four residual blocks
 (LayerNorm -> SiLU -> submanifold conv 3x3x3 -> SiLU -> conv -> +skip) at
 C = 128 with fp16 state and ggml Q8_0 weights.  One step = rebuild the
 topology (hash + 27-tap neighbour map, as the refiner does on every refine
-pass) and run the four blocks (8 sparse convs).
+pass), build the level's conv plan (Morton subtiles with their distinct input
+rows) and run the four blocks (8 sparse convs) through the row-cached conv.
+``--conv direct`` runs the convs on the neighbour map instead (no plan).
 
     value = active voxels x sparse convs per step / step time   (device-resident inputs)
     e2e   = the same, through the C ABI with host buffers: the step's coordinates and
@@ -41,6 +43,7 @@ N_BLOCKS = 4
 CONVS_PER_STEP = 2 * N_BLOCKS
 METRIC = "active voxels/s per sparse conv"
 WORKLOAD = "res4_c128"
+PLAN_SORT_KERNELS = 8  # cub onesweep radix sort of 55-bit keys: histogram + 7 digit passes
 
 
 def load_peaks():
@@ -224,10 +227,13 @@ def run_ours(args):
                                                 C_CH, C_CH, 27)))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    cached = args.conv == "cached"
+
     def step():
         nbr = ex.make_level(coords_d)
+        plan = ex.conv_plan(coords_d, nbr) if cached else None
         for blk in blocks:
-            ex.res_block(x_d, nbr, blk)
+            ex.res_block(x_d, None if cached else nbr, blk, plan=plan)
         return nbr
 
     # warm-up (also validates device status once)
@@ -289,10 +295,14 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel (tensor-core sparse conv)
     peak_tf, peak_hbm, peak_src = load_peaks()
-    conv_launches, conv_ms = prof.get("conv_tc", (0, 0.0))
+    conv_family = "conv_cached" if cached else "conv_tc"
+    conv_launches, conv_ms = prof.get(conv_family, (0, 0.0))
     flops_per_launch = 2.0 * C_CH * C_CH * e_pairs
     achieved = flops_per_launch / (conv_ms / max(conv_launches, 1) * 1e-3) / 1e12 if conv_launches else None
-    kernels_per_family = {"make_level": 3, "conv_tc": 1, "act_prepare": 1}
+    # launches per profiled call: make_level = clear + insert + neighbour kernels;
+    # plan_build = header + Morton keys + the radix sort's kernels + subtiles
+    kernels_per_family = {"make_level": 3, "plan_build": 3 + PLAN_SORT_KERNELS, "conv_tc": 1, "conv_cached": 1,
+                          "act_prepare": 1}
     launches = sum(kernels_per_family.get(k, 1) * v[0] for k, v in prof.items())
 
     line = None
@@ -306,18 +316,20 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q8_0 x fp16 (exact fp16 hi/lo split on tcgen05, fp32 accumulate)",
+            "vs_baseline": None,
+            "dtype": "q8_0 (int8 codes exact on tcgen05, per-32-block fp32 scaling as ggml)",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "voxels": n, "valid_pairs": e_pairs, "channels": C_CH,
                        "blocks": N_BLOCKS, "convs_per_step": CONVS_PER_STEP, "grid": 256,
-                       "step": "make_level + 4 res blocks", "l2": "flushed between steps (256 MiB write)",
+                       "step": "make_level + conv plan + 4 res blocks" if cached else "make_level + 4 res blocks",
+                       "conv": args.conv, "l2": "flushed between steps (256 MiB write)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "e2e": {"value": world * n * CONVS_PER_STEP / (e2e_t * 1e-3), "unit": "voxels/s",
                     "h2d_bytes_per_step": int(coords.nbytes + x0.nbytes), "d2h_bytes_per_step": int(x0.nbytes),
                     "ms_per_step": e2e_t},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": (achieved / peak_tf) if achieved else None, "traffic": None,
-                         "kernel": "conv_tc (Q8_0, C=128)", "peak_source": peak_src,
+                         "kernel": f"{conv_family} (Q8_0, C=128)", "peak_source": peak_src,
                          "flops_per_launch": flops_per_launch,
                          "avg_launch_ms": conv_ms / max(conv_launches, 1)},
             "effective_tflops_per_conv": achieved,
@@ -339,6 +351,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--conv", default="cached", choices=["cached", "direct"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -66,6 +66,7 @@ extern "C" {
 #define MSC_DEV_DUP_COORD 0x8u
 #define MSC_DEV_POOL_OVERFLOW 0x10u
 #define MSC_DEV_BAD_INDEX 0x20u
+#define MSC_DEV_PLAN_OVERFLOW 0x40u
 
 typedef struct msc_context* msc_ctx_t;
 
@@ -149,6 +150,39 @@ size_t msc_op_workspace_bytes(int64_t n, int c);
 int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
                     const void* blob, const float* bias, void* y, int y_dtype, void* ws, size_t ws_bytes,
                     void* stream);
+
+/* ---------------------------------------------------------------- conv plan
+ * A conv plan is a per-level reordering of the voxels that lets the Q8_0
+ * sparse conv load every input row once per tile: voxels in Morton order of
+ * (x, y, z) within each sample, cut into subtiles of at most 128 rows that
+ * reference at most 384 distinct input rows each, with those rows' list and a
+ * 16-bit (row, tap) -> list position map.  Build it once per level, after
+ * msc_make_level, and pass it to every conv on that level.  No counterpart in
+ * the reference (its CPU gather walks the neighbour map directly,
+ * src/sparse.cpp:579-627); results match the unplanned calls within the
+ * features tolerance (the tap summation order differs). */
+
+/* Bytes of the plan buffer (256-byte aligned) and of the build workspace. */
+size_t msc_conv_plan_bytes(int64_t n);
+size_t msc_conv_plan_workspace_bytes(int64_t n);
+
+/* Builds the plan of a level from its coords and neighbour map.  Device
+ * failures (MSC_DEV_PLAN_OVERFLOW) are reported by msc_check. */
+int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, void* plan,
+                        size_t plan_bytes, void* ws, size_t ws_bytes, void* stream);
+
+/* msc_sparse_conv with an optional plan (NULL = msc_sparse_conv).  With a
+ * plan, Q8_0 weights and cin = 128 the row-cached conv runs and nbr may be
+ * NULL; other weights ignore the plan and use nbr. */
+int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                            const void* plan, const void* blob, const float* bias, void* y, int y_dtype, void* ws,
+                            size_t ws_bytes, void* stream);
+
+/* msc_res_block with an optional plan, same rules as msc_sparse_conv_planned. */
+int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr,
+                          const void* plan, const float* norm_w, const float* norm_b, const void* blob1,
+                          const float* b1, const void* blob2, const float* b2, void* ws, size_t ws_bytes,
+                          void* stream);
 
 /* y = W x + bias per row.  Replaces: linear (src/sparse.cpp:515-518). */
 int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const void* blob, const float* bias,

@@ -5,6 +5,7 @@
 // status and a thread-local message; nothing throws across the boundary.
 #include "conv.h"
 #include "ops.h"
+#include "plan.h"
 #include "topology.h"
 
 #include "../../include/moge_sparse_cuda.h"
@@ -28,6 +29,7 @@ struct msc_context {
     };
     std::mutex mu;
     std::unordered_map<const void*, Blob> blobs;
+    std::unordered_map<const void*, int64_t> plans;  // conv plan -> voxel count
     // kernel profiling (msc_profile_*): one event pair per launch
     struct Rec {
         const char* name;
@@ -134,8 +136,10 @@ msc_context::Blob blob_info(msc_ctx_t ctx, const void* blob) {
     return it->second;
 }
 
-int act_mode(int wtype, int x_dtype, int cin) {
-    if (wtype == MSC_W_Q8_0) return msc::weight_is_i8(wtype, cin) ? msc::ACT_Q8I : msc::ACT_Q8;
+// Operand preparation mode for a weight type; `planned` selects the row-cached
+// Q8_0 conv, which gathers int8 codes for every cin.
+int act_mode(int wtype, int x_dtype, int cin, bool planned = false) {
+    if (wtype == MSC_W_Q8_0) return (planned || msc::weight_is_i8(wtype, cin)) ? msc::ACT_Q8I : msc::ACT_Q8;
     if (wtype == MSC_W_F16) return msc::ACT_FP16;
     return x_dtype == MSC_F16 ? msc::ACT_FP16 : msc::ACT_SPLIT;
 }
@@ -155,7 +159,7 @@ void need_ws(size_t have, size_t want) {
 
 void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
               const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
-              int res_dtype, void* y, int y_dtype, cudaStream_t st) {
+              int res_dtype, void* y, int y_dtype, cudaStream_t st, const void* plan = nullptr) {
     msc::ConvArgs a{};
     a.planes = planes;
     a.q8 = mode == msc::ACT_Q8 || mode == msc::ACT_Q8I;
@@ -181,8 +185,32 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
     a.y = y;
     a.y_dtype = y_dtype;
     a.status = ctx->status;
+    if (plan) {
+        a.blob = static_cast<const char*>(blob) + msc::weight_cached_offset(b.wtype, b.cin, b.cout, b.ntaps);
+        a.nbr = nullptr;
+        ProfScope ps(ctx, "conv_cached", st);
+        cuda_ok(msc::launch_conv_cached(a, plan, st), "cached conv launch");
+        return;
+    }
     ProfScope ps(ctx, nbr ? "conv_tc" : "linear_tc", st);
     cuda_ok(msc::launch_conv(a, st), "conv launch");
+}
+
+// The plan, when given, must come from msc_conv_plan_build on this context
+// for n voxels; it is used by the row-cached conv (Q8_0 conv weights, cin =
+// 128), and null is returned for every other weight.
+const void* use_plan(msc_ctx_t ctx, const void* plan, int64_t n, const msc_context::Blob& b) {
+    if (!plan) return nullptr;
+    int64_t pn = -1;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        auto it = ctx->plans.find(plan);
+        if (it == ctx->plans.end()) fail(MSC_E_INVALID, "conv plan was not built by this context");
+        pn = it->second;
+    }
+    if (pn != n) fail(MSC_E_INVALID, "conv plan covers " + std::to_string(pn) + " voxels, not " + std::to_string(n));
+    return msc::weight_has_cached(b.wtype, b.cin, b.ntaps) && msc::conv_cached_supported(b.cin, b.cout) ? plan
+                                                                                                      : nullptr;
 }
 
 void check_conv_shape(const msc_context::Blob& b, int cin, int ntaps) {
@@ -257,6 +285,7 @@ int msc_check(msc_ctx_t ctx, void* stream, uint32_t* bits) {
             if (h & MSC_DEV_BAD_COORD) m += " coordinate-out-of-range";
             if (h & MSC_DEV_POOL_OVERFLOW) m += " pool-slot-overflow";
             if (h & MSC_DEV_BAD_INDEX) m += " index-out-of-range";
+            if (h & MSC_DEV_PLAN_OVERFLOW) m += " plan-overflow";
             fail(MSC_E_DEVICE, m);
         }
     });
@@ -348,9 +377,36 @@ size_t msc_op_workspace_bytes(int64_t n, int c) {
     return align256(static_cast<size_t>(n) * c * 4) + align256(static_cast<size_t>(n) * c * 4) + 256;
 }
 
-int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
-                    const void* blob, const float* bias, void* y, int y_dtype, void* ws, size_t ws_bytes,
-                    void* stream) {
+size_t msc_conv_plan_bytes(int64_t n) { return n < 0 ? 0 : msc::plan_bytes(n); }
+
+size_t msc_conv_plan_workspace_bytes(int64_t n) { return n < 0 ? 0 : msc::plan_workspace_bytes(n); }
+
+int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, void* plan,
+                        size_t plan_bytes, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        need(plan != nullptr, "null plan pointer");
+        need_aligned(plan, 256, "plan");
+        need_ws(plan_bytes, msc::plan_bytes(n));
+        if (n > 0) {
+            need(coords && nbr && ws, "null pointer");
+            need_aligned(coords, 16, "coords");
+            need_aligned(ws, 256, "workspace");
+            need_ws(ws_bytes, msc::plan_workspace_bytes(n));
+        }
+        {
+            ProfScope ps(ctx, "plan_build", S(stream));
+            cuda_ok(msc::launch_plan_build(coords, nbr, n, plan, ws, ctx->status, S(stream)), "plan build launch");
+        }
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        ctx->plans[plan] = n;
+    });
+}
+
+int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                            const void* plan, const void* blob, const float* bias, void* y, int y_dtype, void* ws,
+                            size_t ws_bytes, void* stream) {
     return guard([&] {
         need_ctx(ctx);
         need_dtype(x_dtype, "x");
@@ -359,16 +415,24 @@ int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int ci
         check_conv_shape(b, cin, 27);
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0) return;
-        need(x && nbr && y && ws, "null pointer");
+        const void* pl = use_plan(ctx, plan, n, b);
+        need(x && (nbr || pl) && y && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
-        const int mode = act_mode(b.wtype, x_dtype, b.cin);
+        const int mode = act_mode(b.wtype, x_dtype, b.cin, pl != nullptr);
         need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
-        run_conv(ctx, ws, mode, n, cin, nbr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream));
+        run_conv(ctx, ws, mode, n, cin, nbr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream), pl);
     });
+}
+
+int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                    const void* blob, const float* bias, void* y, int y_dtype, void* ws, size_t ws_bytes,
+                    void* stream) {
+    return msc_sparse_conv_planned(ctx, x, x_dtype, n, cin, nbr, nullptr, blob, bias, y, y_dtype, ws, ws_bytes,
+                                   stream);
 }
 
 int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const void* blob, const float* bias,
@@ -396,6 +460,14 @@ int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, co
 int msc_res_block(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr, const float* norm_w,
                   const float* norm_b, const void* blob1, const float* b1, const void* blob2, const float* b2,
                   void* ws, size_t ws_bytes, void* stream) {
+    return msc_res_block_planned(ctx, x, x_dtype, n, c, nbr, nullptr, norm_w, norm_b, blob1, b1, blob2, b2, ws,
+                                 ws_bytes, stream);
+}
+
+int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr,
+                          const void* plan, const float* norm_w, const float* norm_b, const void* blob1,
+                          const float* b1, const void* blob2, const float* b2, void* ws, size_t ws_bytes,
+                          void* stream) {
     return guard([&] {
         need_ctx(ctx);
         need_dtype(x_dtype, "x");
@@ -406,21 +478,23 @@ int msc_res_block(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const i
         need(w1.cout == c && w2.cout == c, "res_block convs must map c -> c");
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0) return;
-        need(x && nbr && ws, "null pointer");
+        const void* p1 = use_plan(ctx, plan, n, w1);
+        const void* p2 = use_plan(ctx, plan, n, w2);
+        need(x && ((p1 && p2) || nbr) && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(ws, 256, "workspace");
         const size_t planes_bytes = align256(static_cast<size_t>(n) * c * 4);
         need_ws(ws_bytes, planes_bytes + static_cast<size_t>(n) * c * 4);
         void* planes = ws;
         float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
-        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin);
+        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1 != nullptr);
         cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
                 "norm1 prepare");
-        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream));
-        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin);
+        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1);
+        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2 != nullptr);
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
-        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream));
+        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);
     });
 }
 

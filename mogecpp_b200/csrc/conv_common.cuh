@@ -1,0 +1,110 @@
+// Device helpers shared by the tensor-core conv kernels (conv_tc.cu,
+// conv_cached.cu): bounded waits, tap-order rotation, packed f32x2
+// arithmetic and row stores.
+#pragma once
+
+#include "common.cuh"
+#include "conv.h"
+
+namespace msc {
+
+// Bounded wait that also gives up once another role has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* abort_flag, uint32_t* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 31u) == 31u) {
+            if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+            if (global_timer_ns() - t0 > kWaitBudgetNs) {
+                atomicExch(abort_flag, 1);
+                set_status(status, MSC_DEV_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// One arrival per warp on a barrier that counts warps.  Arrivals from every
+// lane of a CTA on one mbarrier serialise in shared memory (hundreds of
+// cycles per phase at 512 threads); the warp sync orders the lanes' prior
+// writes before the elected lane's arrive.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+    const unsigned m = __activemask();
+    __syncwarp(m);
+    if (static_cast<int>(threadIdx.x & 31) == __ffs(m) - 1) mbar_arrive(bar);
+}
+
+// Taps are visited in a per-tile rotated order so that the CTAs, which all
+// stream the same small weight tensor, do not request the same weight tile
+// from L2 at the same moment.  rot_mask() rotates the tap mask so that bit 0
+// is tap `r`; rot_tap() maps a rotated bit back to the tap.
+__device__ __forceinline__ int tap_rotation(int64_t tile, int ntaps) {
+    return ntaps == 27 ? static_cast<int>(tile % 27) : 0;
+}
+__device__ __forceinline__ uint32_t rot_mask(uint32_t m, int r) {
+    return r ? ((m >> r) | (m << (27 - r))) & 0x7ffffffu : m;
+}
+__device__ __forceinline__ int rot_tap(int bit, int r) {
+    const int t = bit + r;
+    return t >= 27 ? t - 27 : t;
+}
+
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+__device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t idx) {
+    if (dtype == DT_F32) return static_cast<const float*>(p)[idx];
+    if (dtype == DT_F16) return __half2float(static_cast<const __half*>(p)[idx]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
+}
+
+template <int N>
+__device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const float (&v)[N]) {
+    if (dtype == DT_F32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(y) + off);
+#pragma unroll
+        for (int k = 0; k < N / 4; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    } else if (dtype == DT_F16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(y) + off);
+#pragma unroll
+        for (int k = 0; k < N / 8; ++k) {
+            __half2 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
+            dst[k] = *reinterpret_cast<uint4*>(h);
+        }
+    } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + off);
+#pragma unroll
+        for (int k = 0; k < N / 8; ++k) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
+            dst[k] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+}
+
+}  // namespace msc

@@ -43,6 +43,7 @@
 // and the CTA unwinds.
 #include "common.cuh"
 #include "conv.h"
+#include "conv_common.cuh"
 
 namespace msc {
 namespace {
@@ -109,43 +110,11 @@ struct Smem {
     int* abort;
 };
 
-// Bounded wait that also gives up once another role has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* abort_flag, uint32_t* status) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 31u) == 31u) {
-            if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
-            if (global_timer_ns() - t0 > kWaitBudgetNs) {
-                atomicExch(abort_flag, 1);
-                set_status(status, MSC_DEV_TIMEOUT);
-                return false;
-            }
-        }
-    }
-}
-
 __device__ __forceinline__ uint32_t tile_mask(const Smem& S, int buf) {
     uint32_t m = 0;
 #pragma unroll
     for (int w = 0; w < kProducerWarps; ++w) m |= S.wmask[buf * kProducerWarps + w];
     return m;
-}
-
-// Taps are visited in a per-tile rotated order so that the CTAs, which all
-// stream the same small weight tensor, do not request the same weight tile
-// from L2 at the same moment.  rot_mask() rotates the tap mask so that bit 0
-// is tap `r`; rot_tap() maps a rotated bit back to the tap.
-__device__ __forceinline__ int tap_rotation(int64_t tile, int ntaps) {
-    return ntaps == 27 ? static_cast<int>(tile % 27) : 0;
-}
-__device__ __forceinline__ uint32_t rot_mask(uint32_t m, int r) {
-    return r ? ((m >> r) | (m << (27 - r))) & 0x7ffffffu : m;
-}
-__device__ __forceinline__ int rot_tap(int bit, int r) {
-    const int t = bit + r;
-    return t >= 27 ? t - 27 : t;
 }
 
 __device__ __forceinline__ int64_t tile_row(const ConvArgs& a, int64_t idx) {
@@ -154,23 +123,6 @@ __device__ __forceinline__ int64_t tile_row(const ConvArgs& a, int64_t idx) {
 }
 
 // D[tmem] (+)= A * B^T, kind::i8 (signed int8 operands, int32 accumulator).
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// Instruction descriptor for kind::i8: signed int8 A and B (format 1), int32
-// accumulator (format 2), both K-major, shape M x N.
-__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-           (static_cast<uint32_t>(m >> 4) << 24);
-}
-
 // ------------------------------------------------------------------ roles
 
 template <int CIN, int COUT, int NA, int NB, int KIND>
@@ -198,7 +150,7 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
             // still need those stages of an earlier tile
             cp_async_wait_all();
             fence_proxy_async();
-            for (; arrived < i; ++arrived) mbar_arrive(&S.full[arrived % C::STAGES]);
+            for (; arrived < i; ++arrived) warp_arrive(&S.full[arrived % C::STAGES]);
             if (!wait_or_abort(&S.tile_free[buf], ((k >> 1) - 1) & 1, S.abort, a.status)) {
                 ok = false;
                 break;
@@ -234,7 +186,7 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
         m = __reduce_or_sync(0xffffffffu, m);
         if (lane == 0) S.wmask[buf * kProducerWarps + warp] = m;
         asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
-        mbar_arrive(&S.tile_ready[buf]);
+        warp_arrive(&S.tile_ready[buf]);
         const int rot = tap_rotation(tile, a.ntaps);
         uint32_t rem = rot_mask(tile_mask(S, buf), rot);
         const int nst = __popc(rem) * C::KCH;
@@ -278,7 +230,7 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
             if (i + 1 - arrived > LAG) {
                 cp_async_wait<LAG>();
                 fence_proxy_async();
-                mbar_arrive(&S.full[arrived % C::STAGES]);
+                warp_arrive(&S.full[arrived % C::STAGES]);
                 ++arrived;
             }
             ++kc;
@@ -287,7 +239,7 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
     cp_async_wait_all();
     if (ok) {
         fence_proxy_async();
-        for (; arrived < i; ++arrived) mbar_arrive(&S.full[arrived % C::STAGES]);
+        for (; arrived < i; ++arrived) warp_arrive(&S.full[arrived % C::STAGES]);
     }
 }
 
@@ -332,58 +284,6 @@ __device__ void mma_issuer(const ConvArgs& a, const Smem& S, int64_t ntiles, uin
                 umma_commit(&S.acc_full[slot]);
             }
             umma_commit(&S.empty[s]);
-        }
-    }
-}
-
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-
-__device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t idx) {
-    if (dtype == DT_F32) return static_cast<const float*>(p)[idx];
-    if (dtype == DT_F16) return __half2float(static_cast<const __half*>(p)[idx]);
-    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
-}
-
-template <int N>
-__device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const float (&v)[N]) {
-    if (dtype == DT_F32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(y) + off);
-#pragma unroll
-        for (int k = 0; k < N / 4; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-    } else if (dtype == DT_F16) {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(y) + off);
-#pragma unroll
-        for (int k = 0; k < N / 8; ++k) {
-            __half2 h[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
-            dst[k] = *reinterpret_cast<uint4*>(h);
-        }
-    } else {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + off);
-#pragma unroll
-        for (int k = 0; k < N / 8; ++k) {
-            __nv_bfloat162 h[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
-            dst[k] = *reinterpret_cast<uint4*>(h);
         }
     }
 }
@@ -460,7 +360,7 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                     tmem_wait_ld();
                     if (c + CH == COLS) {
                         tc_fence_before();
-                        mbar_arrive(&S.acc_empty[slot]);
+                        warp_arrive(&S.acc_empty[slot]);
                     }
                     if (KIND == KIND_Q8I) {
                         // acc += (d_a * d_w[n]) * isum[n]: (isum * d_a) is rounded once
@@ -514,7 +414,7 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                 store_row<EC>(a.y, a.y_dtype, static_cast<int64_t>(row) * COUT + c_base + c0, v);
             }
         }
-        mbar_arrive(&S.tile_free[buf]);
+        warp_arrive(&S.tile_free[buf]);
     }
 }
 
@@ -548,16 +448,16 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&S.full[s], kProducers + 1);
+            mbar_init(&S.full[s], kProducerWarps + 1);
             mbar_init(&S.empty[s], 1);
         }
         for (int s = 0; s < C::NACC; ++s) {
             mbar_init(&S.acc_full[s], 1);
-            mbar_init(&S.acc_empty[s], kDrainers);
+            mbar_init(&S.acc_empty[s], kDrainWarps);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&S.tile_ready[b], kProducers);
-            mbar_init(&S.tile_free[b], kDrainers);
+            mbar_init(&S.tile_ready[b], kProducerWarps);
+            mbar_init(&S.tile_free[b], kDrainWarps);
         }
         *S.abort = 0;
         fence_mbar_init();

@@ -34,6 +34,13 @@ SIGNATURES = {
     "msc_weight_prepare": (C.c_int, [_vp, _i32, _vp, _i32, _i32, _i32, _vp, _sz, _vp]),
     "msc_op_workspace_bytes": (_sz, [_i64, _i32]),
     "msc_sparse_conv": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
+    "msc_conv_plan_bytes": (_sz, [_i64]),
+    "msc_conv_plan_workspace_bytes": (_sz, [_i64]),
+    "msc_conv_plan_build": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp, _sz, _vp]),
+    "msc_sparse_conv_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz,
+                                          _vp]),
+    "msc_res_block_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                        _sz, _vp]),
     "msc_linear": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
     "msc_res_block": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "msc_pool_down": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),

@@ -7,6 +7,7 @@ refiner's operators with the reference's names and argument meaning
 (src/sparse.cpp):
 
     make_level(coords)                    -> nbr [n, 27]          (:238-272)
+    conv_plan(coords, nbr)                -> plan (no counterpart: row-cached Q8_0 conv)
     downsample(coords)                    -> Transition           (:312-357)
     sparse_conv(x, nbr, w, bias)          -> y [n, cout]          (:579-627)
     res_block(x, nbr, block)              -> x (in place)         (:629-642)
@@ -141,6 +142,18 @@ class SparseCudaExecutor:
         m = np_host.value
         return Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n)
 
+    def conv_plan(self, coords: torch.Tensor, nbr: torch.Tensor) -> torch.Tensor:
+        """Conv plan of a level (``msc_conv_plan_build``): pass it to sparse_conv /
+        res_block on the same level to run the row-cached Q8_0 conv."""
+        n = coords.shape[0]
+        pb = self.lib.msc_conv_plan_bytes(n)
+        plan = torch.empty(pb, dtype=torch.uint8, device=coords.device)
+        wsb = self.lib.msc_conv_plan_workspace_bytes(n)
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_conv_plan_build(self.ctx, _p(coords), n, _p(nbr), _p(plan), pb, _p(ws), wsb,
+                                             _stream()))
+        return plan
+
     # ---------------------------------------------------------- weights
     def prepare_weight(self, w: torch.Tensor, wtype: str, cin: int, cout: int, ntaps: int) -> PreparedWeight:
         """w: packed [cout, ntaps*cin] float32 / float16, or uint8 block_q8_0 rows."""
@@ -151,13 +164,14 @@ class SparseCudaExecutor:
         return PreparedWeight(blob, wtype, cin, cout, ntaps)
 
     # ---------------------------------------------------------- operators
-    def sparse_conv(self, x, nbr, w: PreparedWeight, bias=None, out_dtype=torch.float32):
+    def sparse_conv(self, x, nbr, w: PreparedWeight, bias=None, out_dtype=torch.float32, plan=None):
         n, cin = x.shape
         y = torch.empty((n, w.cout), dtype=out_dtype, device=x.device)
         wsb = self.lib.msc_op_workspace_bytes(n, max(cin, w.cout))
         ws = self.workspace(wsb)
-        L.check(self.lib.msc_sparse_conv(self.ctx, _p(x), _DT[x.dtype], n, cin, _p(nbr), _p(w.blob), _p(bias), _p(y),
-                                         _DT[out_dtype], _p(ws), wsb, _stream()))
+        L.check(self.lib.msc_sparse_conv_planned(self.ctx, _p(x), _DT[x.dtype], n, cin, _p(nbr), _p(plan),
+                                                 _p(w.blob), _p(bias), _p(y), _DT[out_dtype], _p(ws), wsb,
+                                                 _stream()))
         return y
 
     def linear(self, x, w: PreparedWeight, bias=None, out_dtype=torch.float32):
@@ -169,14 +183,15 @@ class SparseCudaExecutor:
                                     _DT[out_dtype], _p(ws), wsb, _stream()))
         return y
 
-    def res_block(self, x, nbr, blk: dict):
+    def res_block(self, x, nbr, blk: dict, plan=None):
         """In place on x.  blk: norm_w, norm_b, w1 (PreparedWeight), b1, w2, b2."""
         n, c = x.shape
         wsb = self.lib.msc_op_workspace_bytes(n, c)
         ws = self.workspace(wsb)
-        L.check(self.lib.msc_res_block(self.ctx, _p(x), _DT[x.dtype], n, c, _p(nbr), _p(blk.get("norm_w")),
-                                       _p(blk.get("norm_b")), _p(blk["w1"].blob), _p(blk.get("b1")),
-                                       _p(blk["w2"].blob), _p(blk.get("b2")), _p(ws), wsb, _stream()))
+        L.check(self.lib.msc_res_block_planned(self.ctx, _p(x), _DT[x.dtype], n, c, _p(nbr), _p(plan),
+                                               _p(blk.get("norm_w")), _p(blk.get("norm_b")), _p(blk["w1"].blob),
+                                               _p(blk.get("b1")), _p(blk["w2"].blob), _p(blk.get("b2")), _p(ws),
+                                               wsb, _stream()))
         return x
 
     def pool_down(self, x, tr: Transition, w: PreparedWeight, bias=None, out_dtype=torch.float32):

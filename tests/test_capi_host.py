@@ -33,13 +33,25 @@ def test_abi_version():
 def test_size_queries_are_host_only():
     from mogecpp_b200 import lib as L
     lib = L.load()
-    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == 256 + 27 * 128 * 128 + 27 * 4 * 128 * 4
+    # Q8_0 with cin 128: int8 tiles + block scales, then at a 256-byte
+    # boundary the row-cached conv's per-tap records (codes, then scales);
+    # Q8_0 with cin 64: an exact fp16 hi/lo pair, no row-cached section
+    def r256(v):
+        return (v + 255) // 256 * 256
+    cached128 = 27 * (128 * 128 + 4 * 128 * 4)
+    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == \
+        r256(256 + 27 * 128 * 128 + 27 * 4 * 128 * 4) + cached128
+    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 64, 1) == 256 + 128 * 64 + 4 * 64 * 4
     assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 64, 64, 27) == 256 + 2 * 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(L.MSC_W_F32, 64, 64, 27) == 256 + 2 * 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(L.MSC_W_F16, 64, 64, 27) == 256 + 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(99, 64, 64, 27) == 0
     assert lib.msc_topology_workspace_bytes(1000) > 2048 * 16
     assert lib.msc_op_workspace_bytes(1000, 128) >= 1000 * 128 * 8
+    # conv plan: header + perm + descriptors + (row, tap) slots + U-list pool
+    assert lib.msc_conv_plan_bytes(1000) >= 1000 * 4 + 1000 * 27 * 2 + 4 * 1000 * 4
+    assert lib.msc_conv_plan_bytes(-1) == 0
+    assert lib.msc_conv_plan_workspace_bytes(1000) >= 1000 * 20
 
 
 def test_create_fails_cleanly_without_sm100():
