@@ -1,26 +1,36 @@
 """Benchmark of the sparse-voxel hot path on B200 (one JSON line on rank 0).
 
-Workload ``res4_c128`` (the residual-stack configuration): seeded sine-surface
-voxels on a 256^3 grid (364,846 active voxels), four residual blocks
-(LayerNorm -> SiLU -> submanifold conv 3x3x3 -> SiLU -> conv -> +skip) at
-C = 128 with fp16 state and ggml Q8_0 weights.  One step = rebuild the
-topology (hash + 27-tap neighbour map, as the refiner does on every refine
-pass), build the level's conv plan (Morton subtiles with their distinct input
-rows) and run the four blocks (8 sparse convs) through the row-cached conv.
-``--conv direct`` runs the convs on the neighbour map instead (no plan).
+Workloads (seeded synthetic surfaces, mogecpp_b200/synth.py; C = 128, fp16
+state, ggml Q8_0 weights, LayerNorm -> SiLU -> submanifold conv 3x3x3 ->
+SiLU -> conv -> +skip per residual block):
+
+* ``shell_4m`` (default) - 3,145,728 voxels, a 3-voxel-thick height shell on
+  a 1024^3 grid, 8 residual blocks: the large sharded configuration, run on
+  1/2/4/8 GPUs.
+* ``res4_c128`` - 364,846 voxels on a 256^3 grid, 4 residual blocks.
+
+One step = rebuild the topology (hash + 27-tap neighbour map, as the refiner
+does on every refine pass) and run the residual stack (2 sparse convs per
+block).  The convs gather through the neighbour map; ``--conv ordered``
+(default) also builds the level's tap-order plan (voxels sorted by their
+27-tap neighbourhood mask, so that each 128-row tile runs over fewer taps),
+``--conv direct`` runs the tiles in (b, z, y, x) order, and ``--conv
+cached`` builds the row-cache plan and runs the row-cached conv.
 
     value = active voxels x sparse convs per step / step time   (device-resident inputs)
     e2e   = the same, through the C ABI with host buffers: the step's coordinates and
             features are copied from pinned host memory and the result copied back
             inside the timed region.
 
+Multi-GPU (torchrun, one process per GPU): the voxels are split into z-slabs
+at voxel-count quantiles (mogecpp_b200/slab.py); each rank builds the
+topology of its slab plus a two-plane halo per side and, before every block,
+exchanges the boundary planes with its z-neighbours over NCCL.  Total work
+is fixed ("scaling": "strong"); timing is the max over ranks.
+
 ``--impl reference`` times the reference's own CPU implementation (mogecpp
 src/sparse.cpp + ggml CPU backend, compiled from the reference sources into
 oracle/_ref/) on a bounded voxel sample of the same workload.
-
-Multi-GPU (torchrun): each rank runs the workload on its own GPU (independent
-replicas; per-GPU work is fixed, "scaling": "weak"); timing is the max over
-ranks.
 """
 
 from __future__ import annotations
@@ -39,10 +49,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 C_CH = 128
-N_BLOCKS = 4
-CONVS_PER_STEP = 2 * N_BLOCKS
 METRIC = "active voxels/s per sparse conv"
-WORKLOAD = "res4_c128"
+WORKLOADS = {
+    "shell_4m": dict(blocks=8, coords="shell_4m_coords", grid=1024),
+    "res4_c128": dict(blocks=4, coords="res4_c128_coords", grid=256),
+}
 PLAN_SORT_KERNELS = 8  # cub onesweep radix sort of 55-bit keys: histogram + 7 digit passes
 
 
@@ -55,13 +66,16 @@ def load_peaks():
         return 1590.0, 6650.0, "fallback"
 
 
-def workload_inputs():
+def workload_inputs(name: str, rows=None):
+    """Coordinates (all voxels), the fp16 features of `rows` (default: all)
+    and the residual blocks' parameters."""
     from mogecpp_b200 import synth
-    coords = synth.res4_c128_coords()
+    w = WORKLOADS[name]
+    coords = getattr(synth, w["coords"])()
     n = coords.shape[0]
-    x0 = synth.features(2, n, C_CH).astype(np.float16)
+    x0 = synth.features_rows(2, np.arange(n) if rows is None else rows, C_CH, np.float16)
     blocks = []
-    for b in range(N_BLOCKS):
+    for b in range(w["blocks"]):
         rng = np.random.default_rng(1000 + b)
         blocks.append(dict(norm_w=(1 + 0.1 * rng.standard_normal(C_CH)).astype(np.float32),
                            norm_b=(0.1 * rng.standard_normal(C_CH)).astype(np.float32),
@@ -158,7 +172,12 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    coords, x0, blocks = workload_inputs()
+    from mogecpp_b200 import synth
+    coords = getattr(synth, WORKLOADS[args.workload]["coords"])()
+    # the sample is the first voxels: draw only those features
+    _, x0, blocks = workload_inputs(args.workload, np.arange(min(coords.shape[0], 1 << 18)))
+    coords = coords[:x0.shape[0]]
+    convs = 2 * len(blocks)
     threads = os.cpu_count() or 1
     from oracle.oracle import W_Q8_0
     per_step = min(8.0, 150.0 / max(1, args.steps + args.warmup))
@@ -185,12 +204,13 @@ def run_reference(args):
             if i >= args.warmup:
                 times.append(time.perf_counter() - t0)
     t = sum(times) / len(times)
-    value = ns * CONVS_PER_STEP / t
-    sample = f"first {ns} of {coords.shape[0]} voxels in (b,z,y,x) order (a z-slab), 4 res blocks, Q8_0"
+    value = ns * convs / t
+    sample = (f"first {ns} voxels of {args.workload} in (b,z,y,x) order (a z-slab), {len(blocks)} res blocks, "
+              "Q8_0")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 x fp32 (ggml CPU)", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "voxels": int(ns), "channels": C_CH, "blocks": N_BLOCKS},
+            "scaling": "strong", "vs_baseline": None, "dtype": "q8_0 x fp32 (ggml CPU)", "data": "synthetic",
+            "config": {"workload": args.workload, "voxels": int(ns), "channels": C_CH, "blocks": len(blocks)},
             "cpu_baseline": {"value": value, "unit": "voxels/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -206,17 +226,25 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
-    from mogecpp_b200 import synth
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from mogecpp_b200 import slab, synth
     from mogecpp_b200.sparse import SparseCudaExecutor
 
     ex = SparseCudaExecutor(local)
-    coords, x0, blocks_np = workload_inputs()
+    coords = getattr(synth, WORKLOADS[args.workload]["coords"])()
+    part = slab.partition(coords, world)[rank]
+    rows = part.local_rows()
+    # this rank's rows only (and rank 0's CPU sample, the first voxels)
+    _, lx0, blocks_np = workload_inputs(args.workload, rows)
     n = coords.shape[0]
+    convs = 2 * len(blocks_np)
+    lcoords = np.ascontiguousarray(coords[rows])
+    nl = lcoords.shape[0]
     dev = torch.device("cuda", local)
-    coords_d = torch.from_numpy(coords).to(dev)
-    x0_d = torch.from_numpy(x0).to(dev)
+    coords_d = torch.from_numpy(lcoords).to(dev)
+    x0_d = torch.from_numpy(lx0).to(dev)
     x_d = torch.empty_like(x0_d)
+    halo = slab.SlabExchange(part, world)
     blocks = []
     for b in blocks_np:
         blocks.append(dict(norm_w=torch.from_numpy(b["norm_w"]).to(dev), norm_b=torch.from_numpy(b["norm_b"]).to(dev),
@@ -226,33 +254,40 @@ def run_ours(args):
                            w2=ex.prepare_weight(torch.from_numpy(synth.quantize_q8_0(b["w2"])).to(dev), "q8_0",
                                                 C_CH, C_CH, 27)))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-
     cached = args.conv == "cached"
+    plan_kind = {"cached": "row_cache", "ordered": "tap_order"}.get(args.conv)
 
     def step():
         nbr = ex.make_level(coords_d)
-        plan = ex.conv_plan(coords_d, nbr) if cached else None
+        plan = ex.conv_plan(coords_d, nbr, plan_kind) if plan_kind else None
         for blk in blocks:
+            halo.exchange(x_d)
             ex.res_block(x_d, None if cached else nbr, blk, plan=plan)
         return nbr
 
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    barrier()
     # warm-up (also validates device status once)
     for _ in range(args.warmup):
         x_d.copy_(x0_d)
         nbr = step()
     ex.check()
-    e_pairs = int((nbr < n).sum().item())
+    e_pairs = int((nbr < nl).sum().item())
+    barrier()
 
     # ---- device-resident timed region
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
     torch.cuda.synchronize()
+    barrier()
     ex.profile(True)
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             x_d.copy_(x0_d)
             flush.fill_(i & 0xff)  # L2 flush between steps (outside the events)
+            barrier()
             ev[i][0].record()
             step()
             ev[i][1].record()
@@ -266,22 +301,24 @@ def run_ours(args):
         t = torch.tensor([t_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         t_ms = float(t.item())
-        dist.barrier()
-    value = world * n * CONVS_PER_STEP / (t_ms * 1e-3)
+        barrier()
+    value = n * convs / (t_ms * 1e-3)
 
     # ---- end to end through the C ABI with host buffers
-    h_coords = torch.from_numpy(coords).pin_memory()
-    h_x = torch.from_numpy(x0).pin_memory()
-    h_out = torch.empty_like(h_x).pin_memory()
+    h_coords = torch.from_numpy(lcoords).pin_memory()
+    h_x = torch.from_numpy(lx0).pin_memory()
+    h_out = torch.empty((part.n_owned, C_CH), dtype=x0_d.dtype).pin_memory()
     e2e_ms = []
     for i in range(args.warmup + args.steps):
         flush.fill_(i & 0xff)
+        torch.cuda.synchronize()
+        barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         coords_d.copy_(h_coords, non_blocking=True)
         x_d.copy_(h_x, non_blocking=True)
         step()
-        h_out.copy_(x_d, non_blocking=True)
+        h_out.copy_(x_d[:part.n_owned], non_blocking=True)
         b.record()
         b.synchronize()
         if i >= args.warmup:
@@ -301,32 +338,35 @@ def run_ours(args):
     achieved = flops_per_launch / (conv_ms / max(conv_launches, 1) * 1e-3) / 1e12 if conv_launches else None
     # launches per profiled call: make_level = clear + insert + neighbour kernels;
     # plan_build = header + Morton keys + the radix sort's kernels + subtiles
-    kernels_per_family = {"make_level": 3, "plan_build": 3 + PLAN_SORT_KERNELS, "conv_tc": 1, "conv_cached": 1,
+    # (row-cache: + subtiles; tap order: header + mask keys + a 27-bit sort)
+    plan_kernels = 3 + PLAN_SORT_KERNELS if cached else 2 + 4
+    kernels_per_family = {"make_level": 3, "plan_build": plan_kernels, "conv_tc": 1, "conv_cached": 1,
                           "act_prepare": 1}
     launches = sum(kernels_per_family.get(k, 1) * v[0] for k, v in prof.items())
 
-    line = None
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            R, kind, ns, sec = cpu_reference_sample(coords, x0, blocks_np, 6.0, os.cpu_count() or 1)
-            cpu = {"value": ns * CONVS_PER_STEP / sec, "unit": "voxels/s",
+            R, kind, ns, sec = cpu_reference_sample(coords, lx0, blocks_np, 6.0, os.cpu_count() or 1)
+            cpu = {"value": ns * convs / sec, "unit": "voxels/s",
                    "cores": (os.cpu_count() or 1) if kind == "reference" else 1, "kind": kind,
-                   "sample": f"first {ns} voxels in (b,z,y,x) order (a z-slab), one 4-block stack run"}
+                   "sample": f"first {ns} voxels in (b,z,y,x) order (a z-slab), one {len(blocks_np)}-block stack run"}
         line = {
             "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None,
             "dtype": "q8_0 (int8 codes exact on tcgen05, per-32-block fp32 scaling as ggml)",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "voxels": n, "valid_pairs": e_pairs, "channels": C_CH,
-                       "blocks": N_BLOCKS, "convs_per_step": CONVS_PER_STEP, "grid": 256,
-                       "step": "make_level + conv plan + 4 res blocks" if cached else "make_level + 4 res blocks",
+            "config": {"workload": args.workload, "voxels": n, "channels": C_CH, "blocks": len(blocks_np),
+                       "convs_per_step": convs, "grid": WORKLOADS[args.workload]["grid"],
+                       "rank0_local_voxels": nl, "rank0_valid_pairs": e_pairs,
+                       "step": (f"make_level + {plan_kind} plan + " if plan_kind else "make_level + ") +
+                               f"{len(blocks_np)} res blocks" + (" (halo exchange before each)" if world > 1 else ""),
                        "conv": args.conv, "l2": "flushed between steps (256 MiB write)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-            "e2e": {"value": world * n * CONVS_PER_STEP / (e2e_t * 1e-3), "unit": "voxels/s",
-                    "h2d_bytes_per_step": int(coords.nbytes + x0.nbytes), "d2h_bytes_per_step": int(x0.nbytes),
-                    "ms_per_step": e2e_t},
+                       "parallelism": f"z-slabs x{world}, 2-plane halo over NCCL" if world > 1 else "single GPU"},
+            "e2e": {"value": n * convs / (e2e_t * 1e-3), "unit": "voxels/s",
+                    "h2d_bytes_per_step": int(lcoords.nbytes + lx0.nbytes),
+                    "d2h_bytes_per_step": int(part.n_owned * C_CH * lx0.itemsize), "ms_per_step": e2e_t},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": (achieved / peak_tf) if achieved else None, "traffic": None,
                          "kernel": f"{conv_family} (Q8_0, C=128)", "peak_source": peak_src,
@@ -340,18 +380,19 @@ def run_ours(args):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.barrier()
+        barrier()
         dist.destroy_process_group()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="shell_4m", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--conv", default="cached", choices=["cached", "direct"])
+    ap.add_argument("--conv", default="ordered", choices=["ordered", "direct", "cached"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

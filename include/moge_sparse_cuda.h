@@ -152,28 +152,35 @@ int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int ci
                     void* stream);
 
 /* ---------------------------------------------------------------- conv plan
- * A conv plan is a per-level reordering of the voxels that lets the Q8_0
- * sparse conv load every input row once per tile: voxels in Morton order of
- * (x, y, z) within each sample, cut into subtiles of at most 128 rows that
- * reference at most 384 distinct input rows each, with those rows' list and a
- * 16-bit (row, tap) -> list position map.  Build it once per level, after
- * msc_make_level, and pass it to every conv on that level.  No counterpart in
- * the reference (its CPU gather walks the neighbour map directly,
- * src/sparse.cpp:579-627); results match the unplanned calls within the
- * features tolerance (the tap summation order differs). */
+ * A conv plan is a per-level reordering of the voxels for the sparse convs
+ * on that level.  Build it once per level, after msc_make_level, and pass it
+ * to every conv on the level.  No counterpart in the reference (its CPU
+ * gather walks the neighbour map directly, src/sparse.cpp:579-627); results
+ * match the unplanned calls within the features tolerance (the tap
+ * summation order differs).  Two kinds:
+ *   MSC_PLAN_TAP_ORDER  the voxels sorted by their 27-bit tap mask (rarest
+ *                       taps first), so that each 128-row tile of the conv
+ *                       runs over fewer taps; used for every weight type.
+ *   MSC_PLAN_ROW_CACHE  voxels in Morton order of (x, y, z), cut into
+ *                       subtiles of at most 128 rows that reference at most
+ *                       384 distinct input rows, with those rows' list and a
+ *                       16-bit (row, tap) -> list position map; used by the
+ *                       row-cached conv (Q8_0 weights, cin = 128). */
+#define MSC_PLAN_TAP_ORDER 0
+#define MSC_PLAN_ROW_CACHE 1
 
 /* Bytes of the plan buffer (256-byte aligned) and of the build workspace. */
 size_t msc_conv_plan_bytes(int64_t n);
 size_t msc_conv_plan_workspace_bytes(int64_t n);
 
-/* Builds the plan of a level from its coords and neighbour map.  Device
- * failures (MSC_DEV_PLAN_OVERFLOW) are reported by msc_check. */
-int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, void* plan,
+/* Builds a plan of the given kind from a level's coords and neighbour map.
+ * Device failures (MSC_DEV_PLAN_OVERFLOW) are reported by msc_check. */
+int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, int kind, void* plan,
                         size_t plan_bytes, void* ws, size_t ws_bytes, void* stream);
 
 /* msc_sparse_conv with an optional plan (NULL = msc_sparse_conv).  With a
- * plan, Q8_0 weights and cin = 128 the row-cached conv runs and nbr may be
- * NULL; other weights ignore the plan and use nbr. */
+ * row-cache plan, Q8_0 weights and cin = 128 the row-cached conv runs and
+ * nbr may be NULL; otherwise nbr is required. */
 int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
                             const void* plan, const void* blob, const float* bias, void* y, int y_dtype, void* ws,
                             size_t ws_bytes, void* stream);

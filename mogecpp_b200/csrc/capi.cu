@@ -29,7 +29,11 @@ struct msc_context {
     };
     std::mutex mu;
     std::unordered_map<const void*, Blob> blobs;
-    std::unordered_map<const void*, int64_t> plans;  // conv plan -> voxel count
+    struct Plan {
+        int64_t n;
+        int kind;
+    };
+    std::unordered_map<const void*, Plan> plans;  // conv plans built by this context
     // kernel profiling (msc_profile_*): one event pair per launch
     struct Rec {
         const char* name;
@@ -157,9 +161,16 @@ void need_ws(size_t have, size_t want) {
         fail(MSC_E_WORKSPACE, "workspace too small: " + std::to_string(have) + " < " + std::to_string(want));
 }
 
+// What a conv plan contributes to one conv: the row-cached kernel's plan, or
+// the tap order for the neighbour-map kernel, or nothing.
+struct PlanUse {
+    const void* cached = nullptr;
+    const int32_t* order = nullptr;
+};
+
 void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
               const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
-              int res_dtype, void* y, int y_dtype, cudaStream_t st, const void* plan = nullptr) {
+              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}) {
     msc::ConvArgs a{};
     a.planes = planes;
     a.q8 = mode == msc::ACT_Q8 || mode == msc::ACT_Q8I;
@@ -185,32 +196,40 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
     a.y = y;
     a.y_dtype = y_dtype;
     a.status = ctx->status;
-    if (plan) {
+    if (pu.cached) {
         a.blob = static_cast<const char*>(blob) + msc::weight_cached_offset(b.wtype, b.cin, b.cout, b.ntaps);
         a.nbr = nullptr;
         ProfScope ps(ctx, "conv_cached", st);
-        cuda_ok(msc::launch_conv_cached(a, plan, st), "cached conv launch");
+        cuda_ok(msc::launch_conv_cached(a, pu.cached, st), "cached conv launch");
         return;
     }
+    a.perm = pu.order;
     ProfScope ps(ctx, nbr ? "conv_tc" : "linear_tc", st);
     cuda_ok(msc::launch_conv(a, st), "conv launch");
 }
 
 // The plan, when given, must come from msc_conv_plan_build on this context
-// for n voxels; it is used by the row-cached conv (Q8_0 conv weights, cin =
-// 128), and null is returned for every other weight.
-const void* use_plan(msc_ctx_t ctx, const void* plan, int64_t n, const msc_context::Blob& b) {
-    if (!plan) return nullptr;
-    int64_t pn = -1;
+// for n voxels.  A tap-order plan reorders the neighbour-map conv's tiles for
+// every weight type; a row-cache plan runs the row-cached conv for Q8_0 conv
+// weights with cin = 128 and is ignored for other weights.
+PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n, const msc_context::Blob& b) {
+    PlanUse pu;
+    if (!plan) return pu;
+    msc_context::Plan pl{};
     {
         std::lock_guard<std::mutex> lk(ctx->mu);
         auto it = ctx->plans.find(plan);
         if (it == ctx->plans.end()) fail(MSC_E_INVALID, "conv plan was not built by this context");
-        pn = it->second;
+        pl = it->second;
     }
-    if (pn != n) fail(MSC_E_INVALID, "conv plan covers " + std::to_string(pn) + " voxels, not " + std::to_string(n));
-    return msc::weight_has_cached(b.wtype, b.cin, b.ntaps) && msc::conv_cached_supported(b.cin, b.cout) ? plan
-                                                                                                      : nullptr;
+    if (pl.n != n)
+        fail(MSC_E_INVALID, "conv plan covers " + std::to_string(pl.n) + " voxels, not " + std::to_string(n));
+    if (pl.kind == MSC_PLAN_TAP_ORDER) {
+        pu.order = msc::plan_view(static_cast<uint8_t*>(const_cast<void*>(plan)), n, msc::plan_max_desc(n)).order;
+    } else if (msc::weight_has_cached(b.wtype, b.cin, b.ntaps) && msc::conv_cached_supported(b.cin, b.cout)) {
+        pu.cached = plan;
+    }
+    return pu;
 }
 
 void check_conv_shape(const msc_context::Blob& b, int cin, int ntaps) {
@@ -381,10 +400,11 @@ size_t msc_conv_plan_bytes(int64_t n) { return n < 0 ? 0 : msc::plan_bytes(n); }
 
 size_t msc_conv_plan_workspace_bytes(int64_t n) { return n < 0 ? 0 : msc::plan_workspace_bytes(n); }
 
-int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, void* plan,
+int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, int kind, void* plan,
                         size_t plan_bytes, void* ws, size_t ws_bytes, void* stream) {
     return guard([&] {
         need_ctx(ctx);
+        need(kind == MSC_PLAN_TAP_ORDER || kind == MSC_PLAN_ROW_CACHE, "unknown plan kind");
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         need(plan != nullptr, "null plan pointer");
         need_aligned(plan, 256, "plan");
@@ -397,10 +417,11 @@ int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const i
         }
         {
             ProfScope ps(ctx, "plan_build", S(stream));
-            cuda_ok(msc::launch_plan_build(coords, nbr, n, plan, ws, ctx->status, S(stream)), "plan build launch");
+            cuda_ok(msc::launch_plan_build(coords, nbr, n, kind, plan, ws, ctx->status, S(stream)),
+                    "plan build launch");
         }
         std::lock_guard<std::mutex> lk(ctx->mu);
-        ctx->plans[plan] = n;
+        ctx->plans[plan] = msc_context::Plan{n, kind};
     });
 }
 
@@ -415,12 +436,12 @@ int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n
         check_conv_shape(b, cin, 27);
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0) return;
-        const void* pl = use_plan(ctx, plan, n, b);
-        need(x && (nbr || pl) && y && ws, "null pointer");
+        const PlanUse pl = use_plan(ctx, plan, n, b);
+        need(x && (nbr || pl.cached) && y && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
-        const int mode = act_mode(b.wtype, x_dtype, b.cin, pl != nullptr);
+        const int mode = act_mode(b.wtype, x_dtype, b.cin, pl.cached != nullptr);
         need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
@@ -478,20 +499,20 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
         need(w1.cout == c && w2.cout == c, "res_block convs must map c -> c");
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0) return;
-        const void* p1 = use_plan(ctx, plan, n, w1);
-        const void* p2 = use_plan(ctx, plan, n, w2);
-        need(x && ((p1 && p2) || nbr) && ws, "null pointer");
+        const PlanUse p1 = use_plan(ctx, plan, n, w1);
+        const PlanUse p2 = use_plan(ctx, plan, n, w2);
+        need(x && ((p1.cached && p2.cached) || nbr) && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(ws, 256, "workspace");
         const size_t planes_bytes = align256(static_cast<size_t>(n) * c * 4);
         need_ws(ws_bytes, planes_bytes + static_cast<size_t>(n) * c * 4);
         void* planes = ws;
         float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
-        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1 != nullptr);
+        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1.cached != nullptr);
         cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
                 "norm1 prepare");
         run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1);
-        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2 != nullptr);
+        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2.cached != nullptr);
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
         run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);

@@ -224,6 +224,36 @@ __device__ __forceinline__ void tmem_st8_fill(uint32_t taddr, uint32_t v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// tcgen05.wait::ld that also names the registers of the awaited load as
+// read-write, so that the compiler cannot move their uses above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[N]) {
+    static_assert(N == 8 || N == 16 || N == 32, "width");
+    if constexpr (N == 32) {
+        asm volatile("tcgen05.wait::ld.sync.aligned;"
+                     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                       "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                       "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]),
+                       "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]),
+                       "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                     :
+                     : "memory");
+    } else if constexpr (N == 16) {
+        asm volatile("tcgen05.wait::ld.sync.aligned;"
+                     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                       "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                       "+r"(r[14]), "+r"(r[15])
+                     :
+                     : "memory");
+    } else {
+        asm volatile("tcgen05.wait::ld.sync.aligned;"
+                     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                       "+r"(r[7])
+                     :
+                     : "memory");
+    }
+}
+
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
     static_assert(N == 8 || N == 16 || N == 32, "tcgen05.ld width");

@@ -347,7 +347,7 @@ __device__ void c_drain(const ConvArgs& a, const CSmem& S, int64_t ndesc, uint32
                 for (int c = 0; c < COLS; c += 16) {
                     uint32_t dv[16];
                     tmem_ld<16>(col + c, dv);
-                    tmem_wait_ld();
+                    tmem_wait_ld_regs(dv);
                     const float4* sb = reinterpret_cast<const float4*>(sbrow + c);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {

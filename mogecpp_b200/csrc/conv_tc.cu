@@ -357,7 +357,7 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                 for (int c = 0; c < COLS; c += CH) {
                     uint32_t d[CH];
                     tmem_ld<CH>(tmem + lane_addr + static_cast<uint32_t>(slot * COUT + c_base + c), d);
-                    tmem_wait_ld();
+                    tmem_wait_ld_regs(d);
                     if (c + CH == COLS) {
                         tc_fence_before();
                         warp_arrive(&S.acc_empty[slot]);

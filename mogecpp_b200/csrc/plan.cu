@@ -1,8 +1,18 @@
-// Conv plan: a per-level tiling of the voxels that lets the sparse conv load
-// each input row once per tile instead of once per (tile row, tap).
+// Conv plans, built once per topology level (the refiner rebuilds topology
+// every refine pass, src/sparse.cpp:443-472) and shared by every conv on it.
 //
-// Built once per topology level (the refiner rebuilds topology every refine
-// pass, src/sparse.cpp:443-472) and shared by every conv on that level.
+// Tap order (kind 0).  The neighbour-map conv runs a 128-row tile over the
+// union of its rows' taps, so a tile of rows with different neighbourhoods
+// costs 27 taps of work for ~15 (surfaces) or ~6 (thin shells) taps of
+// data.  Sorting the voxels by their 27-bit tap mask puts rows with equal
+// or similar neighbourhoods together; the mask bits are ordered so that the
+// rarest taps (corners, then edges, then faces, then the centre) decide the
+// order first.  On the seeded surfaces this lifts the useful fraction of a
+// tile from 0.54 to 0.70 (res4_c128) and from 0.21 to 0.66 (shell_4m).  The
+// stable sort keeps the (b, z, y, x) order among equal masks.
+//
+// Row cache (kind 1): a tiling that lets the conv load each input row once
+// per tile instead of once per (tile row, tap).
 //
 //  1. Voxels are ordered along a Morton curve of (x, y, z) within each sample
 //     (key = b << 48 | interleaved low 16 bits of x, y, z), so consecutive
@@ -54,6 +64,37 @@ __global__ void morton_keys_kernel(const int4* __restrict__ coords, int n, uint6
     const int4 c = __ldg(coords + i);
     keys[i] = (static_cast<uint64_t>(c.w & 0x7f) << 48) | spread3(static_cast<uint32_t>(c.x)) |
               (spread3(static_cast<uint32_t>(c.y)) << 1) | (spread3(static_cast<uint32_t>(c.z)) << 2);
+    vals[i] = i;
+}
+
+// Bit of each tap in the sort key: corners (|dx|+|dy|+|dz| = 3) take the
+// high bits, then edges, faces and the centre.
+struct TapBits {
+    unsigned char bit[27];
+};
+
+TapBits make_tap_bits() {
+    TapBits tb{};
+    int next = 26;
+    for (int cls = 3; cls >= 0; --cls)
+        for (int t = 0; t < 27; ++t) {
+            const int dx = t / 9 - 1, dy = (t / 3) % 3 - 1, dz = t % 3 - 1;
+            if ((dx < 0 ? -dx : dx) + (dy < 0 ? -dy : dy) + (dz < 0 ? -dz : dz) == cls)
+                tb.bit[t] = static_cast<unsigned char>(next--);
+        }
+    return tb;
+}
+
+__global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, TapBits tb, uint32_t* __restrict__ keys,
+                                 int* __restrict__ vals) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t k = 0;
+    const int* r = nbr + static_cast<int64_t>(i) * 27;
+#pragma unroll
+    for (int t = 0; t < 27; ++t)
+        if (static_cast<unsigned>(__ldg(r + t)) < static_cast<unsigned>(n)) k |= 1u << tb.bit[t];
+    keys[i] = k;
     vals[i] = i;
 }
 
@@ -192,11 +233,14 @@ __global__ void __launch_bounds__(kPlanThreads) subtile_kernel(const int* __rest
 size_t align256(size_t v) { return plan_align(v); }
 
 size_t sort_temp_bytes(int64_t n) {
-    size_t bytes = 0;
-    cub::DeviceRadixSort::SortPairs(nullptr, bytes, static_cast<const uint64_t*>(nullptr),
+    size_t b64 = 0, b32 = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, b64, static_cast<const uint64_t*>(nullptr),
                                     static_cast<uint64_t*>(nullptr), static_cast<const int*>(nullptr),
                                     static_cast<int*>(nullptr), static_cast<int>(n), 0, 55);
-    return bytes;
+    cub::DeviceRadixSort::SortPairs(nullptr, b32, static_cast<const uint32_t*>(nullptr),
+                                    static_cast<uint32_t*>(nullptr), static_cast<const int*>(nullptr),
+                                    static_cast<int*>(nullptr), static_cast<int>(n), 0, 27);
+    return b64 > b32 ? b64 : b32;
 }
 
 }  // namespace
@@ -210,7 +254,7 @@ int64_t plan_pool_cap(int64_t n) { return 8 * n + 4 * plan_max_desc(n) + 65536; 
 size_t plan_bytes(int64_t n) {
     return align256(sizeof(PlanHeader)) + align256(static_cast<size_t>(n) * 4) +
            align256(static_cast<size_t>(plan_max_desc(n)) * 16) + align256(static_cast<size_t>(n) * 27 * 2) +
-           align256(static_cast<size_t>(plan_pool_cap(n)) * 4);
+           align256(static_cast<size_t>(n) * 4) + align256(static_cast<size_t>(plan_pool_cap(n)) * 4);
 }
 
 size_t plan_workspace_bytes(int64_t n) {
@@ -218,7 +262,7 @@ size_t plan_workspace_bytes(int64_t n) {
            align256(sort_temp_bytes(n)) + 256;
 }
 
-cudaError_t launch_plan_build(const int32_t* coords, const int32_t* nbr, int64_t n, void* plan, void* ws,
+cudaError_t launch_plan_build(const int32_t* coords, const int32_t* nbr, int64_t n, int kind, void* plan, void* ws,
                               uint32_t* status, cudaStream_t st) {
     auto* hdr = static_cast<PlanHeader*>(plan);
     const int64_t max_desc = plan_max_desc(n);
@@ -235,6 +279,13 @@ cudaError_t launch_plan_build(const int32_t* coords, const int32_t* nbr, int64_t
     size_t temp_bytes = sort_temp_bytes(n);
     PlanView P = plan_view(static_cast<uint8_t*>(plan), n, max_desc);
     const int ni = static_cast<int>(n);
+    if (kind == PLAN_TAP_ORDER) {
+        static const TapBits tb = make_tap_bits();
+        uint32_t* k_in = reinterpret_cast<uint32_t*>(keys_in);
+        uint32_t* k_out = reinterpret_cast<uint32_t*>(keys_out);
+        mask_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(nbr, ni, tb, k_in, vals_in);
+        return cub::DeviceRadixSort::SortPairs(temp, temp_bytes, k_in, k_out, vals_in, P.order, ni, 0, 27, st);
+    }
     morton_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<const int4*>(coords), ni, keys_in, vals_in);
     cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, P.perm, ni, 0, 55,

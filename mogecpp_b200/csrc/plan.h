@@ -1,5 +1,9 @@
-// Conv plan (plan.cu): Morton-ordered subtiles with per-subtile unique input
-// row lists and 16-bit neighbour slots.
+// Conv plan (plan.cu).  Two kinds share one buffer layout:
+//  * tap order (kind 0): the voxels sorted by their tap masks, so that the
+//    128-row tiles of the neighbour-map conv (conv_tc.cu) see few distinct
+//    taps;
+//  * row cache (kind 1): Morton-ordered subtiles with per-subtile unique
+//    input row lists and 16-bit neighbour slots (conv_cached.cu).
 #pragma once
 
 #include <cstddef>
@@ -22,8 +26,11 @@ struct PlanHeader {
     unsigned long long pool_used;    // U-list entries written (each list padded to 4)
 };
 
+enum PlanKind : int { PLAN_TAP_ORDER = 0, PLAN_ROW_CACHE = 1 };
+
 struct PlanView {
     int* perm;        // [n] voxel index per plan row (Morton order)
+    int* order;       // [n] voxel index per row, sorted by tap mask (kind 0)
     int4* desc;       // [max_desc] {row_begin, u_off, rows | u_cnt << 8, tap mask}
     uint16_t* slots;  // [n][27] slot of each (plan row, tap) in its subtile's U list
     int* pool;        // U lists
@@ -41,6 +48,8 @@ __host__ __device__ inline PlanView plan_view(uint8_t* plan, int64_t n, int64_t 
     p += plan_align(static_cast<size_t>(max_desc) * 16);
     v.slots = reinterpret_cast<uint16_t*>(p);
     p += plan_align(static_cast<size_t>(n) * 27 * 2);
+    v.order = reinterpret_cast<int*>(p);
+    p += plan_align(static_cast<size_t>(n) * 4);
     v.pool = reinterpret_cast<int*>(p);
     return v;
 }
@@ -49,7 +58,7 @@ int64_t plan_max_desc(int64_t n);
 int64_t plan_pool_cap(int64_t n);
 size_t plan_bytes(int64_t n);
 size_t plan_workspace_bytes(int64_t n);
-cudaError_t launch_plan_build(const int32_t* coords, const int32_t* nbr, int64_t n, void* plan, void* ws,
+cudaError_t launch_plan_build(const int32_t* coords, const int32_t* nbr, int64_t n, int kind, void* plan, void* ws,
                               uint32_t* status, cudaStream_t st);
 
 }  // namespace msc

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(PKG, "libmoge_sparse_cuda.so")
 
 MSC_OK = 0
 MSC_F32, MSC_F16, MSC_BF16 = 0, 1, 2
+MSC_PLAN_TAP_ORDER, MSC_PLAN_ROW_CACHE = 0, 1
 MSC_W_F32, MSC_W_F16, MSC_W_Q8_0 = 0, 1, 8
 DEV_TIMEOUT, DEV_HASH_FULL, DEV_BAD_COORD, DEV_DUP_COORD, DEV_POOL_OVERFLOW, DEV_BAD_INDEX = 1, 2, 4, 8, 16, 32
 
@@ -36,7 +37,7 @@ SIGNATURES = {
     "msc_sparse_conv": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
     "msc_conv_plan_bytes": (_sz, [_i64]),
     "msc_conv_plan_workspace_bytes": (_sz, [_i64]),
-    "msc_conv_plan_build": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp, _sz, _vp]),
+    "msc_conv_plan_build": (C.c_int, [_vp, _vp, _i64, _vp, _i32, _vp, _sz, _vp, _sz, _vp]),
     "msc_sparse_conv_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz,
                                           _vp]),
     "msc_res_block_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

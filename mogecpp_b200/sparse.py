@@ -142,15 +142,18 @@ class SparseCudaExecutor:
         m = np_host.value
         return Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n)
 
-    def conv_plan(self, coords: torch.Tensor, nbr: torch.Tensor) -> torch.Tensor:
-        """Conv plan of a level (``msc_conv_plan_build``): pass it to sparse_conv /
-        res_block on the same level to run the row-cached Q8_0 conv."""
+    def conv_plan(self, coords: torch.Tensor, nbr: torch.Tensor, kind: str = "tap_order") -> torch.Tensor:
+        """Conv plan of a level (``msc_conv_plan_build``) for sparse_conv /
+        res_block on the same level: "tap_order" (tiles of rows with similar
+        neighbourhoods, any weights) or "row_cache" (the row-cached Q8_0
+        conv)."""
         n = coords.shape[0]
         pb = self.lib.msc_conv_plan_bytes(n)
         plan = torch.empty(pb, dtype=torch.uint8, device=coords.device)
         wsb = self.lib.msc_conv_plan_workspace_bytes(n)
         ws = self.workspace(wsb)
-        L.check(self.lib.msc_conv_plan_build(self.ctx, _p(coords), n, _p(nbr), _p(plan), pb, _p(ws), wsb,
+        code = {"tap_order": L.MSC_PLAN_TAP_ORDER, "row_cache": L.MSC_PLAN_ROW_CACHE}[kind]
+        L.check(self.lib.msc_conv_plan_build(self.ctx, _p(coords), n, _p(nbr), code, _p(plan), pb, _p(ws), wsb,
                                              _stream()))
         return plan
 

@@ -121,8 +121,28 @@ def small_coords(seed: int, extent: int = 24, grid: int = 32, dilation: str = "c
     return dedup_sorted(height_surface(seed, extent, grid, grid / 2, grid / 6, 3.0, 4.0, 1.0, dilation, b=b))
 
 
+_FEATURE_CHUNK = 65536
+
+
+def features_rows(seed: int, rows: np.ndarray, c: int, dtype=np.float32) -> np.ndarray:
+    """N(0, 1) features of the given rows of a seeded [n, c] array, drawn in
+    float32 chunks of 65536 rows with their own streams, so that a rank can
+    draw only its slab's rows and get the same values as a full draw."""
+    rows = np.asarray(rows, dtype=np.int64)
+    out = np.empty((rows.shape[0], c), dtype=dtype)
+    if rows.size == 0:
+        return out
+    chunk = rows // _FEATURE_CHUNK
+    for ch in np.unique(chunk):
+        sel = np.flatnonzero(chunk == ch)
+        block = np.random.default_rng([seed, int(ch)]).standard_normal((_FEATURE_CHUNK, c), dtype=np.float32)
+        out[sel] = block[rows[sel] - ch * _FEATURE_CHUNK]
+    return out
+
+
 def features(seed: int, n: int, c: int, dtype=np.float32) -> np.ndarray:
-    return np.random.default_rng(seed).standard_normal((n, c)).astype(dtype)
+    """N(0, 1) features for rows 0..n-1 (see features_rows)."""
+    return features_rows(seed, np.arange(n), c, dtype)
 
 
 def conv_weight(seed: int, cin: int, cout: int) -> np.ndarray:

@@ -1,7 +1,10 @@
-"""Conv plan (msc_conv_plan_build) and the row-cached Q8_0 conv that runs over
-it (msc_sparse_conv_planned / msc_res_block_planned).
+"""Conv plans (msc_conv_plan_build) and the convs that run over them
+(msc_sparse_conv_planned / msc_res_block_planned): the tap order for the
+neighbour-map conv and the row-cache plan for the row-cached Q8_0 conv.
 
-The plan's integer content is checked exactly against the neighbour map:
+The tap order must be a permutation sorted, stably, by the class-ordered
+tap-mask key.  The row-cache plan's integer content is checked exactly
+against the neighbour map:
 every voxel appears once, in Morton order; every subtile's U list holds
 exactly the distinct neighbours of its rows; every (row, tap) slot points at
 the neighbour the map names, or is 0xFFFF where the map says missing.  The
@@ -43,9 +46,11 @@ def parse_plan(buf, n):
     off += _align(16 * max_desc)
     slots = b[off:off + 2 * 27 * n].view(np.uint16).reshape(n, 27)
     off += _align(2 * 27 * n)
+    order = b[off:off + 4 * n].view(np.int32)
+    off += _align(4 * n)
     pool = b[off:off + 4 * pool_cap].view(np.int32)
     return dict(magic=magic, overflow=overflow, n=hn, max_desc=max_desc, ndesc=ndesc, pool_used=pool_used,
-                perm=perm, desc=desc[:ndesc], slots=slots, pool=pool)
+                perm=perm, desc=desc[:ndesc], slots=slots, order=order, pool=pool)
 
 
 def _spread3(v):
@@ -107,12 +112,72 @@ def dense_offset_cube(side=20, offset=(5, 3, 6)):
     return c[np.argsort(keys, kind="stable")]
 
 
-def _level(ex, oracle, coords):
+def _level(ex, oracle, coords, kind="row_cache"):
     nbr = oracle.make_level(coords)
     cd = dev(coords)
-    plan = ex.conv_plan(cd, dev(nbr))
+    plan = ex.conv_plan(cd, dev(nbr), kind)
     ex.check()
     return nbr, plan
+
+
+def tap_order_keys(nbr):
+    """Sort key of the tap order: corners in the high bits, then edges,
+    faces, centre (tap index order within a class)."""
+    n = nbr.shape[0]
+    bits = np.zeros(27, dtype=np.int64)
+    nxt = 26
+    for cls in (3, 2, 1, 0):
+        for t in range(27):
+            d = (t // 9 - 1, (t // 3) % 3 - 1, t % 3 - 1)
+            if sum(abs(v) for v in d) == cls:
+                bits[t] = nxt
+                nxt -= 1
+    return ((nbr < n).astype(np.int64) << bits[None, :]).sum(1)
+
+
+@pytest.mark.parametrize("case", ["surface", "split", "ragged"])
+def test_tap_order_is_a_stable_sort_by_mask(ex, oracle, case):
+    coords = {"surface": synth.small_coords(205, extent=28, grid=32), "split": dense_offset_cube(),
+              "ragged": synth.small_coords(31, extent=30, grid=32)[:129]}[case]
+    nbr, plan = _level(ex, oracle, coords, "tap_order")
+    order = parse_plan(plan, coords.shape[0])["order"]
+    np.testing.assert_array_equal(order, np.argsort(tap_order_keys(nbr), kind="stable"))
+
+
+@pytest.mark.parametrize("tag", ["f32", "f16", "q8_0"])
+@pytest.mark.parametrize("cin,cout", [(64, 64), (128, 128)])
+def test_tap_ordered_conv_matches_oracle(ex, oracle, tag, cin, cout):
+    from oracle.oracle import W_F16, W_F32
+    coords = synth.small_coords(240 + cin, extent=24, grid=32, dilation="z1")
+    n = coords.shape[0]
+    nbr, plan = _level(ex, oracle, coords, "tap_order")
+    x = synth.features(241, n, cin)
+    w = synth.conv_weight(242, cin, cout)
+    b = (0.1 * np.random.default_rng(243).standard_normal(cout)).astype(np.float32)
+    ref = oracle.sparse_conv(x, nbr, w, {"f32": W_F32, "f16": W_F16, "q8_0": W_Q8_0}[tag], b)
+    pw = ex.prepare_weight(weight_tensor(oracle, w, tag), tag, cin, cout, 27)
+    y = host(ex.sparse_conv(dev(x), dev(nbr), pw, dev(b), plan=plan))
+    yu = host(ex.sparse_conv(dev(x), dev(nbr), pw, dev(b)))
+    ex.check()
+    if tag == "f32":
+        assert rel_l2(y, ref) < 1e-4
+    else:
+        assert rel_l2(y, ref) < TOL_FP16[0] and max_abs(y, ref) < TOL_FP16[1]
+    assert rel_l2(y, yu) < 1e-5, rel_l2(y, yu)
+
+
+def test_tap_ordered_res_block_matches_oracle(ex, oracle):
+    from test_blocks_gpu import make_block, raw_block
+    coords = synth.small_coords(250, extent=28, grid=32)
+    nbr, plan = _level(ex, oracle, coords, "tap_order")
+    x = dev(synth.features(251, coords.shape[0], 128)).to(torch.float16)
+    raw = raw_block(252, 128)
+    xin = host(x)
+    ex.res_block(x, dev(nbr), make_block(ex, oracle, raw, "q8_0", 128), plan=plan)
+    ex.check()
+    ref = oracle.res_block(xin, nbr, raw, W_Q8_0)
+    y = host(x)
+    assert rel_l2(y, ref) < TOL_FP16[0] and max_abs(y, ref) < TOL_FP16[1]
 
 
 @pytest.mark.parametrize("case", ["surface", "two_samples", "split"])
