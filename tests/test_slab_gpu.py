@@ -1,0 +1,114 @@
+"""Z-slab residual stack on two GPUs: one process per GPU, NCCL halo
+exchange before each Q8_0 residual block (mogecpp_b200/slab.py).  The owned
+rows of the two ranks are compared with the single-GPU stack over the whole
+set and with the oracle.  The runs differ only in the fp32 summation order
+of the conv tiles, which the fp16 state and the Q8_0 re-quantisation of
+each conv input turn into occasional one-step rounding flips (rel-L2 ~1e-4);
+a wrong halo would put O(1) errors on the rows next to the slab boundary,
+which the max-abs bound catches.  Skipped with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from mogecpp_b200 import slab, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _coords():
+    return synth.small_coords(330, extent=40, grid=64, dilation="z1")
+
+
+def _raw_block(seed, c):
+    rng = np.random.default_rng(seed)
+    return dict(norm_w=(1 + 0.1 * rng.standard_normal(c)).astype(np.float32),
+                norm_b=(0.1 * rng.standard_normal(c)).astype(np.float32),
+                w1=synth.conv_weight(seed + 1, c, c), b1=(0.05 * rng.standard_normal(c)).astype(np.float32),
+                w2=synth.conv_weight(seed + 2, c, c), b2=(0.05 * rng.standard_normal(c)).astype(np.float32))
+
+
+def _stack(ex, coords_np, x_np, world=1, part=None, exchange=None, plan_kind=None):
+    import torch
+    from mogecpp_b200.synth import quantize_q8_0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cd = torch.from_numpy(coords_np).to(dev)
+    nbr = ex.make_level(cd)
+    plan = ex.conv_plan(cd, nbr, plan_kind) if plan_kind else None
+    x = torch.from_numpy(x_np).to(dev)
+    for blk in range(2):
+        raw = _raw_block(340 + blk, 128)
+        b = dict(norm_w=torch.from_numpy(raw["norm_w"]).to(dev), norm_b=torch.from_numpy(raw["norm_b"]).to(dev),
+                 b1=torch.from_numpy(raw["b1"]).to(dev), b2=torch.from_numpy(raw["b2"]).to(dev),
+                 w1=ex.prepare_weight(torch.from_numpy(quantize_q8_0(raw["w1"])).to(dev), "q8_0", 128, 128, 27),
+                 w2=ex.prepare_weight(torch.from_numpy(quantize_q8_0(raw["w2"])).to(dev), "q8_0", 128, 128, 27))
+        if exchange is not None:
+            exchange.exchange(x)
+        ex.res_block(x, nbr, b, plan=plan)
+    ex.check()
+    return x.float().cpu().numpy()
+
+
+def _rank_main(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from mogecpp_b200.sparse import SparseCudaExecutor
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        ex = SparseCudaExecutor(rank)
+        coords = _coords()
+        part = slab.partition(coords, world)[rank]
+        rows = part.local_rows()
+        x = synth.features_rows(331, rows, 128, np.float16)
+        y = _stack(ex, np.ascontiguousarray(coords[rows]), x, world, part, slab.SlabExchange(part, world),
+                   plan_kind="tap_order")
+        np.save(out_path, y[:part.n_owned])
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle):
+    import multiprocessing as mp
+    import torch
+    from conftest import max_abs, rel_l2
+    from oracle.oracle import W_Q8_0
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    outs = [str(tmp_path / f"rank{r}.npy") for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, outs[r])) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = np.concatenate([np.load(o) for o in outs])
+    coords = _coords()
+    x = synth.features(331, coords.shape[0], 128, np.float16)
+    single = _stack(ex, coords, x)
+    assert rel_l2(got, single) < 1e-3 and max_abs(got, single) < 3e-2, (rel_l2(got, single), max_abs(got, single))
+    # rows of the two planes on either side of the cut
+    cut = slab.partition(coords, world)[1].lo
+    zc = coords[cut, 2]
+    near = np.flatnonzero(np.abs(coords[:, 2] - zc) <= 2)
+    assert max_abs(got[near], single[near]) < 3e-2
+    nbr = oracle.make_level(coords)
+    h = x.astype(np.float32)
+    for blk in range(2):
+        h = oracle.res_block(h, nbr, _raw_block(340 + blk, 128), W_Q8_0).astype(np.float16).astype(np.float32)
+    assert rel_l2(got, h) < 3e-3 and max_abs(got, h) < 3e-2
