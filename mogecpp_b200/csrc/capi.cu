@@ -170,7 +170,7 @@ struct PlanUse {
 
 void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
               const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
-              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}) {
+              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}, void* q_out = nullptr) {
     msc::ConvArgs a{};
     a.planes = planes;
     a.q8 = mode == msc::ACT_Q8 || mode == msc::ACT_Q8I;
@@ -195,6 +195,12 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
     a.res_dtype = res_dtype;
     a.y = y;
     a.y_dtype = y_dtype;
+    if (q_out) {
+        // fused re-quantisation: the ACT_Q8I operand of the next conv
+        a.q_codes = static_cast<int8_t*>(q_out);
+        a.q_scales = reinterpret_cast<float*>(static_cast<char*>(q_out) +
+                                              msc::act_scale_offset(msc::ACT_Q8I, n, b.cout));
+    }
     a.status = ctx->status;
     if (pu.cached) {
         a.blob = static_cast<const char*>(blob) + msc::weight_cached_offset(b.wtype, b.cin, b.cout, b.ntaps);
@@ -511,8 +517,16 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
         const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1.cached != nullptr);
         cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
                 "norm1 prepare");
-        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1);
         const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2.cached != nullptr);
+        if (m2 == msc::ACT_Q8I && !p1.cached && c == 128) {
+            // conv1's epilogue quantises SiLU(conv1 + b1) for conv2 in place of
+            // an fp32 intermediate and a separate preparation pass (same ggml
+            // quantiser, same values: identical operand)
+            run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1, h);
+            run_conv(ctx, h, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);
+            return;
+        }
+        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1);
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
         run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);

@@ -81,6 +81,12 @@ struct ConvArgs {
     int res_dtype;
     void* y;                 // [rows][cout]
     int y_dtype;
+    // When set (cout = 128), the output is re-quantised for the next Q8_0
+    // conv instead of stored in y: int8 codes [rows][cout] and fp32(fp16(d))
+    // block scales [rows][cout/32] of ggml's x86 quantiser (the ACT_Q8I
+    // operand).  Only the neighbour-map kernel (conv_tc.cu) supports it.
+    int8_t* q_codes;
+    float* q_scales;
     uint32_t* status;
 };
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t st);

@@ -107,4 +107,28 @@ __device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const
     }
 }
 
+// Quantises one 32-channel block with ggml's x86 Q8_0 rules (d = amax/127,
+// id = 127/amax, codes rounded half to even; quants.c:302) and stores the
+// 32 int8 codes (16-byte aligned) and fp32(fp16(d)), exactly as the
+// ACT_Q8I activation preparation does.
+__device__ __forceinline__ void quantize_store_block32(const float (&v)[32], int8_t* codes, float* scale) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t t = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            t |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[4 * k + j], id))) & 0xffu) << (8 * j);
+        w[k] = t;
+    }
+    reinterpret_cast<uint4*>(codes)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4*>(codes)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *scale = __half2float(__float2half_rn(d));
+}
+
 }  // namespace msc

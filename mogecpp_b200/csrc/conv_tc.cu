@@ -411,6 +411,14 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                     if (a.residual) t += load_elem(a.residual, a.res_dtype, static_cast<int64_t>(row) * COUT + n);
                     v[e] = t;
                 }
+                if constexpr (EC == 32) {
+                    // this thread holds one whole 32-channel block of the row
+                    if (a.q_codes) {
+                        const int64_t blk = static_cast<int64_t>(row) * (COUT / 32) + (c_base + c0) / 32;
+                        quantize_store_block32(v, a.q_codes + blk * 32, a.q_scales + blk);
+                        continue;
+                    }
+                }
                 store_row<EC>(a.y, a.y_dtype, static_cast<int64_t>(row) * COUT + c_base + c0, v);
             }
         }

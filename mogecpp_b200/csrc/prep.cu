@@ -145,7 +145,53 @@ __global__ void weight_q8c_kernel(const BlockQ8* w, int cin, int cout, int ntaps
 
 __global__ void weight_cached_off_kernel(WeightHeader* h, uint32_t off) { h->cached_off = off; }
 
-// One warp per row; lane l holds channels [l*EPL, (l+1)*EPL).
+// EPL consecutive 32-bit words <-> memory at p, in the widest aligned
+// accesses (the row part of a lane is EPL elements at an EPL-aligned offset).
+template <int NW>
+__device__ __forceinline__ void load_words(const void* p, uint32_t (&w)[NW]) {
+    if constexpr (NW % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < NW / 4; ++k) {
+            const uint4 t = reinterpret_cast<const uint4*>(p)[k];
+            w[4 * k] = t.x, w[4 * k + 1] = t.y, w[4 * k + 2] = t.z, w[4 * k + 3] = t.w;
+        }
+    } else if constexpr (NW == 2) {
+        const uint2 t = *reinterpret_cast<const uint2*>(p);
+        w[0] = t.x, w[1] = t.y;
+    } else {
+        w[0] = *reinterpret_cast<const uint32_t*>(p);
+    }
+}
+template <int NW>
+__device__ __forceinline__ void store_words(void* p, const uint32_t (&w)[NW]) {
+    if constexpr (NW % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < NW / 4; ++k)
+            reinterpret_cast<uint4*>(p)[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+    } else if constexpr (NW == 2) {
+        *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+    } else {
+        *reinterpret_cast<uint32_t*>(p) = w[0];
+    }
+}
+
+// EPL fp16 values as half-words: vector stores when EPL >= 2.
+template <int EPL>
+__device__ __forceinline__ void store_halves(__half* dst, const __half (&h)[EPL]) {
+    if constexpr (EPL >= 2) {
+        uint32_t w[EPL / 2];
+#pragma unroll
+        for (int k = 0; k < EPL / 2; ++k)
+            w[k] = static_cast<uint32_t>(__half_as_ushort(h[2 * k])) |
+                   (static_cast<uint32_t>(__half_as_ushort(h[2 * k + 1])) << 16);
+        store_words<EPL / 2>(dst, w);
+    } else {
+        dst[0] = h[0];
+    }
+}
+
+// One warp per row; lane l holds channels [l*EPL, (l+1)*EPL), read and
+// written with one vector access each where the width allows.
 template <int C>
 __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
                                    const float* beta, float eps, int silu, int mode, __half* planes) {
@@ -155,14 +201,27 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
     if (row >= n) return;
     float v[EPL];
     const int64_t base = row * C + lane * EPL;
+    if (x_dtype == DT_F32) {
+        if constexpr (EPL >= 4) {
+            uint32_t w[EPL];
+            load_words<EPL>(static_cast<const float*>(x) + base, w);
 #pragma unroll
-    for (int k = 0; k < EPL; ++k) {
-        if (x_dtype == DT_F32)
-            v[k] = static_cast<const float*>(x)[base + k];
-        else if (x_dtype == DT_F16)
-            v[k] = __half2float(static_cast<const __half*>(x)[base + k]);
-        else
-            v[k] = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base + k]);
+            for (int k = 0; k < EPL; ++k) v[k] = __uint_as_float(w[k]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < EPL; ++k) v[k] = static_cast<const float*>(x)[base + k];
+        }
+    } else if constexpr (EPL >= 2) {
+        uint32_t w[EPL / 2];
+        load_words<EPL / 2>(static_cast<const __half*>(x) + base, w);
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            const unsigned short b = static_cast<unsigned short>(w[k / 2] >> (16 * (k & 1)));
+            v[k] = x_dtype == DT_F16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
+        }
+    } else {
+        v[0] = x_dtype == DT_F16 ? __half2float(static_cast<const __half*>(x)[base])
+                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base]);
     }
     if (ln) {
         float s = 0.0f;
@@ -181,8 +240,8 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
 #pragma unroll
         for (int k = 0; k < EPL; ++k) {
             float t = __fmul_rn(v[k] - mean, scale);
-            if (gamma) t = __fmul_rn(t, gamma[lane * EPL + k]);
-            if (beta) t = __fadd_rn(t, beta[lane * EPL + k]);
+            if (gamma) t = __fmul_rn(t, __ldg(gamma + lane * EPL + k));
+            if (beta) t = __fadd_rn(t, __ldg(beta + lane * EPL + k));
             v[k] = t;
         }
     }
@@ -192,8 +251,10 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
     }
     const int64_t plane = n * C;
     if (mode == ACT_FP16) {
+        __half h[EPL];
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) planes[base + k] = __float2half_rn(v[k]);
+        for (int k = 0; k < EPL; ++k) h[k] = __float2half_rn(v[k]);
+        store_halves<EPL>(planes + base, h);
         return;
     }
     if (mode == ACT_Q8 || mode == ACT_Q8I) {
@@ -204,13 +265,28 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         for (int o = 1; o < 32 / EPL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        int q[EPL];
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) q[k] = __float2int_rn(__fmul_rn(v[k], id));
         if (mode == ACT_Q8I) {
-            int8_t* codes = reinterpret_cast<int8_t*>(planes);
+            int8_t* codes = reinterpret_cast<int8_t*>(planes) + base;
+            if constexpr (EPL >= 4) {
+                uint32_t w[EPL / 4];
 #pragma unroll
-            for (int k = 0; k < EPL; ++k) codes[base + k] = static_cast<int8_t>(__float2int_rn(__fmul_rn(v[k], id)));
+                for (int k = 0; k < EPL / 4; ++k)
+                    w[k] = (static_cast<uint32_t>(q[4 * k]) & 0xffu) | ((static_cast<uint32_t>(q[4 * k + 1]) & 0xffu) << 8) |
+                           ((static_cast<uint32_t>(q[4 * k + 2]) & 0xffu) << 16) |
+                           (static_cast<uint32_t>(q[4 * k + 3]) << 24);
+                store_words<EPL / 4>(codes, w);
+            } else {
+#pragma unroll
+                for (int k = 0; k < EPL; ++k) codes[k] = static_cast<int8_t>(q[k]);
+            }
         } else {
+            __half h[EPL];
 #pragma unroll
-            for (int k = 0; k < EPL; ++k) planes[base + k] = __int2half_rn(__float2int_rn(__fmul_rn(v[k], id)));
+            for (int k = 0; k < EPL; ++k) h[k] = __int2half_rn(q[k]);
+            store_halves<EPL>(planes + base, h);
         }
         if ((lane * EPL) % 32 == 0) {
             float* scales = reinterpret_cast<float*>(reinterpret_cast<char*>(planes) +
@@ -219,13 +295,11 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         }
         return;
     }
+    __half hi[EPL], lo[EPL];
 #pragma unroll
-    for (int k = 0; k < EPL; ++k) {
-        __half hi, lo;
-        split_f16(v[k], hi, lo);
-        planes[base + k] = hi;
-        planes[plane + base + k] = lo;
-    }
+    for (int k = 0; k < EPL; ++k) split_f16(v[k], hi[k], lo[k]);
+    store_halves<EPL>(planes + base, hi);
+    store_halves<EPL>(planes + plane + base, lo);
 }
 
 }  // namespace
