@@ -191,6 +191,37 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
                           const float* b1, const void* blob2, const float* b2, void* ws, size_t ws_bytes,
                           void* stream);
 
+/* --------------------------------------------------- GroupNorm res block
+ * The GroupNorm variant of the residual block, in place:
+ *   x = x + conv2(SiLU(GroupNorm_32(conv1(x) + b1))) + b2
+ * GroupNorm is sample-wide: for each sample (coords[i][3]) and each of 32
+ * groups of c/32 channels, the mean over the sample's voxels (double sum),
+ * then the variance of the float deviations (double sum of their squares),
+ * y = (h - mean) * (1 / sqrtf(var + eps)), then * gn_w, then + gn_b (either
+ * may be NULL).  Restates ggml's group_norm_f32 (ggml-cpu/ops.cpp:4208-4283)
+ * on the [C, N] features viewed as [N, 1, C]; the reference's res_block
+ * (src/sparse.cpp:629-642) uses LayerNorm instead and has no counterpart.
+ *
+ * Sharded runs: rows [0, n_stat) are this rank's own voxels and enter the
+ * statistics; rows [n_stat, n) are halo rows, normalised with the same
+ * statistics.  stats is a caller-owned device buffer of
+ * msc_gn_stats_doubles(nsamples) doubles.  When allreduce is given it is
+ * called twice on the calling thread, in stream order, with a device span
+ * of the statistics to sum over all ranks in place (enqueued on `stream`,
+ * e.g. an NCCL all-reduce): first the sums and counts (nsamples * 33
+ * doubles at stats), then the squared deviations (nsamples * 32 doubles at
+ * stats + nsamples * 33).  A non-zero return fails the call.  With n = 0
+ * the callback is still called (collectives stay matched across ranks). */
+typedef int (*msc_allreduce_fn)(double* buf, int64_t count, void* stream, void* user);
+
+int64_t msc_gn_stats_doubles(int nsamples);
+size_t msc_res_block_gn_workspace_bytes(int64_t n, int c, int nsamples);
+int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_stat, int c, const int32_t* coords,
+                     int nsamples, const int32_t* nbr, const void* plan, const float* gn_w, const float* gn_b,
+                     float eps, const void* blob1, const float* b1, const void* blob2, const float* b2,
+                     double* stats, msc_allreduce_fn allreduce, void* allreduce_user, void* ws, size_t ws_bytes,
+                     void* stream);
+
 /* y = W x + bias per row.  Replaces: linear (src/sparse.cpp:515-518). */
 int msc_linear(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const void* blob, const float* bias,
                void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream);

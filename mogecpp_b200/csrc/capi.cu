@@ -4,6 +4,7 @@
 // every call runs inside guard(), which converts exceptions into a negative
 // status and a thread-local message; nothing throws across the boundary.
 #include "conv.h"
+#include "gn.h"
 #include "ops.h"
 #include "plan.h"
 #include "topology.h"
@@ -402,6 +403,13 @@ size_t msc_op_workspace_bytes(int64_t n, int c) {
     return align256(static_cast<size_t>(n) * c * 4) + align256(static_cast<size_t>(n) * c * 4) + 256;
 }
 
+int64_t msc_gn_stats_doubles(int nsamples) { return nsamples < 1 ? 0 : msc::gn_stats_doubles(nsamples); }
+
+size_t msc_res_block_gn_workspace_bytes(int64_t n, int c, int nsamples) {
+    if (n < 0 || c <= 0 || nsamples < 1) return 0;
+    return msc_op_workspace_bytes(n, c) + align256(static_cast<size_t>(nsamples) * 32 * sizeof(float2));
+}
+
 size_t msc_conv_plan_bytes(int64_t n) { return n < 0 ? 0 : msc::plan_bytes(n); }
 
 size_t msc_conv_plan_workspace_bytes(int64_t n) { return n < 0 ? 0 : msc::plan_workspace_bytes(n); }
@@ -530,6 +538,78 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
         run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);
+    });
+}
+
+int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_stat, int c, const int32_t* coords,
+                     int nsamples, const int32_t* nbr, const void* plan, const float* gn_w, const float* gn_b,
+                     float eps, const void* blob1, const float* b1, const void* blob2, const float* b2,
+                     double* stats, msc_allreduce_fn allreduce, void* allreduce_user, void* ws, size_t ws_bytes,
+                     void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        const auto w1 = blob_info(ctx, blob1);
+        const auto w2 = blob_info(ctx, blob2);
+        check_conv_shape(w1, c, 27);
+        check_conv_shape(w2, c, 27);
+        need(w1.cout == c && w2.cout == c, "res_block convs must map c -> c");
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        need(n_stat >= 0 && n_stat <= n, "n_stat must be in [0, n]");
+        need(nsamples >= 1 && nsamples <= (1 << 20), "nsamples out of range");
+        need(eps > 0.0f, "eps must be positive");
+        if (n == 0 && !allreduce) return;
+        const PlanUse p1 = use_plan(ctx, plan, n, w1);
+        const PlanUse p2 = use_plan(ctx, plan, n, w2);
+        need(stats && ws && (n == 0 || (x && coords && ((p1.cached && p2.cached) || nbr))), "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(coords, 16, "coords");
+        need_aligned(stats, 8, "stats");
+        need_aligned(ws, 256, "workspace");
+        need_ws(ws_bytes, msc_res_block_gn_workspace_bytes(n, c, nsamples));
+        const size_t planes_bytes = align256(static_cast<size_t>(n) * c * 4);
+        void* planes = ws;
+        float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
+        float2* gn = reinterpret_cast<float2*>(static_cast<char*>(ws) + 2 * planes_bytes + 256);
+        const int64_t ns = nsamples;
+        cudaStream_t st = S(stream);
+        auto reduce = [&](double* buf, int64_t count, const char* what) {
+            if (allreduce && allreduce(buf, count, stream, allreduce_user) != 0)
+                fail(MSC_E_INVALID, std::string("GroupNorm statistics all-reduce failed (") + what + ")");
+        };
+        // conv1 + b1 on the raw features
+        if (n > 0) {
+            const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1.cached != nullptr);
+            cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 0, nullptr, nullptr, 0.f, 0, m1, planes, st), "conv1 prepare");
+            run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 0, nullptr, 0, h, MSC_F32, st, p1);
+        }
+        // sample-wide statistics of the owned rows: sums and counts, then the
+        // squared deviations from the complete means
+        cuda_ok(cudaMemsetAsync(stats, 0, sizeof(double) * msc::gn_stats_doubles(nsamples), st), "stats clear");
+        {
+            ProfScope ps(ctx, "gn_stats", st);
+            if (n > 0) cuda_ok(msc::launch_gn_pass(1, h, c, coords, n, n_stat, nsamples, stats, ctx->status, st),
+                               "GroupNorm sums");
+        }
+        reduce(stats, ns * 33, "sums");
+        {
+            ProfScope ps(ctx, "gn_stats", st);
+            if (n > 0) cuda_ok(msc::launch_gn_pass(2, h, c, coords, n, n_stat, nsamples, stats, ctx->status, st),
+                               "GroupNorm deviations");
+        }
+        reduce(stats + ns * 33, ns * 32, "deviations");
+        if (n == 0) return;
+        cuda_ok(msc::launch_gn_finalize(stats, c, nsamples, eps, gn, st), "GroupNorm finalize");
+        // GroupNorm + SiLU fused into conv2's operand preparation, then
+        // conv2 + b2 + x into x
+        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2.cached != nullptr);
+        {
+            ProfScope ps(ctx, "act_prepare", st);
+            cuda_ok(msc::launch_act_prepare(h, MSC_F32, n, c, 0, gn_w, gn_b, eps, 1, m2, planes, st, gn, coords,
+                                            nsamples),
+                    "GroupNorm apply");
+        }
+        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, st, p2);
     });
 }
 

@@ -54,10 +54,14 @@ size_t act_bytes(int mode, int64_t n, int c);
 // Q8 modes: the per-block scales follow the code plane at this byte offset.
 size_t act_scale_offset(int mode, int64_t n, int c);
 // x: [n][c] (dtype) -> prepared operand (planes [act_planes][n][c] fp16, plus
-// scales in Q8 mode).  Optional LayerNorm (affine gamma/beta, either may be
-// null) and SiLU before preparation.
+// scales in Q8 mode).  Optional normalisation before preparation: LayerNorm
+// (ln), or, when gn is given, 32-group GroupNorm with gn[sample*32 + group] =
+// {mean, 1/sqrt(var + eps)} and the sample of row i in coords[i][3]
+// (clamped to [0, nsamples)); both
+// with the affine gamma/beta (either may be null).  Then optional SiLU.
 cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int ln, const float* gamma,
-                               const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st);
+                               const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st,
+                               const float2* gn = nullptr, const int32_t* coords = nullptr, int nsamples = 0);
 
 struct ConvArgs {
     const void* planes;      // [na][n_in][cin] fp16 operand planes (Q8: the int8 codes as fp16)

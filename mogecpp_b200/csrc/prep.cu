@@ -194,7 +194,8 @@ __device__ __forceinline__ void store_halves(__half* dst, const __half (&h)[EPL]
 // written with one vector access each where the width allows.
 template <int C>
 __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
-                                   const float* beta, float eps, int silu, int mode, __half* planes) {
+                                   const float* beta, float eps, int silu, int mode, __half* planes,
+                                   const float2* gn, const int4* coords, int nsamples) {
     constexpr int EPL = C / 32;
     const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -223,7 +224,20 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         v[0] = x_dtype == DT_F16 ? __half2float(static_cast<const __half*>(x)[base])
                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base]);
     }
-    if (ln) {
+    if (gn) {
+        // GroupNorm with 32 groups: lane l holds group l; ggml order
+        // ((x - mean) * scale, then * gamma, then + beta)
+        int b = __ldg(coords + row).w;  // out-of-range samples are reported by the statistics pass
+        b = b < 0 ? 0 : (b >= nsamples ? nsamples - 1 : b);
+        const float2 ms = gn[b * 32 + lane];
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            float t = __fmul_rn(v[k] - ms.x, ms.y);
+            if (gamma) t = __fmul_rn(t, __ldg(gamma + lane * EPL + k));
+            if (beta) t = __fadd_rn(t, __ldg(beta + lane * EPL + k));
+            v[k] = t;
+        }
+    } else if (ln) {
         float s = 0.0f;
 #pragma unroll
         for (int k = 0; k < EPL; ++k) s += v[k];
@@ -370,15 +384,18 @@ size_t act_bytes(int mode, int64_t n, int c) {
 }
 
 cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int ln, const float* gamma,
-                               const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st) {
+                               const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st,
+                               const float2* gn, const int32_t* coords, int nsamples) {
     if (n == 0) return cudaSuccess;
     const unsigned grid = static_cast<unsigned>((n * 32 + 255) / 256);
     auto* out = static_cast<__half*>(planes);
+    const int4* c4 = reinterpret_cast<const int4*>(coords);
+    if (gn && (c % 32 != 0 || !coords || nsamples < 1)) return cudaErrorInvalidValue;
     switch (c) {
-        case 32: act_prepare_kernel<32><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
-        case 64: act_prepare_kernel<64><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
-        case 128: act_prepare_kernel<128><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
-        case 256: act_prepare_kernel<256><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out); break;
+        case 32: act_prepare_kernel<32><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out, gn, c4, nsamples); break;
+        case 64: act_prepare_kernel<64><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out, gn, c4, nsamples); break;
+        case 128: act_prepare_kernel<128><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out, gn, c4, nsamples); break;
+        case 256: act_prepare_kernel<256><<<grid, 256, 0, st>>>(x, x_dtype, n, ln, gamma, beta, eps, silu, mode, out, gn, c4, nsamples); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -42,6 +42,10 @@ SIGNATURES = {
                                           _vp]),
     "msc_res_block_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _sz, _vp]),
+    "msc_gn_stats_doubles": (_i64, [_i32]),
+    "msc_res_block_gn_workspace_bytes": (_sz, [_i64, _i32, _i32]),
+    "msc_res_block_gn": (C.c_int, [_vp, _vp, _i32, _i64, _i64, _i32, _vp, _i32, _vp, _vp, _vp, _vp, C.c_float, _vp,
+                                   _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "msc_linear": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
     "msc_res_block": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "msc_pool_down": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
@@ -50,6 +54,10 @@ SIGNATURES = {
     "msc_profile_enable": (C.c_int, [_vp, _i32]),
     "msc_profile_read": (C.c_int, [_vp, _vp, _i32, C.POINTER(_i32)]),
 }
+
+
+# int (*)(double* buf, int64_t count, void* stream, void* user)
+ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, _vp, _i64, _vp, _vp)
 
 
 class ProfileEntry(C.Structure):

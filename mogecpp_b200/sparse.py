@@ -11,6 +11,7 @@ refiner's operators with the reference's names and argument meaning
     downsample(coords)                    -> Transition           (:312-357)
     sparse_conv(x, nbr, w, bias)          -> y [n, cout]          (:579-627)
     res_block(x, nbr, block)              -> x (in place)         (:629-642)
+    res_block_gn(x, nbr, coords, ...)     -> x (in place)         (GroupNorm variant; ggml group_norm)
     pool_down(x, tr, w, bias)             -> y [np, cout]         (:646-668)
     nearest_up(x, tr, w, bias, skip)      -> y [nfine, cout]      (:670-674)
     linear(x, w, bias)                    -> y [n, cout]          (:515-518)
@@ -195,6 +196,38 @@ class SparseCudaExecutor:
                                                _p(blk.get("norm_w")), _p(blk.get("norm_b")), _p(blk["w1"].blob),
                                                _p(blk.get("b1")), _p(blk["w2"].blob), _p(blk.get("b2")), _p(ws),
                                                wsb, _stream()))
+        return x
+
+    def res_block_gn(self, x, nbr, coords, nsamples: int, blk: dict, eps: float = 1e-5, plan=None,
+                     n_stat: int | None = None, allreduce=None):
+        """In place on x: x + conv2(SiLU(GroupNorm_32(conv1(x) + b1))) + b2.
+
+        blk: w1, b1, w2, b2 as for res_block, gn_w / gn_b the GroupNorm
+        affine.  coords [n, 4] int32 give each row's sample (field 3).  Rows
+        [0, n_stat) enter the sample-wide statistics (default: all rows);
+        ``allreduce(t)``, when given, sums the float64 tensor t over all
+        ranks in place on the current stream (two calls per block)."""
+        n, c = x.shape
+        n_stat = n if n_stat is None else n_stat
+        wsb = self.lib.msc_res_block_gn_workspace_bytes(n, c, nsamples)
+        ws = self.workspace(wsb)
+        stats = torch.empty(self.lib.msc_gn_stats_doubles(nsamples), dtype=torch.float64, device=x.device)
+        cb = None
+        if allreduce is not None:
+            base = stats.data_ptr()
+
+            def _cb(buf, count, _stream, _user):
+                try:
+                    off = (buf - base) // 8
+                    allreduce(stats[off:off + count])
+                    return 0
+                except Exception:  # noqa: BLE001 - reported through the return code
+                    return 1
+            cb = L.ALLREDUCE_FN(_cb)
+        L.check(self.lib.msc_res_block_gn(self.ctx, _p(x), _DT[x.dtype], n, n_stat, c, _p(coords), nsamples,
+                                          _p(nbr), _p(plan), _p(blk.get("gn_w")), _p(blk.get("gn_b")), eps,
+                                          _p(blk["w1"].blob), _p(blk.get("b1")), _p(blk["w2"].blob),
+                                          _p(blk.get("b2")), _p(stats), cb, None, _p(ws), wsb, _stream()))
         return x
 
     def pool_down(self, x, tr: Transition, w: PreparedWeight, bias=None, out_dtype=torch.float32):

@@ -408,6 +408,67 @@ void orc_res_block(const float *x, int64_t n, int c, const int32_t *nbr, int wty
     free(h2);
 }
 
+/* ggml-cpu/ops.cpp:4208-4283 group_norm_f32 applied per sample, then the
+ * affine ggml_mul / ggml_add. */
+void orc_group_norm(const float *x, int64_t n, int c, const int32_t *sample, int nsamples, int groups, float eps,
+                    const float *gamma, const float *beta, float *y) {
+    const int cpg = (c + groups - 1) / groups;
+    int64_t *count = (int64_t *)calloc((size_t)nsamples, sizeof(int64_t));
+    double *sum = (double *)calloc((size_t)nsamples * (size_t)groups, sizeof(double));
+    double *sum2 = (double *)calloc((size_t)nsamples * (size_t)groups, sizeof(double));
+    float *mean = (float *)malloc(sizeof(float) * (size_t)nsamples * (size_t)groups);
+    float *scale = (float *)malloc(sizeof(float) * (size_t)nsamples * (size_t)groups);
+    for (int64_t i = 0; i < n; ++i) count[sample[i]]++;
+    for (int64_t i = 0; i < n; ++i)
+        for (int j = 0; j < c; ++j) sum[(int64_t)sample[i] * groups + j / cpg] += (double)x[i * c + j];
+    for (int b = 0; b < nsamples; ++b)
+        for (int g = 0; g < groups; ++g) {
+            const int start = g * cpg, end = start + cpg > c ? c : start + cpg;
+            const double cnt = (double)count[b] * (double)(end - start);
+            mean[b * groups + g] = cnt > 0 ? (float)(sum[b * groups + g] / cnt) : 0.0f;
+        }
+    for (int64_t i = 0; i < n; ++i)
+        for (int j = 0; j < c; ++j) {
+            const int64_t k = (int64_t)sample[i] * groups + j / cpg;
+            const float v = x[i * c + j] - mean[k];
+            y[i * c + j] = v;
+            sum2[k] += (double)(v * v);
+        }
+    for (int b = 0; b < nsamples; ++b)
+        for (int g = 0; g < groups; ++g) {
+            const int start = g * cpg, end = start + cpg > c ? c : start + cpg;
+            const double cnt = (double)count[b] * (double)(end - start);
+            const float variance = cnt > 0 ? (float)(sum2[b * groups + g] / cnt) : 0.0f;
+            scale[b * groups + g] = 1.0f / sqrtf(variance + eps);
+        }
+    for (int64_t i = 0; i < n; ++i)
+        for (int j = 0; j < c; ++j) {
+            float t = y[i * c + j] * scale[(int64_t)sample[i] * groups + j / cpg];
+            if (gamma) t = t * gamma[j];
+            if (beta) t = t + beta[j];
+            y[i * c + j] = t;
+        }
+    free(count);
+    free(sum);
+    free(sum2);
+    free(mean);
+    free(scale);
+}
+
+void orc_res_block_gn(const float *x, int64_t n, int c, const int32_t *nbr, const int32_t *sample, int nsamples,
+                      int groups, float eps, int wtype, const float *gn_w, const float *gn_b, const void *w1,
+                      const float *b1, const void *w2, const float *b2, float *y) {
+    float *h = (float *)malloc(sizeof(float) * (size_t)(n * c));
+    float *h2 = (float *)malloc(sizeof(float) * (size_t)(n * c));
+    orc_sparse_conv(x, n, c, nbr, wtype, w1, c, b1, h);
+    orc_group_norm(h, n, c, sample, nsamples, groups, eps, gn_w, gn_b, h2);
+    orc_silu(h2, n * c);
+    orc_sparse_conv(h2, n, c, nbr, wtype, w2, c, b2, h);
+    for (int64_t i = 0; i < n * c; ++i) y[i] = h[i] + x[i];
+    free(h);
+    free(h2);
+}
+
 /* src/sparse.cpp:646-668 pool_down: sum of the slot gathers in slot order,
  * times inv_count, then linear. */
 void orc_pool_down(const float *x, int64_t nfine, int c, const int32_t *pool_rows, const float *inv_count, int64_t np,

@@ -59,6 +59,21 @@ void orc_silu(float *x, int64_t n);
 /* LN -> SiLU -> conv1 -> SiLU -> conv2 -> +x; weights as in orc_sparse_conv. */
 void orc_res_block(const float *x, int64_t n, int c, const int32_t *nbr, int wtype, const float *norm_w,
                    const float *norm_b, const void *w1, const float *b1, const void *w2, const float *b2, float *y);
+/* Sample-wide GroupNorm, restating ggml group_norm_f32
+ * (ggml-cpu/ops.cpp:4208-4283) on the [C, N] features viewed as [N, 1, C]
+ * per sample: per (sample, group of c/groups channels) the mean of all the
+ * sample's voxels' group values (double sum), then the variance of the
+ * float differences (double sum of float squares), y = (x - mean) *
+ * (1 / sqrtf(var + eps)), then the per-channel affine y * gamma + beta
+ * (ggml_mul, ggml_add; either may be NULL).  sample: [n] sample index of
+ * each voxel, 0 <= sample < nsamples.  No counterpart in mogecpp's
+ * refiner (its blocks use LayerNorm). */
+void orc_group_norm(const float *x, int64_t n, int c, const int32_t *sample, int nsamples, int groups, float eps,
+                    const float *gamma, const float *beta, float *y);
+/* conv1 -> GroupNorm -> SiLU -> conv2 -> +x (the GroupNorm block variant). */
+void orc_res_block_gn(const float *x, int64_t n, int c, const int32_t *nbr, const int32_t *sample, int nsamples,
+                      int groups, float eps, int wtype, const float *gn_w, const float *gn_b, const void *w1,
+                      const float *b1, const void *w2, const float *b2, float *y);
 /* mean over children (slot-major pool_rows, sentinel nfine) then linear. */
 void orc_pool_down(const float *x, int64_t nfine, int c, const int32_t *pool_rows, const float *inv_count, int64_t np,
                    int slots, int wtype, const void *w, int cout, const float *bias, float *y);

@@ -54,6 +54,10 @@ class Oracle:
                                     C.c_void_p, _f32p]
         L.orc_nearest_up.argtypes = [_f32p, _i64, C.c_int, _i32p, _i64, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                      _f32p]
+        L.orc_group_norm.argtypes = [_f32p, _i64, C.c_int, _i32p, C.c_int, C.c_int, C.c_float, C.c_void_p,
+                                     C.c_void_p, _f32p]
+        L.orc_res_block_gn.argtypes = [_f32p, _i64, C.c_int, _i32p, _i32p, C.c_int, C.c_int, C.c_float, C.c_int,
+                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, _f32p]
         L.orc_quantize_q8_0_ref.argtypes = [_f32p, C.c_void_p, _i64]
         L.orc_quantize_q8_0_act.argtypes = [_f32p, C.c_void_p, _i64]
         L.orc_fp32_to_fp16.argtypes = [C.c_float]
@@ -148,6 +152,29 @@ class Oracle:
                                _opt(p["b2"]), y)
         return y
 
+    def group_norm(self, x, sample, groups=32, eps=1e-5, gamma=None, beta=None):
+        """Sample-wide GroupNorm (ggml group_norm_f32 per sample, then affine)."""
+        x = _c(x, np.float32)
+        sample = _c(sample, np.int32)
+        y = np.empty_like(x)
+        ns = int(sample.max()) + 1 if sample.size else 1
+        self.lib.orc_group_norm(x, x.shape[0], x.shape[1], sample, ns, groups, eps, _opt(gamma), _opt(beta), y)
+        return y
+
+    def res_block_gn(self, x, nbr, sample, p: dict, wtype, groups=32, eps=1e-5):
+        """conv1 -> GroupNorm -> SiLU -> conv2 -> +x; p: gn_w, gn_b, w1, b1, w2, b2."""
+        x = _c(x, np.float32)
+        n, c = x.shape
+        sample = _c(sample, np.int32)
+        ns = int(sample.max()) + 1 if sample.size else 1
+        w1 = self.weight_payload(p["w1"], wtype, self)
+        w2 = self.weight_payload(p["w2"], wtype, self)
+        y = np.empty_like(x)
+        self.lib.orc_res_block_gn(x, n, c, _c(nbr, np.int32), sample, ns, groups, eps, wtype, _opt(p.get("gn_w")),
+                                  _opt(p.get("gn_b")), w1.ctypes.data_as(C.c_void_p), _opt(p["b1"]),
+                                  w2.ctypes.data_as(C.c_void_p), _opt(p["b2"]), y)
+        return y
+
     def pool_down(self, x, pool_rows, inv_count, w, wtype, bias=None):
         x = _c(x, np.float32)
         nfine, c = x.shape
@@ -188,6 +215,7 @@ class Reference:
                                     C.c_void_p, _f32p]
         L.ref_nearest_up.argtypes = [C.c_int, _f32p, _i64, _i64, _i32p, _i64, C.c_int, _f32p, _i64, C.c_void_p, _f32p]
         L.ref_topology_timed.argtypes = [_i32p, C.c_int32, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        L.ref_group_norm.argtypes = [C.c_int, _f32p, _i64, _i64, C.c_int, C.c_float, _f32p]
 
     def _check(self, rc):
         if rc != 0:
@@ -199,6 +227,13 @@ class Reference:
         if coords.shape[1] == 4 and coords.shape[0] and coords[:, 3].max() > 0:
             raise ValueError("the reference has no batch field; call it once per sample")
         return _c(coords[:, :3], np.int32)
+
+    def group_norm(self, x, groups=32, eps=1e-5):
+        """ggml_group_norm of one sample's [n, c] features (no affine)."""
+        x = _c(x, np.float32)
+        y = np.empty_like(x)
+        self._check(self.lib.ref_group_norm(self.n_threads, x, x.shape[0], x.shape[1], groups, eps, y))
+        return y
 
     def make_level(self, coords):
         c3 = self._xyz(coords)

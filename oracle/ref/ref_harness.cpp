@@ -366,6 +366,33 @@ int ref_nearest_up(int n_threads, const float * x, int64_t np, int64_t c, const 
 
 // Times make_level + downsample on the reference's topology threads
 // (MOGE_SPARSE_TOPOLOGY_THREADS governs the thread count, as in the reference).
+// ggml_group_norm (ggml.c:3233, CPU ops.cpp:4208-4283) of one sample's
+// features [C, N] viewed as [N, 1, C] (groups along channels), no affine.
+int ref_group_norm(int n_threads, const float * x, int64_t n, int64_t c, int groups, float eps, float * y) {
+    return guard([&] {
+        std::vector<float> one(1, 0.0f);
+        std::vector<MoggTensorSpec> specs;
+        specs.push_back(make_vec("unused.bias", one.data(), 1));
+        auto img = build_mogg(specs);
+        moge::MoggFile mf(img.data(), img.size(), true);
+        Runner r(n_threads);
+        moge::WeightStore ws(mf, r.cpu);
+        State s(4);
+        auto * tx = s.f32_2d(c, n);
+        auto * ty = s.f32_2d(c, n);
+        s.alloc(r.cpu);
+        ggml_backend_tensor_set(tx, x, 0, ggml_nbytes(tx));
+        run_graph(r, ws, ty, [&](ggml_context * g, const moge::WeightStore &) {
+            ggml_tensor * t = ggml_cont(g, ggml_transpose(g, tx));            // [N, C]
+            t = ggml_reshape_3d(g, t, n, 1, c);                               // [N, 1, C]
+            t = ggml_group_norm(g, t, groups, eps);
+            t = ggml_reshape_2d(g, t, n, c);                                  // [N, C]
+            return ggml_cont(g, ggml_transpose(g, t));                        // [C, N]
+        });
+        ggml_backend_tensor_get(ty, y, 0, ggml_nbytes(ty));
+    });
+}
+
 int ref_topology_timed(const int32_t * coords, int32_t n, int iters, double * make_level_s, double * downsample_s) {
     return guard([&] {
         auto cs = to_coords(coords, n);

@@ -6,7 +6,8 @@ oracle/ref/Makefile into oracle/_ref/libmoge_ref.so.  Run from the repo root
 in a checkout that has the reference tree next to it:
 
     make -f oracle/ref/Makefile REF=<path to mogecpp>
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py             # every fixture
+    python tests/golden/make_golden.py groupnorm   # groupnorm.npz only
 
 Fixtures are seeded synthetic inputs and the reference's outputs; the tests
 use them to pin the oracle port and the GPU path.  Inputs are rounded to
@@ -48,8 +49,26 @@ def topology_cases():
     return cases
 
 
+def groupnorm_fixture(R):
+    """ggml_group_norm (32 groups, eps 1e-5) of two samples' features, each
+    normalised over its own voxels (the reference has no GroupNorm block;
+    this pins the oracle's restatement of ggml's kernel)."""
+    rng = np.random.default_rng(80)
+    out = {}
+    for s, n in enumerate((300, 200)):
+        x = f16r(rng.standard_normal((n, 128)) * (1.5 + s) + 0.3 * s)
+        out[f"gn{s}_x"] = x
+        out[f"gn{s}_y"] = R.group_norm(x.astype(np.float32), 32, 1e-5)
+    np.savez_compressed(os.path.join(HERE, "groupnorm.npz"), **out)
+    print("groupnorm.npz", os.path.getsize(os.path.join(HERE, "groupnorm.npz")), "bytes")
+
+
 def main():
     R = Reference(n_threads=os.cpu_count() or 1)
+    if sys.argv[1:] == ["groupnorm"]:
+        groupnorm_fixture(R)
+        return
+    groupnorm_fixture(R)
     out = {}
     for name, c in topology_cases().items():
         c = np.ascontiguousarray(c, dtype=np.int32)

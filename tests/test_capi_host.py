@@ -52,6 +52,11 @@ def test_size_queries_are_host_only():
     assert lib.msc_conv_plan_bytes(1000) >= 1000 * 4 + 1000 * 27 * 2 + 4 * 1000 * 4
     assert lib.msc_conv_plan_bytes(-1) == 0
     assert lib.msc_conv_plan_workspace_bytes(1000) >= 1000 * 20
+    # GroupNorm statistics: 32 sums, 1 count, 32 squared deviations per sample
+    assert lib.msc_gn_stats_doubles(3) == 3 * 65
+    assert lib.msc_gn_stats_doubles(0) == 0
+    assert lib.msc_res_block_gn_workspace_bytes(1000, 128, 2) == lib.msc_op_workspace_bytes(1000, 128) + 512
+    assert lib.msc_res_block_gn_workspace_bytes(1000, 128, 0) == 0
 
 
 def test_create_fails_cleanly_without_sm100():
