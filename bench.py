@@ -50,10 +50,15 @@ sys.path.insert(0, ROOT)
 
 C_CH = 128
 METRIC = "active voxels/s per sparse conv"
+# block: the residual block each workload is quoted on: "ln" is the
+# reference's res_block (LayerNorm -> SiLU -> conv -> SiLU -> conv -> +x),
+# "gn" the GroupNorm(32) block (conv -> GroupNorm -> SiLU -> conv -> +x)
 WORKLOADS = {
-    "shell_4m": dict(blocks=8, coords="shell_4m_coords", grid=1024),
-    "res4_c128": dict(blocks=4, coords="res4_c128_coords", grid=256),
+    "shell_4m": dict(blocks=8, coords="shell_4m_coords", grid=1024, block="ln"),
+    "res4_c128": dict(blocks=4, coords="res4_c128_coords", grid=256, block="gn"),
 }
+GN_EPS = 1e-5
+BLOCK_NAME = {"ln": "LayerNorm res_block", "gn": "GroupNorm(32) res block"}
 PLAN_SORT_KERNELS = 8  # cub onesweep radix sort of 55-bit keys: histogram + 7 digit passes
 
 
@@ -77,13 +82,35 @@ def workload_inputs(name: str, rows=None):
     blocks = []
     for b in range(w["blocks"]):
         rng = np.random.default_rng(1000 + b)
-        blocks.append(dict(norm_w=(1 + 0.1 * rng.standard_normal(C_CH)).astype(np.float32),
-                           norm_b=(0.1 * rng.standard_normal(C_CH)).astype(np.float32),
-                           w1=synth.conv_weight(2000 + 2 * b, C_CH, C_CH),
-                           b1=(0.05 * rng.standard_normal(C_CH)).astype(np.float32),
-                           w2=synth.conv_weight(2001 + 2 * b, C_CH, C_CH),
-                           b2=(0.05 * rng.standard_normal(C_CH)).astype(np.float32)))
+        blk = dict(norm_w=(1 + 0.1 * rng.standard_normal(C_CH)).astype(np.float32),
+                   norm_b=(0.1 * rng.standard_normal(C_CH)).astype(np.float32),
+                   w1=synth.conv_weight(2000 + 2 * b, C_CH, C_CH),
+                   b1=(0.05 * rng.standard_normal(C_CH)).astype(np.float32),
+                   w2=synth.conv_weight(2001 + 2 * b, C_CH, C_CH),
+                   b2=(0.05 * rng.standard_normal(C_CH)).astype(np.float32))
+        blk["gn_w"], blk["gn_b"] = blk["norm_w"], blk["norm_b"]  # the one affine serves either norm
+        blocks.append(blk)
     return coords, x0, blocks
+
+
+def cpu_stack(impl, x, nbr, blocks, block_kind):
+    """One pass of the residual stack on the CPU: `impl` is the reference
+    build (Reference) or the oracle (Oracle).  Returns seconds."""
+    from oracle.oracle import Reference, W_Q8_0
+    is_ref = isinstance(impl, Reference)
+    if block_kind == "ln" and is_ref:
+        return impl.res_stack(x, nbr, blocks, W_Q8_0, iters=1)[1]
+    t0 = time.perf_counter()
+    h = x
+    sample = np.zeros(x.shape[0], np.int32)
+    for b in blocks:
+        if block_kind == "ln":
+            h = impl.res_block(h, nbr, b, W_Q8_0)
+        elif is_ref:
+            h = impl.res_block_gn(h, nbr, b, W_Q8_0, 32, GN_EPS)
+        else:
+            h = impl.res_block_gn(h, nbr, sample, b, W_Q8_0, 32, GN_EPS)
+    return time.perf_counter() - t0
 
 
 class ClockSampler:
@@ -138,30 +165,20 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_reference_sample(coords, x0, blocks, target_s: float, n_threads: int):
+def cpu_reference_sample(coords, x0, blocks, target_s: float, n_threads: int, block_kind: str):
     """Times the reference CPU res-block stack on the first voxels of the
     (b, z, y, x)-ordered set (a z-slab), sized to about target_s per run."""
-    from oracle.oracle import Oracle, Reference, W_Q8_0
+    from oracle.oracle import Oracle, Reference
     try:
         R = Reference(n_threads=n_threads)
         kind = "reference"
     except FileNotFoundError:
-        R = None
+        R = Oracle()
         kind = "port"
     ns = min(coords.shape[0], 4096)
     for _ in range(3):
-        sub = coords[:ns]
-        if R is not None:
-            nbr = R.make_level(sub)
-            _, sec = R.res_stack(x0[:ns].astype(np.float32), nbr, blocks, W_Q8_0, iters=1)
-        else:
-            O = Oracle()
-            nbr = O.make_level(sub)
-            t0 = time.perf_counter()
-            h = x0[:ns].astype(np.float32)
-            for b in blocks:
-                h = O.res_block(h, nbr, b, W_Q8_0)
-            sec = time.perf_counter() - t0
+        nbr = R.make_level(coords[:ns])
+        sec = cpu_stack(R, x0[:ns].astype(np.float32), nbr, blocks, block_kind)
         if sec >= 0.5 * target_s or ns == coords.shape[0]:
             break
         ns = int(min(coords.shape[0], ns * max(2.0, target_s / max(sec, 1e-3))))
@@ -179,38 +196,25 @@ def run_reference(args):
     coords = coords[:x0.shape[0]]
     convs = 2 * len(blocks)
     threads = os.cpu_count() or 1
-    from oracle.oracle import W_Q8_0
     per_step = min(8.0, 150.0 / max(1, args.steps + args.warmup))
-    R, kind, ns, _ = cpu_reference_sample(coords, x0, blocks, per_step, threads)
-    sub = coords[:ns]
-    times = []
-    if R is not None:
-        nbr = R.make_level(sub)
-        for i in range(args.warmup + args.steps):
-            t0 = time.perf_counter()
-            R.res_stack(x0[:ns].astype(np.float32), nbr, blocks, W_Q8_0, iters=1)
-            if i >= args.warmup:
-                times.append(time.perf_counter() - t0)
-    else:
-        from oracle.oracle import Oracle
-        O = Oracle()
-        nbr = O.make_level(sub)
+    R, kind, ns, _ = cpu_reference_sample(coords, x0, blocks, per_step, threads, args.block)
+    if kind == "port":
         threads = 1
-        for i in range(args.warmup + args.steps):
-            t0 = time.perf_counter()
-            h = x0[:ns].astype(np.float32)
-            for b in blocks:
-                h = O.res_block(h, nbr, b, W_Q8_0)
-            if i >= args.warmup:
-                times.append(time.perf_counter() - t0)
+    nbr = R.make_level(coords[:ns])
+    times = []
+    for i in range(args.warmup + args.steps):
+        sec = cpu_stack(R, x0[:ns].astype(np.float32), nbr, blocks, args.block)
+        if i >= args.warmup:
+            times.append(sec)
     t = sum(times) / len(times)
     value = ns * convs / t
-    sample = (f"first {ns} voxels of {args.workload} in (b,z,y,x) order (a z-slab), {len(blocks)} res blocks, "
-              "Q8_0")
+    sample = (f"first {ns} voxels of {args.workload} in (b,z,y,x) order (a z-slab), {len(blocks)} x "
+              f"{BLOCK_NAME[args.block]}, Q8_0")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "q8_0 x fp32 (ggml CPU)", "data": "synthetic",
-            "config": {"workload": args.workload, "voxels": int(ns), "channels": C_CH, "blocks": len(blocks)},
+            "config": {"workload": args.workload, "voxels": int(ns), "channels": C_CH, "blocks": len(blocks),
+                       "block": BLOCK_NAME[args.block]},
             "cpu_baseline": {"value": value, "unit": "voxels/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -248,6 +252,7 @@ def run_ours(args):
     blocks = []
     for b in blocks_np:
         blocks.append(dict(norm_w=torch.from_numpy(b["norm_w"]).to(dev), norm_b=torch.from_numpy(b["norm_b"]).to(dev),
+                           gn_w=torch.from_numpy(b["gn_w"]).to(dev), gn_b=torch.from_numpy(b["gn_b"]).to(dev),
                            b1=torch.from_numpy(b["b1"]).to(dev), b2=torch.from_numpy(b["b2"]).to(dev),
                            w1=ex.prepare_weight(torch.from_numpy(synth.quantize_q8_0(b["w1"])).to(dev), "q8_0",
                                                 C_CH, C_CH, 27),
@@ -257,12 +262,19 @@ def run_ours(args):
     cached = args.conv == "cached"
     plan_kind = {"cached": "row_cache", "ordered": "tap_order"}.get(args.conv)
 
+    # GroupNorm statistics are sample-wide: summed over the slabs (NCCL)
+    gn_allreduce = (lambda t: dist.all_reduce(t)) if world > 1 else None
+
     def step():
         nbr = ex.make_level(coords_d)
         plan = ex.conv_plan(coords_d, nbr, plan_kind) if plan_kind else None
         for blk in blocks:
             halo.exchange(x_d)
-            ex.res_block(x_d, None if cached else nbr, blk, plan=plan)
+            if args.block == "gn":
+                ex.res_block_gn(x_d, None if cached else nbr, coords_d, 1, blk, eps=GN_EPS, plan=plan,
+                                n_stat=part.n_owned, allreduce=gn_allreduce)
+            else:
+                ex.res_block(x_d, None if cached else nbr, blk, plan=plan)
         return nbr
 
     def barrier():
@@ -347,10 +359,11 @@ def run_ours(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            R, kind, ns, sec = cpu_reference_sample(coords, lx0, blocks_np, 6.0, os.cpu_count() or 1)
+            R, kind, ns, sec = cpu_reference_sample(coords, lx0, blocks_np, 6.0, os.cpu_count() or 1, args.block)
             cpu = {"value": ns * convs / sec, "unit": "voxels/s",
                    "cores": (os.cpu_count() or 1) if kind == "reference" else 1, "kind": kind,
-                   "sample": f"first {ns} voxels in (b,z,y,x) order (a z-slab), one {len(blocks_np)}-block stack run"}
+                   "sample": f"first {ns} voxels in (b,z,y,x) order (a z-slab), one run of {len(blocks_np)} x "
+                             f"{BLOCK_NAME[args.block]}"}
         line = {
             "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "strong",
@@ -360,8 +373,10 @@ def run_ours(args):
             "config": {"workload": args.workload, "voxels": n, "channels": C_CH, "blocks": len(blocks_np),
                        "convs_per_step": convs, "grid": WORKLOADS[args.workload]["grid"],
                        "rank0_local_voxels": nl, "rank0_valid_pairs": e_pairs,
+                       "block": BLOCK_NAME[args.block],
                        "step": (f"make_level + {plan_kind} plan + " if plan_kind else "make_level + ") +
-                               f"{len(blocks_np)} res blocks" + (" (halo exchange before each)" if world > 1 else ""),
+                               f"{len(blocks_np)} res blocks" + (" (halo exchange before each)" if world > 1 else "") +
+                               (", GroupNorm statistics all-reduced" if world > 1 and args.block == "gn" else ""),
                        "conv": args.conv, "l2": "flushed between steps (256 MiB write)",
                        "parallelism": f"z-slabs x{world}, 2-plane halo over NCCL" if world > 1 else "single GPU"},
             "e2e": {"value": n * convs / (e2e_t * 1e-3), "unit": "voxels/s",
@@ -393,7 +408,11 @@ def main():
     ap.add_argument("--workload", default="shell_4m", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--conv", default="ordered", choices=["ordered", "direct", "cached"])
+    ap.add_argument("--block", default=None, choices=["ln", "gn"],
+                    help="residual block (default: the one the workload is quoted on)")
     args = ap.parse_args()
+    if args.block is None:
+        args.block = WORKLOADS[args.workload]["block"]
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -599,7 +599,10 @@ int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_s
         }
         reduce(stats + ns * 33, ns * 32, "deviations");
         if (n == 0) return;
-        cuda_ok(msc::launch_gn_finalize(stats, c, nsamples, eps, gn, st), "GroupNorm finalize");
+        {
+            ProfScope ps(ctx, "gn_finalize", st);
+            cuda_ok(msc::launch_gn_finalize(stats, c, nsamples, eps, gn, st), "GroupNorm finalize");
+        }
         // GroupNorm + SiLU fused into conv2's operand preparation, then
         // conv2 + b2 + x into x
         const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2.cached != nullptr);

@@ -262,6 +262,19 @@ class Reference:
                                              _c(w, np.float32), w.shape[0], _opt(bias), y))
         return y
 
+    def res_block_gn(self, x, nbr, p: dict, wtype, groups=32, eps=1e-5):
+        """One sample's GroupNorm residual block composed from the reference's
+        sparse conv and ggml_group_norm: x + conv2(SiLU(GN(conv1(x) + b1) *
+        gn_w + gn_b)) + b2 (affine, SiLU and skip in float32 numpy)."""
+        x = _c(x, np.float32)
+        h = self.group_norm(self.sparse_conv(x, nbr, p["w1"], wtype, p["b1"]), groups, eps)
+        if p.get("gn_w") is not None:
+            h = h * p["gn_w"]
+        if p.get("gn_b") is not None:
+            h = h + p["gn_b"]
+        h = h / (np.float32(1.0) + np.exp(-h))
+        return self.sparse_conv(h, nbr, p["w2"], wtype, p["b2"]) + x
+
     def res_stack(self, x, nbr, blocks: list, wtype, iters=0):
         """Runs len(blocks) reference res_blocks; returns (y, median seconds)."""
         x = _c(x, np.float32)

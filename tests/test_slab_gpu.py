@@ -1,5 +1,6 @@
 """Z-slab residual stack on two GPUs: one process per GPU, NCCL halo
-exchange before each Q8_0 residual block (mogecpp_b200/slab.py).  The owned
+exchange before each Q8_0 residual block (mogecpp_b200/slab.py); for the
+GroupNorm block the sample-wide statistics are also all-reduced over NCCL.  The owned
 rows of the two ranks are compared with the single-GPU stack over the whole
 set and with the oracle.  The runs differ only in the fp32 summation order
 of the conv tiles, which the fp16 state and the Q8_0 re-quantisation of
@@ -23,13 +24,15 @@ def _coords():
 
 def _raw_block(seed, c):
     rng = np.random.default_rng(seed)
-    return dict(norm_w=(1 + 0.1 * rng.standard_normal(c)).astype(np.float32),
-                norm_b=(0.1 * rng.standard_normal(c)).astype(np.float32),
-                w1=synth.conv_weight(seed + 1, c, c), b1=(0.05 * rng.standard_normal(c)).astype(np.float32),
-                w2=synth.conv_weight(seed + 2, c, c), b2=(0.05 * rng.standard_normal(c)).astype(np.float32))
+    r = dict(norm_w=(1 + 0.1 * rng.standard_normal(c)).astype(np.float32),
+             norm_b=(0.1 * rng.standard_normal(c)).astype(np.float32),
+             w1=synth.conv_weight(seed + 1, c, c), b1=(0.05 * rng.standard_normal(c)).astype(np.float32),
+             w2=synth.conv_weight(seed + 2, c, c), b2=(0.05 * rng.standard_normal(c)).astype(np.float32))
+    r["gn_w"], r["gn_b"] = r["norm_w"], r["norm_b"]
+    return r
 
 
-def _stack(ex, coords_np, x_np, world=1, part=None, exchange=None, plan_kind=None):
+def _stack(ex, coords_np, x_np, block, world=1, part=None, exchange=None, plan_kind=None):
     import torch
     from mogecpp_b200.synth import quantize_q8_0
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -40,17 +43,23 @@ def _stack(ex, coords_np, x_np, world=1, part=None, exchange=None, plan_kind=Non
     for blk in range(2):
         raw = _raw_block(340 + blk, 128)
         b = dict(norm_w=torch.from_numpy(raw["norm_w"]).to(dev), norm_b=torch.from_numpy(raw["norm_b"]).to(dev),
+                 gn_w=torch.from_numpy(raw["gn_w"]).to(dev), gn_b=torch.from_numpy(raw["gn_b"]).to(dev),
                  b1=torch.from_numpy(raw["b1"]).to(dev), b2=torch.from_numpy(raw["b2"]).to(dev),
                  w1=ex.prepare_weight(torch.from_numpy(quantize_q8_0(raw["w1"])).to(dev), "q8_0", 128, 128, 27),
                  w2=ex.prepare_weight(torch.from_numpy(quantize_q8_0(raw["w2"])).to(dev), "q8_0", 128, 128, 27))
         if exchange is not None:
             exchange.exchange(x)
-        ex.res_block(x, nbr, b, plan=plan)
+        if block == "gn":
+            import torch.distributed as dist
+            ex.res_block_gn(x, nbr, cd, 1, b, plan=plan, n_stat=part.n_owned if part else None,
+                            allreduce=(lambda t: dist.all_reduce(t)) if world > 1 else None)
+        else:
+            ex.res_block(x, nbr, b, plan=plan)
     ex.check()
     return x.float().cpu().numpy()
 
 
-def _rank_main(rank, world, port, out_path):
+def _rank_main(rank, world, port, out_path, block):
     import torch
     import torch.distributed as dist
     from mogecpp_b200.sparse import SparseCudaExecutor
@@ -64,7 +73,7 @@ def _rank_main(rank, world, port, out_path):
         part = slab.partition(coords, world)[rank]
         rows = part.local_rows()
         x = synth.features_rows(331, rows, 128, np.float16)
-        y = _stack(ex, np.ascontiguousarray(coords[rows]), x, world, part, slab.SlabExchange(part, world),
+        y = _stack(ex, np.ascontiguousarray(coords[rows]), x, block, world, part, slab.SlabExchange(part, world),
                    plan_kind="tap_order")
         np.save(out_path, y[:part.n_owned])
         dist.barrier()
@@ -80,7 +89,8 @@ def _free_port():
     return port
 
 
-def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle):
+@pytest.mark.parametrize("block", ["ln", "gn"])
+def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle, block):
     import multiprocessing as mp
     import torch
     from conftest import max_abs, rel_l2
@@ -91,7 +101,7 @@ def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle):
     ctx = mp.get_context("spawn")
     port = _free_port()
     outs = [str(tmp_path / f"rank{r}.npy") for r in range(world)]
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, outs[r])) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, outs[r], block)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -100,7 +110,7 @@ def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle):
     got = np.concatenate([np.load(o) for o in outs])
     coords = _coords()
     x = synth.features(331, coords.shape[0], 128, np.float16)
-    single = _stack(ex, coords, x)
+    single = _stack(ex, coords, x, block)
     assert rel_l2(got, single) < 1e-3 and max_abs(got, single) < 3e-2, (rel_l2(got, single), max_abs(got, single))
     # rows of the two planes on either side of the cut
     cut = slab.partition(coords, world)[1].lo
@@ -110,5 +120,8 @@ def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle):
     nbr = oracle.make_level(coords)
     h = x.astype(np.float32)
     for blk in range(2):
-        h = oracle.res_block(h, nbr, _raw_block(340 + blk, 128), W_Q8_0).astype(np.float16).astype(np.float32)
+        raw = _raw_block(340 + blk, 128)
+        h = (oracle.res_block_gn(h, nbr, coords[:, 3], raw, W_Q8_0) if block == "gn"
+             else oracle.res_block(h, nbr, raw, W_Q8_0))
+        h = h.astype(np.float16).astype(np.float32)
     assert rel_l2(got, h) < 3e-3 and max_abs(got, h) < 3e-2
