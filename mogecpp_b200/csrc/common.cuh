@@ -224,6 +224,12 @@ __device__ __forceinline__ void tmem_st8_fill(uint32_t taddr, uint32_t v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Two 64-bit words from shared memory (shared-window address), e.g. two f32
+// pairs for the f32x2 arithmetic.
+__device__ __forceinline__ void lds_2x64(uint32_t saddr, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(saddr));
+}
+
 // tcgen05.wait::ld that also names the registers of the awaited load as
 // read-write, so that the compiler cannot move their uses above the wait.
 template <int N>

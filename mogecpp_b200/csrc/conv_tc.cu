@@ -12,8 +12,10 @@
 // swizzled, K-major.  Three arithmetic kinds:
 //   * KIND_Q8I (ggml Q8_0 weights, cin = 128): A = the activation's int8
 //     Q8_0 codes, B = the weight's int8 codes; one kind::i8 MMA per
-//     32-channel block gives the exact int32 block dot product isum; the
-//     drain warps apply ggml's per-block scale
+//     32-channel block gives the exact int32 block dot product isum (two
+//     blocks side by side in one accumulator slot, so that a slot's wait,
+//     commit and release serve two blocks); the drain warps apply ggml's
+//     per-block scale
 //         acc += (d_a * d_w) * isum       (ggml-cpu x86 quants.c:1308)
 //   * KIND_Q8F (ggml Q8_0 weights, cin = 64): A = the int8 codes as fp16,
 //     B = the exact hi/lo fp16 pair of the prescaled weight d_w * q_w; one
@@ -69,10 +71,14 @@ struct Cfg {
     static constexpr int B_PLANE = COUT * 128;
     static constexpr int STAGE = NA * A_PLANE + NB * B_PLANE;
     // accumulator groups per stage and MMA k-steps (32 bytes of K) per group
-    static constexpr int GPS = KIND == KIND_Q8I ? 4 : (KIND == KIND_Q8F ? 2 : 1);
-    static constexpr int KSPG = 4 / GPS;
-    static constexpr int NACC = (512 / COUT) < 4 ? (512 / COUT) : 4;
-    static constexpr int TMEM_COLS = NACC * COUT;
+    // Q8I: BPG = 2 block sums side by side in one accumulator slot, so that a
+    // slot's wait, commit and release are paid once per two blocks
+    static constexpr int BPG = KIND == KIND_Q8I ? 2 : 1;
+    static constexpr int GPS = KIND == KIND_Q8I ? 4 / BPG : (KIND == KIND_Q8F ? 2 : 1);
+    static constexpr int KSPG = KIND == KIND_Q8I ? 1 : 4 / GPS;  // MMA k-steps per block (Q8I) or group
+    static constexpr int SLOT = BPG * COUT;                        // TMEM columns per slot
+    static constexpr int NACC = (512 / SLOT) < 4 ? (512 / SLOT) : 4;
+    static constexpr int TMEM_COLS = NACC * SLOT;
     static constexpr int COLS = COUT / (kDrainWarps / 4);  // columns per drain thread
     static constexpr int NBR_BYTES = 2 * BM * 27 * 4;
     static constexpr int ROWS_BYTES = 2 * BM * 4;
@@ -267,15 +273,22 @@ __device__ void mma_issuer(const ConvArgs& a, const Smem& S, int64_t ntiles, uin
                                    a.status))
                     return;
                 tc_fence_after();
-                const uint32_t d = tmem + static_cast<uint32_t>(slot * COUT);
+                const uint32_t d = tmem + static_cast<uint32_t>(slot * C::SLOT);
+                if (KIND == KIND_Q8I) {
+                    // one k-step per block, each block into its own columns
 #pragma unroll
-                for (int ks = 0; ks < C::KSPG; ++ks) {
+                    for (int b = 0; b < C::BPG; ++b) {
+                        const uint32_t off = static_cast<uint32_t>((gg * C::BPG + b) * 32);
+                        umma_i8(d + static_cast<uint32_t>(b * COUT), sdesc_k_sw128(aaddr + off),
+                                sdesc_k_sw128(baddr + off), idesc, 0u);
+                    }
+                }
+#pragma unroll
+                for (int ks = 0; ks < (KIND == KIND_Q8I ? 0 : C::KSPG); ++ks) {
                     const uint32_t off = static_cast<uint32_t>((gg * C::KSPG + ks) * 32);
                     const uint64_t ah = sdesc_k_sw128(aaddr + off);
                     const uint64_t bh = sdesc_k_sw128(baddr + off);
-                    if (KIND == KIND_Q8I) {
-                        umma_i8(d, ah, bh, idesc, ks > 0 ? 1u : 0u);
-                    } else {
+                    {
                         umma_f16(d, ah, bh, idesc, ks > 0 ? 1u : 0u);
                         if (NB == 2) umma_f16(d, ah, sdesc_k_sw128(baddr + C::B_PLANE + off), idesc, 1u);
                         if (NA == 2) umma_f16(d, sdesc_k_sw128(aaddr + C::A_PLANE + off), bh, idesc, 1u);
@@ -340,56 +353,60 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
             }
 #pragma unroll 1
             for (int grp = 0; grp < C::KCH * C::GPS; ++grp, ++g) {
-                // this group's activation block scale (select chain keeps sa in registers)
-                float sg = 0.f;
-                if (Q8) {
-                    sg = sa[0];
-#pragma unroll
-                    for (int b = 1; b < C::NBLK; ++b) sg = grp == b ? sa[b] : sg;
-                }
                 const int slot = static_cast<int>(g % C::NACC);
                 if (!wait_or_abort(&S.acc_full[slot], static_cast<uint32_t>(g / C::NACC) & 1, S.abort, a.status))
                     return;
                 tc_fence_after();
-                // CH columns at a time: load, wait, accumulate; release the slot
-                // after the last load has landed
 #pragma unroll
-                for (int c = 0; c < COLS; c += CH) {
-                    uint32_t d[CH];
-                    tmem_ld<CH>(tmem + lane_addr + static_cast<uint32_t>(slot * COUT + c_base + c), d);
-                    tmem_wait_ld_regs(d);
-                    if (c + CH == COLS) {
-                        tc_fence_before();
-                        warp_arrive(&S.acc_empty[slot]);
+                for (int b = 0; b < C::BPG; ++b) {
+                    const int kb = grp * C::BPG + b;  // 32-channel block (Q8 kinds)
+                    // this block's activation scale (select chain keeps sa in registers)
+                    float sg = 0.f;
+                    if (Q8) {
+                        sg = sa[0];
+#pragma unroll
+                        for (int bb = 1; bb < C::NBLK; ++bb) sg = kb == bb ? sa[bb] : sg;
                     }
-                    if (KIND == KIND_Q8I) {
-                        // acc += (d_a * d_w[n]) * isum[n]: (isum * d_a) is rounded once
-                        // by an FMA that also removes the conversion offset, then
-                        // fused into the accumulator with d_w[n]
-                        const uint64_t s2 = pack2(sg, sg);
-                        const uint64_t off2 = pack2(-kMagic * sg, -kMagic * sg);
-                        const float4* sb = reinterpret_cast<const float4*>(
-                            S.sB + (tap * C::NBLK + grp) * COUT + c_base + c);
+                    // CH columns at a time: load, wait, accumulate; release the slot
+                    // after the last load has landed
 #pragma unroll
-                        for (int e = 0; e < CH / 4; ++e) {
-                            const float4 w = sb[e];
-                            const uint64_t f0 = pack2(__int_as_float(static_cast<int>(d[4 * e]) + kMagicBits),
-                                                      __int_as_float(static_cast<int>(d[4 * e + 1]) + kMagicBits));
-                            const uint64_t f1 = pack2(__int_as_float(static_cast<int>(d[4 * e + 2]) + kMagicBits),
-                                                      __int_as_float(static_cast<int>(d[4 * e + 3]) + kMagicBits));
-                            acc[c / 2 + 2 * e] = fma2(fma2(f0, s2, off2), pack2(w.x, w.y), acc[c / 2 + 2 * e]);
-                            acc[c / 2 + 2 * e + 1] = fma2(fma2(f1, s2, off2), pack2(w.z, w.w), acc[c / 2 + 2 * e + 1]);
+                    for (int c = 0; c < COLS; c += CH) {
+                        uint32_t d[CH];
+                        tmem_ld<CH>(tmem + lane_addr + static_cast<uint32_t>(slot * C::SLOT + b * COUT + c_base + c), d);
+                        tmem_wait_ld_regs(d);
+                        if (b + 1 == C::BPG && c + CH == COLS) {
+                            tc_fence_before();
+                            warp_arrive(&S.acc_empty[slot]);
                         }
-                    } else if (KIND == KIND_Q8F) {
-                        const uint64_t s2 = pack2(sg, sg);
+                        if (KIND == KIND_Q8I) {
+                            // acc += (d_a * d_w[n]) * isum[n]: (isum * d_a) is rounded once
+                            // by an FMA that also removes the conversion offset, then
+                            // fused into the accumulator with d_w[n]
+                            const uint64_t s2 = pack2(sg, sg);
+                            const uint64_t off2 = pack2(-kMagic * sg, -kMagic * sg);
+                            const uint32_t sb = smem_u32(S.sB + (tap * C::NBLK + kb) * COUT + c_base + c);
 #pragma unroll
-                        for (int e = 0; e < CH / 2; ++e)
-                            acc[c / 2 + e] =
-                                fma2(pack2(__uint_as_float(d[2 * e]), __uint_as_float(d[2 * e + 1])), s2, acc[c / 2 + e]);
-                    } else {
+                            for (int e = 0; e < CH / 4; ++e) {
+                                uint64_t w01, w23;
+                                lds_2x64(sb + 16 * e, w01, w23);
+                                const uint64_t f0 = pack2(__int_as_float(static_cast<int>(d[4 * e]) + kMagicBits),
+                                                          __int_as_float(static_cast<int>(d[4 * e + 1]) + kMagicBits));
+                                const uint64_t f1 = pack2(__int_as_float(static_cast<int>(d[4 * e + 2]) + kMagicBits),
+                                                          __int_as_float(static_cast<int>(d[4 * e + 3]) + kMagicBits));
+                                acc[c / 2 + 2 * e] = fma2(fma2(f0, s2, off2), w01, acc[c / 2 + 2 * e]);
+                                acc[c / 2 + 2 * e + 1] = fma2(fma2(f1, s2, off2), w23, acc[c / 2 + 2 * e + 1]);
+                            }
+                        } else if (KIND == KIND_Q8F) {
+                            const uint64_t s2 = pack2(sg, sg);
 #pragma unroll
-                        for (int e = 0; e < CH / 2; ++e)
-                            acc[c / 2 + e] = add2(acc[c / 2 + e], pack2(__uint_as_float(d[2 * e]), __uint_as_float(d[2 * e + 1])));
+                            for (int e = 0; e < CH / 2; ++e)
+                                acc[c / 2 + e] =
+                                    fma2(pack2(__uint_as_float(d[2 * e]), __uint_as_float(d[2 * e + 1])), s2, acc[c / 2 + e]);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < CH / 2; ++e)
+                                acc[c / 2 + e] = add2(acc[c / 2 + e], pack2(__uint_as_float(d[2 * e]), __uint_as_float(d[2 * e + 1])));
+                        }
                     }
                 }
             }

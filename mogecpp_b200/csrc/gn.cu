@@ -13,15 +13,17 @@
 //   [nsamples * 32] group sums | [nsamples] voxel counts | [nsamples * 32] squared deviations
 //
 // One warp per chunk of rows; lane l holds the C/32 channels of group l, so
-// a lane accumulates one group and flushes it with one double atomic add
-// whenever the row's sample changes (rows are normally sorted by sample).
+// a lane accumulates one group (each value added in double, as ggml) and
+// flushes it with one double atomic add whenever the row's sample changes
+// (rows are normally sorted by sample).
 #include "common.cuh"
 #include "gn.h"
 
 namespace msc {
 namespace {
 
-constexpr int kRowsPerWarp = 64;
+constexpr int kRowsPerWarp = 128;
+constexpr int kUnroll = 8;
 
 template <int C>
 __device__ __forceinline__ void load_group(const float* x, int64_t row, int lane, float (&v)[C / 32]) {
@@ -48,82 +50,80 @@ __device__ __forceinline__ int sample_of(const int4* coords, int64_t row, int ns
     return b;
 }
 
-// pass 1: group sums and voxel counts of rows [0, n_stat); the sample
-// index of rows [n_stat, n) (halo rows, normalised but not counted) is only
-// validated
-template <int C>
-__global__ void gn_sum_kernel(const float* __restrict__ x, const int4* __restrict__ coords, int64_t n,
-                              int64_t n_stat, int nsamples, double* stats, uint32_t* status) {
+// PASS 1: group sums and voxel counts of rows [0, n_stat), and the sample
+// index of rows [n_stat, n) (halo rows, normalised but not counted) checked.
+// PASS 2: squared deviations from the complete group means.
+// A warp takes kRowsPerWarp consecutive rows: their sample indices are read
+// 32 at a time (one per lane) and their features kUnroll rows at a time, all
+// loads in flight before the first row is accumulated.
+template <int C, int PASS>
+__global__ void gn_pass_kernel(const float* __restrict__ x, const int4* __restrict__ coords, int64_t n,
+                               int64_t n_stat, int nsamples, double* stats, uint32_t* status) {
+    constexpr int EPL = C / 32;
     const int lane = threadIdx.x & 31;
     const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
     const int64_t r0 = warp * kRowsPerWarp;
     if (r0 >= n) return;
-    const int64_t r2 = r0 + kRowsPerWarp < n ? r0 + kRowsPerWarp : n;
-    if (lane == 0)
-        for (int64_t r = r0 > n_stat ? r0 : n_stat; r < r2; ++r) sample_of(coords, r, nsamples, status);
+    if (PASS == 1) {
+        const int64_t r2 = r0 + kRowsPerWarp < n ? r0 + kRowsPerWarp : n;
+        for (int64_t r = (r0 > n_stat ? r0 : n_stat) + lane; r < r2; r += 32) sample_of(coords, r, nsamples, status);
+    }
     if (r0 >= n_stat) return;
     const int64_t r1 = r0 + kRowsPerWarp < n_stat ? r0 + kRowsPerWarp : n_stat;
     double* sums = stats;
     double* counts = stats + static_cast<int64_t>(nsamples) * 32;
-    int cur = -1;
-    double acc = 0.0, cnt = 0.0;
-    for (int64_t r = r0; r < r1; ++r) {
-        const int b = sample_of(coords, r, nsamples, status);
-        if (b < 0) continue;
-        if (b != cur) {
-            if (cur >= 0) {
-                atomicAdd(sums + cur * 32 + lane, acc);
-                if (lane == 0) atomicAdd(counts + cur, cnt);
-            }
-            cur = b, acc = 0.0, cnt = 0.0;
-        }
-        float v[C / 32];
-        load_group<C>(x, r, lane, v);
-        double s = 0.0;
-#pragma unroll
-        for (int k = 0; k < C / 32; ++k) s += static_cast<double>(v[k]);
-        acc += s;
-        cnt += 1.0;
-    }
-    if (cur >= 0) {
-        atomicAdd(sums + cur * 32 + lane, acc);
-        if (lane == 0) atomicAdd(counts + cur, cnt);
-    }
-}
-
-// pass 2: squared deviations from the group means
-template <int C>
-__global__ void gn_sq_kernel(const float* __restrict__ x, const int4* __restrict__ coords, int64_t n_stat,
-                             int nsamples, double* stats, uint32_t* status) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-    const int64_t r0 = warp * kRowsPerWarp;
-    if (r0 >= n_stat) return;
-    const int64_t r1 = r0 + kRowsPerWarp < n_stat ? r0 + kRowsPerWarp : n_stat;
-    const double* sums = stats;
-    const double* counts = stats + static_cast<int64_t>(nsamples) * 32;
     double* sq = stats + static_cast<int64_t>(nsamples) * 33;
     int cur = -1;
     float mean = 0.0f;
-    double acc = 0.0;
-    for (int64_t r = r0; r < r1; ++r) {
-        const int b = sample_of(coords, r, nsamples, status);
-        if (b < 0) continue;
-        if (b != cur) {
-            if (cur >= 0) atomicAdd(sq + cur * 32 + lane, acc);
-            cur = b, acc = 0.0;
-            const double cnt = counts[b] * (C / 32);
-            mean = cnt > 0.0 ? static_cast<float>(sums[b * 32 + lane] / cnt) : 0.0f;
-        }
-        float v[C / 32];
-        load_group<C>(x, r, lane, v);
+    double acc = 0.0, cnt = 0.0;
+    for (int64_t base = r0; base < r1; base += 32) {
+        const int m = r1 - base < 32 ? static_cast<int>(r1 - base) : 32;
+        const int bl = lane < m ? sample_of(coords, base + lane, nsamples, PASS == 1 ? status : nullptr) : -1;
+        for (int j = 0; j < m; j += kUnroll) {
+            float v[kUnroll][EPL];
 #pragma unroll
-        for (int k = 0; k < C / 32; ++k) {
-            const float d = v[k] - mean;
-            acc += static_cast<double>(d * d);
+            for (int u = 0; u < kUnroll; ++u)
+                if (j + u < m) load_group<C>(x, base + j + u, lane, v[u]);
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int b = __shfl_sync(0xffffffffu, bl, (j + u) & 31);
+                if (j + u >= m || b < 0) continue;
+                if (b != cur) {
+                    if (cur >= 0) {
+                        if (PASS == 1) {
+                            atomicAdd(sums + cur * 32 + lane, acc);
+                            if (lane == 0) atomicAdd(counts + cur, cnt);
+                        } else {
+                            atomicAdd(sq + cur * 32 + lane, acc);
+                        }
+                    }
+                    cur = b, acc = 0.0, cnt = 0.0;
+                    if (PASS == 2) {
+                        const double c = counts[b] * EPL;
+                        mean = c > 0.0 ? static_cast<float>(sums[b * 32 + lane] / c) : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < EPL; ++k) {
+                    if (PASS == 1) {
+                        acc += static_cast<double>(v[u][k]);
+                    } else {
+                        const float d = v[u][k] - mean;
+                        acc += static_cast<double>(d * d);
+                    }
+                }
+                cnt += 1.0;
+            }
         }
     }
-    if (cur >= 0) atomicAdd(sq + cur * 32 + lane, acc);
+    if (cur >= 0) {
+        if (PASS == 1) {
+            atomicAdd(sums + cur * 32 + lane, acc);
+            if (lane == 0) atomicAdd(counts + cur, cnt);
+        } else {
+            atomicAdd(sq + cur * 32 + lane, acc);
+        }
+    }
 }
 
 // mean and 1 / sqrtf(var + eps) per (sample, group)
@@ -146,9 +146,9 @@ cudaError_t launch_pass(int pass, const float* x, const int32_t* coords, int64_t
     const int4* c4 = reinterpret_cast<const int4*>(coords);
     if (grid == 0) return cudaSuccess;
     if (pass == 1)
-        gn_sum_kernel<C><<<grid, 256, 0, st>>>(x, c4, n, n_stat, nsamples, stats, status);
+        gn_pass_kernel<C, 1><<<grid, 256, 0, st>>>(x, c4, n, n_stat, nsamples, stats, status);
     else
-        gn_sq_kernel<C><<<grid, 256, 0, st>>>(x, c4, n_stat, nsamples, stats, status);
+        gn_pass_kernel<C, 2><<<grid, 256, 0, st>>>(x, c4, n, n_stat, nsamples, stats, status);
     return cudaGetLastError();
 }
 

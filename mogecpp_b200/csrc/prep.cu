@@ -190,17 +190,11 @@ __device__ __forceinline__ void store_halves(__half* dst, const __half (&h)[EPL]
     }
 }
 
-// One warp per row; lane l holds channels [l*EPL, (l+1)*EPL), read and
-// written with one vector access each where the width allows.
+// Rows are prepared by warps; lane l holds channels [l*EPL, (l+1)*EPL),
+// read and written with one vector access each where the width allows.
 template <int C>
-__global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
-                                   const float* beta, float eps, int silu, int mode, __half* planes,
-                                   const float2* gn, const int4* coords, int nsamples) {
+__device__ __forceinline__ void load_row(const void* x, int x_dtype, int64_t row, int lane, float (&v)[C / 32]) {
     constexpr int EPL = C / 32;
-    const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (row >= n) return;
-    float v[EPL];
     const int64_t base = row * C + lane * EPL;
     if (x_dtype == DT_F32) {
         if constexpr (EPL >= 4) {
@@ -224,6 +218,15 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
         v[0] = x_dtype == DT_F16 ? __half2float(static_cast<const __half*>(x)[base])
                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base]);
     }
+}
+
+// Normalisation, SiLU and the operand output of one row (warp-uniform row).
+template <int C>
+__device__ __forceinline__ void prepare_row(float (&v)[C / 32], int64_t row, int lane, int64_t n, int ln,
+                                            const float* gamma, const float* beta, float eps, int silu, int mode,
+                                            __half* planes, const float2* gn, const int4* coords, int nsamples) {
+    constexpr int EPL = C / 32;
+    const int64_t base = row * C + lane * EPL;
     if (gn) {
         // GroupNorm with 32 groups: lane l holds group l; ggml order
         // ((x - mean) * scale, then * gamma, then + beta)
@@ -316,6 +319,27 @@ __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln
     store_halves<EPL>(planes + plane + base, lo);
 }
 
+// kRowsPerPrepWarp consecutive rows per warp, all loads issued before the
+// first row is processed (several 512-byte rows in flight per warp).
+constexpr int kRowsPerPrepWarp = 4;
+
+template <int C>
+__global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
+                                   const float* beta, float eps, int silu, int mode, __half* planes,
+                                   const float2* gn, const int4* coords, int nsamples) {
+    const int64_t r0 = ((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5) * kRowsPerPrepWarp;
+    const int lane = threadIdx.x & 31;
+    if (r0 >= n) return;
+    float v[kRowsPerPrepWarp][C / 32];
+#pragma unroll
+    for (int j = 0; j < kRowsPerPrepWarp; ++j)
+        if (r0 + j < n) load_row<C>(x, x_dtype, r0 + j, lane, v[j]);
+#pragma unroll
+    for (int j = 0; j < kRowsPerPrepWarp; ++j)
+        if (r0 + j < n)
+            prepare_row<C>(v[j], r0 + j, lane, n, ln, gamma, beta, eps, silu, mode, planes, gn, coords, nsamples);
+}
+
 }  // namespace
 
 bool weight_is_i8(int wtype, int cin) { return wtype == WT_Q8_0 && cin == 128; }
@@ -387,7 +411,8 @@ cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int
                                const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st,
                                const float2* gn, const int32_t* coords, int nsamples) {
     if (n == 0) return cudaSuccess;
-    const unsigned grid = static_cast<unsigned>((n * 32 + 255) / 256);
+    const int64_t warps = (n + kRowsPerPrepWarp - 1) / kRowsPerPrepWarp;
+    const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
     auto* out = static_cast<__half*>(planes);
     const int4* c4 = reinterpret_cast<const int4*>(coords);
     if (gn && (c % 32 != 0 || !coords || nsamples < 1)) return cudaErrorInvalidValue;
