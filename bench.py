@@ -59,6 +59,11 @@ WORKLOADS = {
 }
 GN_EPS = 1e-5
 BLOCK_NAME = {"ln": "LayerNorm res_block", "gn": "GroupNorm(32) res block"}
+# DRAM bytes per voxel of one sparse-conv launch, by residual-block kind:
+# dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of a
+# block's two convs on res4_c128, averaged (profiles/conv_traffic_res4_c128.md).
+# Other workloads scale it by the voxels a launch processes.
+CONV_DRAM_BYTES_PER_VOXEL = {"gn": 905.0, "ln": None}
 PLAN_SORT_KERNELS = 8  # cub onesweep radix sort of 55-bit keys: histogram + 7 digit passes
 
 
@@ -383,7 +388,10 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(lcoords.nbytes + lx0.nbytes),
                     "d2h_bytes_per_step": int(part.n_owned * C_CH * lx0.itemsize), "ms_per_step": e2e_t},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": (achieved / peak_tf) if achieved else None, "traffic": None,
+                         "frac": (achieved / peak_tf) if achieved else None,
+                         "traffic": (CONV_DRAM_BYTES_PER_VOXEL[args.block] * nl
+                                     if CONV_DRAM_BYTES_PER_VOXEL.get(args.block) else None),
+                         "traffic_unit": "bytes per conv launch (ncu capture, scaled by voxels)",
                          "kernel": f"{conv_family} (Q8_0, C=128)", "peak_source": peak_src,
                          "flops_per_launch": flops_per_launch,
                          "avg_launch_ms": conv_ms / max(conv_launches, 1)},

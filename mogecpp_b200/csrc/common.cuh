@@ -305,5 +305,8 @@ __device__ __forceinline__ void split_f16(float v, __half& hi, __half& lo) {
 }
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+// x / (1 + e^-x) with the hardware exp2 and reciprocal approximations (a few
+// ulp; used where the result is re-quantised or rounded to fp16 anyway)
+__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 }  // namespace msc

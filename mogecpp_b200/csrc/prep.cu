@@ -190,23 +190,23 @@ __device__ __forceinline__ void store_halves(__half* dst, const __half (&h)[EPL]
     }
 }
 
-// Rows are prepared by warps; lane l holds channels [l*EPL, (l+1)*EPL),
-// read and written with one vector access each where the width allows.
+// Rows are prepared by 8-lane groups (4 rows per warp instruction): lane j
+// of a row's group holds channels [j*EPL, (j+1)*EPL), EPL = C/8, read and
+// written with vector accesses; row reductions take 3 shuffle steps and a
+// row's scalar work is shared by 4 rows per instruction.
+constexpr int kLanesPerRow = 8;
+constexpr int kPrepIters = 2;  // row groups per warp, all loads issued first
+
 template <int C>
-__device__ __forceinline__ void load_row(const void* x, int x_dtype, int64_t row, int lane, float (&v)[C / 32]) {
-    constexpr int EPL = C / 32;
-    const int64_t base = row * C + lane * EPL;
+__device__ __forceinline__ void load_row8(const void* x, int x_dtype, int64_t row, int j, float (&v)[C / 8]) {
+    constexpr int EPL = C / 8;
+    const int64_t base = row * C + j * EPL;
     if (x_dtype == DT_F32) {
-        if constexpr (EPL >= 4) {
-            uint32_t w[EPL];
-            load_words<EPL>(static_cast<const float*>(x) + base, w);
+        uint32_t w[EPL];
+        load_words<EPL>(static_cast<const float*>(x) + base, w);
 #pragma unroll
-            for (int k = 0; k < EPL; ++k) v[k] = __uint_as_float(w[k]);
-        } else {
-#pragma unroll
-            for (int k = 0; k < EPL; ++k) v[k] = static_cast<const float*>(x)[base + k];
-        }
-    } else if constexpr (EPL >= 2) {
+        for (int k = 0; k < EPL; ++k) v[k] = __uint_as_float(w[k]);
+    } else {
         uint32_t w[EPL / 2];
         load_words<EPL / 2>(static_cast<const __half*>(x) + base, w);
 #pragma unroll
@@ -214,130 +214,142 @@ __device__ __forceinline__ void load_row(const void* x, int x_dtype, int64_t row
             const unsigned short b = static_cast<unsigned short>(w[k / 2] >> (16 * (k & 1)));
             v[k] = x_dtype == DT_F16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
         }
-    } else {
-        v[0] = x_dtype == DT_F16 ? __half2float(static_cast<const __half*>(x)[base])
-                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base]);
     }
 }
 
-// Normalisation, SiLU and the operand output of one row (warp-uniform row).
-template <int C>
-__device__ __forceinline__ void prepare_row(float (&v)[C / 32], int64_t row, int lane, int64_t n, int ln,
-                                            const float* gamma, const float* beta, float eps, int silu, int mode,
-                                            __half* planes, const float2* gn, const int4* coords, int nsamples) {
-    constexpr int EPL = C / 32;
-    const int64_t base = row * C + lane * EPL;
-    if (gn) {
-        // GroupNorm with 32 groups: lane l holds group l; ggml order
-        // ((x - mean) * scale, then * gamma, then + beta)
-        int b = __ldg(coords + row).w;  // out-of-range samples are reported by the statistics pass
-        b = b < 0 ? 0 : (b >= nsamples ? nsamples - 1 : b);
-        const float2 ms = gn[b * 32 + lane];
+// sum over the 8 lanes of a row group
+__device__ __forceinline__ float row_sum8(float s) {
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) {
-            float t = __fmul_rn(v[k] - ms.x, ms.y);
-            if (gamma) t = __fmul_rn(t, __ldg(gamma + lane * EPL + k));
-            if (beta) t = __fadd_rn(t, __ldg(beta + lane * EPL + k));
-            v[k] = t;
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+}
+
+// Normalisation, SiLU and the operand output of one row; all 32 lanes call
+// it (the shuffles need them), `valid` gates the stores.
+template <int C>
+__device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, bool valid, int j, int64_t n, int ln,
+                                             const float* gamma, const float* beta, float eps, int silu, int mode,
+                                             __half* planes, const float2* gn, const int4* coords, int nsamples) {
+    constexpr int EPL = C / 8;
+    constexpr int CPG = C / 32;  // channels per GroupNorm group
+    const int64_t base = row * C + j * EPL;
+    if (gn) {
+        // GroupNorm, 32 groups: ggml order ((x - mean) * scale, then * gamma,
+        // then + beta); a lane holds EPL / CPG = 4 groups
+        int b = valid ? __ldg(coords + row).w : 0;  // out-of-range samples are reported by the statistics pass
+        b = b < 0 ? 0 : (b >= nsamples ? nsamples - 1 : b);
+#pragma unroll
+        for (int gq = 0; gq < EPL / CPG; ++gq) {
+            const float2 ms = gn[b * 32 + (j * EPL) / CPG + gq];
+#pragma unroll
+            for (int k = gq * CPG; k < (gq + 1) * CPG; ++k) {
+                float t = __fmul_rn(v[k] - ms.x, ms.y);
+                if (gamma) t = __fmul_rn(t, __ldg(gamma + j * EPL + k));
+                if (beta) t = __fadd_rn(t, __ldg(beta + j * EPL + k));
+                v[k] = t;
+            }
         }
     } else if (ln) {
         float s = 0.0f;
 #pragma unroll
         for (int k = 0; k < EPL; ++k) s += v[k];
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const float mean = s / C;
+        const float mean = row_sum8(s) / C;
         float q = 0.0f;
 #pragma unroll
         for (int k = 0; k < EPL; ++k) {
             const float d = v[k] - mean;
             q = fmaf(d, d, q);
         }
-        for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-        const float scale = 1.0f / sqrtf(q / C + eps);
+        const float scale = 1.0f / sqrtf(row_sum8(q) / C + eps);
 #pragma unroll
         for (int k = 0; k < EPL; ++k) {
             float t = __fmul_rn(v[k] - mean, scale);
-            if (gamma) t = __fmul_rn(t, __ldg(gamma + lane * EPL + k));
-            if (beta) t = __fadd_rn(t, __ldg(beta + lane * EPL + k));
+            if (gamma) t = __fmul_rn(t, __ldg(gamma + j * EPL + k));
+            if (beta) t = __fadd_rn(t, __ldg(beta + j * EPL + k));
             v[k] = t;
         }
     }
     if (silu) {
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) v[k] = silu_f(v[k]);
+        for (int k = 0; k < EPL; ++k) v[k] = silu_fast(v[k]);
     }
     const int64_t plane = n * C;
     if (mode == ACT_FP16) {
         __half h[EPL];
 #pragma unroll
         for (int k = 0; k < EPL; ++k) h[k] = __float2half_rn(v[k]);
-        store_halves<EPL>(planes + base, h);
+        if (valid) store_halves<EPL>(planes + base, h);
         return;
     }
     if (mode == ACT_Q8 || mode == ACT_Q8I) {
-        // 32-channel blocks span 32/EPL lanes
+        // a 32-channel block spans LPB lanes of the row group
+        constexpr int LPB = 32 / EPL > 0 ? 32 / EPL : 1;
         float amax = 0.0f;
 #pragma unroll
         for (int k = 0; k < EPL; ++k) amax = fmaxf(amax, fabsf(v[k]));
-        for (int o = 1; o < 32 / EPL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+#pragma unroll
+        for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
         int q[EPL];
 #pragma unroll
         for (int k = 0; k < EPL; ++k) q[k] = __float2int_rn(__fmul_rn(v[k], id));
+        if (!valid) return;
         if (mode == ACT_Q8I) {
-            int8_t* codes = reinterpret_cast<int8_t*>(planes) + base;
-            if constexpr (EPL >= 4) {
-                uint32_t w[EPL / 4];
+            uint32_t w[EPL / 4];
 #pragma unroll
-                for (int k = 0; k < EPL / 4; ++k)
-                    w[k] = (static_cast<uint32_t>(q[4 * k]) & 0xffu) | ((static_cast<uint32_t>(q[4 * k + 1]) & 0xffu) << 8) |
-                           ((static_cast<uint32_t>(q[4 * k + 2]) & 0xffu) << 16) |
-                           (static_cast<uint32_t>(q[4 * k + 3]) << 24);
-                store_words<EPL / 4>(codes, w);
-            } else {
-#pragma unroll
-                for (int k = 0; k < EPL; ++k) codes[k] = static_cast<int8_t>(q[k]);
-            }
+            for (int k = 0; k < EPL / 4; ++k)
+                w[k] = (static_cast<uint32_t>(q[4 * k]) & 0xffu) | ((static_cast<uint32_t>(q[4 * k + 1]) & 0xffu) << 8) |
+                       ((static_cast<uint32_t>(q[4 * k + 2]) & 0xffu) << 16) | (static_cast<uint32_t>(q[4 * k + 3]) << 24);
+            store_words<EPL / 4>(reinterpret_cast<int8_t*>(planes) + base, w);
         } else {
             __half h[EPL];
 #pragma unroll
             for (int k = 0; k < EPL; ++k) h[k] = __int2half_rn(q[k]);
             store_halves<EPL>(planes + base, h);
         }
-        if ((lane * EPL) % 32 == 0) {
+        if ((j * EPL) % 32 == 0) {
             float* scales = reinterpret_cast<float*>(reinterpret_cast<char*>(planes) +
                                                      scale_offset(n, mode == ACT_Q8I ? C / 2 : C));
-            scales[row * (C / 32) + lane * EPL / 32] = __half2float(__float2half_rn(d));
+            const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+            for (int bk = 0; bk < (EPL + 31) / 32; ++bk) scales[row * (C / 32) + (j * EPL) / 32 + bk] = dh;
         }
         return;
     }
     __half hi[EPL], lo[EPL];
 #pragma unroll
     for (int k = 0; k < EPL; ++k) split_f16(v[k], hi[k], lo[k]);
+    if (!valid) return;
     store_halves<EPL>(planes + base, hi);
     store_halves<EPL>(planes + plane + base, lo);
 }
-
-// kRowsPerPrepWarp consecutive rows per warp, all loads issued before the
-// first row is processed (several 512-byte rows in flight per warp).
-constexpr int kRowsPerPrepWarp = 4;
 
 template <int C>
 __global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
                                    const float* beta, float eps, int silu, int mode, __half* planes,
                                    const float2* gn, const int4* coords, int nsamples) {
-    const int64_t r0 = ((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5) * kRowsPerPrepWarp;
+    const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (r0 >= n) return;
-    float v[kRowsPerPrepWarp][C / 32];
+    const int j = lane & (kLanesPerRow - 1);
+    const int64_t r0 = warp * (4 * kPrepIters) + (lane >> 3);
+    if (warp * (4 * kPrepIters) >= n) return;
+    float v[kPrepIters][C / 8];
 #pragma unroll
-    for (int j = 0; j < kRowsPerPrepWarp; ++j)
-        if (r0 + j < n) load_row<C>(x, x_dtype, r0 + j, lane, v[j]);
+    for (int it = 0; it < kPrepIters; ++it) {
+        const int64_t row = r0 + 4 * it;
+        if (row < n) {
+            load_row8<C>(x, x_dtype, row, j, v[it]);
+        } else {
 #pragma unroll
-    for (int j = 0; j < kRowsPerPrepWarp; ++j)
-        if (r0 + j < n)
-            prepare_row<C>(v[j], r0 + j, lane, n, ln, gamma, beta, eps, silu, mode, planes, gn, coords, nsamples);
+            for (int k = 0; k < C / 8; ++k) v[it][k] = 0.0f;
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < kPrepIters; ++it) {
+        const int64_t row = r0 + 4 * it;
+        prepare_row8<C>(v[it], row, row < n, j, n, ln, gamma, beta, eps, silu, mode, planes, gn, coords, nsamples);
+    }
 }
 
 }  // namespace
@@ -411,7 +423,7 @@ cudaError_t launch_act_prepare(const void* x, int x_dtype, int64_t n, int c, int
                                const float* beta, float eps, int silu, int mode, void* planes, cudaStream_t st,
                                const float2* gn, const int32_t* coords, int nsamples) {
     if (n == 0) return cudaSuccess;
-    const int64_t warps = (n + kRowsPerPrepWarp - 1) / kRowsPerPrepWarp;
+    const int64_t warps = (n + 4 * kPrepIters - 1) / (4 * kPrepIters);
     const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
     auto* out = static_cast<__half*>(planes);
     const int4* c4 = reinterpret_cast<const int4*>(coords);
