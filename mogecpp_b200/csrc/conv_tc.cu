@@ -351,12 +351,21 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                 for (int b = 0; b < C::NBLK; ++b) sa[b] = sa_next[b];
                 fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
             }
+            // Q8 kinds: when none of this warp's 32 rows has a neighbour at
+            // this tap, every block sum it would read is scaled by d_a = 0:
+            // keep the slot protocol, skip the loads and the arithmetic
+            const bool idle = Q8 && !__any_sync(0xffffffffu, row >= 0 && nb[tap] >= 0);
 #pragma unroll 1
             for (int grp = 0; grp < C::KCH * C::GPS; ++grp, ++g) {
                 const int slot = static_cast<int>(g % C::NACC);
                 if (!wait_or_abort(&S.acc_full[slot], static_cast<uint32_t>(g / C::NACC) & 1, S.abort, a.status))
                     return;
                 tc_fence_after();
+                if (idle) {
+                    tc_fence_before();
+                    warp_arrive(&S.acc_empty[slot]);
+                    continue;
+                }
 #pragma unroll
                 for (int b = 0; b < C::BPG; ++b) {
                     const int kb = grp * C::BPG + b;  // 32-channel block (Q8 kinds)
