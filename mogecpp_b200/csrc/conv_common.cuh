@@ -80,6 +80,37 @@ __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t idx
     return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
 }
 
+// N consecutive elements (N a multiple of 8, off a multiple of 8) as floats,
+// in 16-byte loads.
+template <int N>
+__device__ __forceinline__ void load_row_vec(const void* p, int dtype, int64_t off, float (&v)[N]) {
+    if (dtype == DT_F32) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p) + off);
+#pragma unroll
+        for (int k = 0; k < N / 4; ++k) {
+            const float4 t = src[k];
+            v[4 * k] = t.x, v[4 * k + 1] = t.y, v[4 * k + 2] = t.z, v[4 * k + 3] = t.w;
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(p) + off);
+#pragma unroll
+        for (int k = 0; k < N / 8; ++k) {
+            const uint4 t = src[k];
+            const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const unsigned short b = static_cast<unsigned short>(w[e / 2] >> (16 * (e & 1)));
+                v[8 * k + e] = dtype == DT_F16 ? __half2float(__ushort_as_half(b))
+                                               : __bfloat162float(__ushort_as_bfloat16(b));
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 template <int N>
 __device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const float (&v)[N]) {
     if (dtype == DT_F32) {

@@ -331,6 +331,10 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
         uint32_t rem = rot_mask(tile_mask(S, buf), rot);
         const int row = S.rows[buf * BM + m];
         const int* nb = S.nbr + buf * BM * 27 + m * 27;
+        if (a.residual && row >= 0) {
+            const int es = a.res_dtype == DT_F32 ? 4 : 2;
+            prefetch_l2(static_cast<const char*>(a.residual) + (static_cast<int64_t>(row) * COUT + c_base) * es);
+        }
         uint64_t acc[COLS / 2];
 #pragma unroll
         for (int e = 0; e < COLS / 2; ++e) acc[e] = 0ull;
@@ -428,14 +432,27 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                 float v[EC];
 #pragma unroll
                 for (int e = 0; e < EC / 2; ++e) unpack2(acc[c0 / 2 + e], v[2 * e], v[2 * e + 1]);
+                // bias and residual in 8-column vector loads (the residual row
+                // was prefetched to L2 at the start of the tile)
 #pragma unroll
-                for (int e = 0; e < EC; ++e) {
-                    const int n = c_base + c0 + e;
-                    float t = v[e] * oscale;
-                    if (a.bias) t += __ldg(a.bias + n);
-                    if (a.silu_out) t = silu_f(t);
-                    if (a.residual) t += load_elem(a.residual, a.res_dtype, static_cast<int64_t>(row) * COUT + n);
-                    v[e] = t;
+                for (int e8 = 0; e8 < EC; e8 += 8) {
+                    float bv[8], rv[8];
+                    if (a.bias) {
+                        const float4* b4 = reinterpret_cast<const float4*>(a.bias + c_base + c0 + e8);
+                        const float4 t0 = __ldg(b4), t1 = __ldg(b4 + 1);
+                        bv[0] = t0.x, bv[1] = t0.y, bv[2] = t0.z, bv[3] = t0.w;
+                        bv[4] = t1.x, bv[5] = t1.y, bv[6] = t1.z, bv[7] = t1.w;
+                    }
+                    if (a.residual)
+                        load_row_vec<8>(a.residual, a.res_dtype, static_cast<int64_t>(row) * COUT + c_base + c0 + e8, rv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        float t = v[e8 + e] * oscale;
+                        if (a.bias) t += bv[e];
+                        if (a.silu_out) t = silu_fast(t);
+                        if (a.residual) t += rv[e];
+                        v[e8 + e] = t;
+                    }
                 }
                 if constexpr (EC == 32) {
                     // this thread holds one whole 32-channel block of the row
