@@ -121,8 +121,9 @@ def _level(ex, oracle, coords, kind="row_cache"):
 
 
 def tap_order_keys(nbr):
-    """Sort key of the tap order: corners in the high bits, then edges,
-    faces, centre (tap index order within a class)."""
+    """Sort key of the tap order: the tap mask with corners in the high bits,
+    then edges, faces, centre (tap index order within a class), taken to its
+    position in the reflected Gray-code sequence (prefix xor)."""
     n = nbr.shape[0]
     bits = np.zeros(27, dtype=np.int64)
     nxt = 26
@@ -132,7 +133,10 @@ def tap_order_keys(nbr):
             if sum(abs(v) for v in d) == cls:
                 bits[t] = nxt
                 nxt -= 1
-    return ((nbr < n).astype(np.int64) << bits[None, :]).sum(1)
+    k = ((nbr < n).astype(np.int64) << bits[None, :]).sum(1)
+    for sh in (1, 2, 4, 8, 16):
+        k ^= k >> sh
+    return k
 
 
 @pytest.mark.parametrize("case", ["surface", "split", "ragged"])
