@@ -195,23 +195,24 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
  * The GroupNorm variant of the residual block, in place:
  *   x = x + conv2(SiLU(GroupNorm_32(conv1(x) + b1))) + b2
  * GroupNorm is sample-wide: for each sample (coords[i][3]) and each of 32
- * groups of c/32 channels, the mean over the sample's voxels (double sum),
- * then the variance of the float deviations (double sum of their squares),
- * y = (h - mean) * (1 / sqrtf(var + eps)), then * gn_w, then + gn_b (either
- * may be NULL).  Restates ggml's group_norm_f32 (ggml-cpu/ops.cpp:4208-4283)
- * on the [C, N] features viewed as [N, 1, C]; the reference's res_block
- * (src/sparse.cpp:629-642) uses LayerNorm instead and has no counterpart.
+ * groups of c/32 channels, the mean and variance of the group's values over
+ * the sample's voxels (double sums of x and x*x, var = E[x^2] - mean^2 in
+ * double), y = (h - mean) * (1 / sqrtf(var + eps)), then * gn_w, then + gn_b
+ * (either may be NULL).  Follows ggml's group_norm_f32
+ * (ggml-cpu/ops.cpp:4208-4283, two passes) on the [C, N] features viewed as
+ * [N, 1, C]; the reference's res_block (src/sparse.cpp:629-642) uses
+ * LayerNorm instead and has no counterpart.
  *
  * Sharded runs: rows [0, n_stat) are this rank's own voxels and enter the
  * statistics; rows [n_stat, n) are halo rows, normalised with the same
  * statistics.  stats is a caller-owned device buffer of
  * msc_gn_stats_doubles(nsamples) doubles.  When allreduce is given it is
- * called twice on the calling thread, in stream order, with a device span
- * of the statistics to sum over all ranks in place (enqueued on `stream`,
- * e.g. an NCCL all-reduce): first the sums and counts (nsamples * 33
- * doubles at stats), then the squared deviations (nsamples * 32 doubles at
- * stats + nsamples * 33).  A non-zero return fails the call.  With n = 0
- * the callback is still called (collectives stay matched across ranks). */
+ * called once per block on the calling thread, in stream order, with the
+ * whole statistics buffer (msc_gn_stats_doubles(nsamples) doubles at
+ * stats: sums, counts, sums of squares) to sum over all ranks in place,
+ * enqueued on `stream` (e.g. an NCCL all-reduce).  A non-zero return fails
+ * the call.  With n = 0 the callback is still called (collectives stay
+ * matched across ranks). */
 typedef int (*msc_allreduce_fn)(double* buf, int64_t count, void* stream, void* user);
 
 int64_t msc_gn_stats_doubles(int nsamples);

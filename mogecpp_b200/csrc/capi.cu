@@ -571,7 +571,6 @@ int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_s
         void* planes = ws;
         float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
         float2* gn = reinterpret_cast<float2*>(static_cast<char*>(ws) + 2 * planes_bytes + 256);
-        const int64_t ns = nsamples;
         cudaStream_t st = S(stream);
         auto reduce = [&](double* buf, int64_t count, const char* what) {
             if (allreduce && allreduce(buf, count, stream, allreduce_user) != 0)
@@ -583,21 +582,15 @@ int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_s
             cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 0, nullptr, nullptr, 0.f, 0, m1, planes, st), "conv1 prepare");
             run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 0, nullptr, 0, h, MSC_F32, st, p1);
         }
-        // sample-wide statistics of the owned rows: sums and counts, then the
-        // squared deviations from the complete means
+        // sample-wide statistics of the owned rows (sums, counts, sums of
+        // squares), summed over the ranks by the hook
         cuda_ok(cudaMemsetAsync(stats, 0, sizeof(double) * msc::gn_stats_doubles(nsamples), st), "stats clear");
-        {
+        if (n > 0) {
             ProfScope ps(ctx, "gn_stats", st);
-            if (n > 0) cuda_ok(msc::launch_gn_pass(1, h, c, coords, n, n_stat, nsamples, stats, ctx->status, st),
-                               "GroupNorm sums");
+            cuda_ok(msc::launch_gn_stats(h, c, coords, n, n_stat, nsamples, stats, ctx->status, st),
+                    "GroupNorm statistics");
         }
-        reduce(stats, ns * 33, "sums");
-        {
-            ProfScope ps(ctx, "gn_stats", st);
-            if (n > 0) cuda_ok(msc::launch_gn_pass(2, h, c, coords, n, n_stat, nsamples, stats, ctx->status, st),
-                               "GroupNorm deviations");
-        }
-        reduce(stats + ns * 33, ns * 32, "deviations");
+        reduce(stats, msc::gn_stats_doubles(nsamples), "statistics");
         if (n == 0) return;
         {
             ProfScope ps(ctx, "gn_finalize", st);

@@ -55,7 +55,6 @@ constexpr int kProducerWarps = 2;
 constexpr int kDrainWarps = 16;
 constexpr int kThreads = 32 * (kProducerWarps + 1 + kDrainWarps);
 constexpr int kProducers = 32 * kProducerWarps;
-constexpr int kDrainers = 32 * kDrainWarps;
 constexpr int kRowsPerProducer = BM / kProducers;
 constexpr int kSmemLimit = 227 * 1024;  // max dynamic shared memory per block on sm_100
 

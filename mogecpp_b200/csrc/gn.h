@@ -8,14 +8,13 @@
 namespace msc {
 
 // Doubles in the statistics buffer for nsamples samples:
-// [nsamples*32] sums | [nsamples] counts | [nsamples*32] squared deviations.
+// [nsamples*32] sums | [nsamples] counts | [nsamples*32] sums of squares.
 int64_t gn_stats_doubles(int nsamples);
-// pass 1 adds the group sums and voxel counts of rows [0, n_stat) and
-// checks the sample index of all n rows (MSC_DEV_BAD_COORD); pass 2 (after
-// the sums are complete) adds the squared deviations of rows [0, n_stat).
-// x: fp32 [n][c], c in {64, 128}; coords: int32 [n][4], sample in field 3.
-cudaError_t launch_gn_pass(int pass, const float* x, int c, const int32_t* coords, int64_t n, int64_t n_stat,
-                           int nsamples, double* stats, uint32_t* status, cudaStream_t st);
+// Adds the group sums, sums of squares and voxel counts of rows [0, n_stat)
+// and checks the sample index of all n rows (MSC_DEV_BAD_COORD).  x: fp32
+// [n][c], c in {64, 128}; coords: int32 [n][4], sample in field 3.
+cudaError_t launch_gn_stats(const float* x, int c, const int32_t* coords, int64_t n, int64_t n_stat,
+                            int nsamples, double* stats, uint32_t* status, cudaStream_t st);
 // gn[b*32 + g] = {mean, 1 / sqrtf(var + eps)}.
 cudaError_t launch_gn_finalize(const double* stats, int c, int nsamples, float eps, float2* gn, cudaStream_t st);
 

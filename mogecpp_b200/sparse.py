@@ -206,7 +206,7 @@ class SparseCudaExecutor:
         affine.  coords [n, 4] int32 give each row's sample (field 3).  Rows
         [0, n_stat) enter the sample-wide statistics (default: all rows);
         ``allreduce(t)``, when given, sums the float64 tensor t over all
-        ranks in place on the current stream (two calls per block)."""
+        ranks in place on the current stream (one call per block)."""
         n, c = x.shape
         n_stat = n if n_stat is None else n_stat
         wsb = self.lib.msc_res_block_gn_workspace_bytes(n, c, nsamples)

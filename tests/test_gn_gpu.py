@@ -76,8 +76,8 @@ def test_gn_block_fp16_state_and_plan(ex, oracle, tag):
 
 
 def test_gn_block_allreduce_callback(ex, oracle):
-    """The all-reduce hook is called twice with the sums+counts span, then the
-    deviations span; an identity reduction leaves the result bit-identical."""
+    """The all-reduce hook is called once per block with the whole statistics
+    buffer; an identity reduction leaves the result bit-identical."""
     coords = two_sample_coords(320)
     nbr = dev(oracle.make_level(coords))
     cd = dev(coords)
@@ -93,7 +93,7 @@ def test_gn_block_allreduce_callback(ex, oracle):
     b = x0.clone()
     ex.res_block_gn(b, nbr, cd, 2, blk, allreduce=ident)
     ex.check()
-    assert seen == [2 * 33, 2 * 32]
+    assert seen == [2 * 65]
     assert torch.equal(a, b)
 
     def broken(t):
