@@ -29,16 +29,20 @@
 // chains drift by ~1e-6 relative, which ggml's activation re-quantisation
 // would amplify.
 //
-// Persistent CTA, one per SM, 19 warps:
+// Persistent CTA, one per SM, 20 warps:
 //   warps 0-1   producers: per tile, stage the rows' neighbour lists and the
 //               tap mask; per stage, gather the 128 A rows with coalesced
 //               16-byte cp.async (8 lanes per 128-byte row, swizzled straight
-//               into the UMMA layout; sentinel rows zero-filled); thread 0
+//               into the UMMA layout; sentinel rows zero-filled), completion
+//               tracked by the stage's `gathered` barrier; thread 0
 //               bulk-copies the stage's pre-swizzled B tile.
 //   warp 2      TMEM allocation and the single-thread MMA issue loop.
 //   warps 3-18  drain + epilogue: TMEM lane quarter (warp % 4) x column quarter;
 //               fp32 accumulators in registers, bias / SiLU / residual / store.
-// Pipelines (mbarriers): smem stages full/empty, TMEM accumulator slots
+//   warp 19     publisher: once a stage's copies have landed, the proxy fence
+//               and the stage's `full` arrival (a thread with no copies of its
+//               own in flight, so the fence does not wait on them).
+// Pipelines (mbarriers): smem stages gathered/full/empty, TMEM accumulator slots
 // acc_full/acc_empty (NACC rotating slots), per-tile tile_ready/tile_free
 // (double-buffered neighbour lists).  Taps are visited in a per-tile rotated
 // order.  Every wait is bounded; a wait that runs out sets MSC_DEV_TIMEOUT
@@ -53,7 +57,8 @@ namespace {
 constexpr int BM = 128;
 constexpr int kProducerWarps = 2;
 constexpr int kDrainWarps = 16;
-constexpr int kThreads = 32 * (kProducerWarps + 1 + kDrainWarps);
+constexpr int kFenceWarp = kProducerWarps + 1 + kDrainWarps;  // last warp
+constexpr int kThreads = 32 * (kProducerWarps + 2 + kDrainWarps);
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kRowsPerProducer = BM / kProducers;
 constexpr int kSmemLimit = 227 * 1024;  // max dynamic shared memory per block on sm_100
@@ -87,9 +92,6 @@ struct Cfg {
     static constexpr int STAGES_FIT = (kSmemLimit - 1024 - FIXED) / STAGE;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int SMEM = 1024 + STAGES * STAGE + FIXED;
-    // gather groups a producer keeps in flight; at least one stage of slack
-    // between the stage being published and the stage being refilled
-    static constexpr int LAG = STAGES >= 4 ? STAGES - 2 : 1;
     static_assert(STAGES >= 2, "at least two pipeline stages");
     static_assert(ROW_BYTES % 128 == 0, "activation rows must be whole 128-byte chunks");
     static_assert(COUT % 64 == 0 && COUT <= 256, "cout must be 64..256 in steps of 64");
@@ -106,6 +108,7 @@ struct Smem {
     float* sB;       // [27][NBLK][COUT] weight block scales (Q8I)
     uint64_t* full;
     uint64_t* empty;
+    uint64_t* gathered;
     uint64_t* acc_full;
     uint64_t* acc_empty;
     uint64_t* tile_ready;  // [2]
@@ -143,23 +146,14 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
     const uint8_t* planes = static_cast<const uint8_t*>(a.planes);
     const uint8_t* wdata = static_cast<const uint8_t*>(a.blob) + sizeof(WeightHeader);
     const int64_t plane_bytes = a.n_in * C::ROW_BYTES;
-    constexpr int LAG = C::LAG;
-    int64_t i = 0;        // stages issued
-    int64_t arrived = 0;  // stages this thread has published (arrived on full)
+    int64_t i = 0;  // stages issued
     bool ok = true;
     int k = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++k) {
         const int buf = k & 1;
-        if (k >= 2) {
-            // publish every issued stage before blocking on the drainers, who may
-            // still need those stages of an earlier tile
-            cp_async_wait_all();
-            fence_proxy_async();
-            for (; arrived < i; ++arrived) warp_arrive(&S.full[arrived % C::STAGES]);
-            if (!wait_or_abort(&S.tile_free[buf], ((k >> 1) - 1) & 1, S.abort, a.status)) {
-                ok = false;
-                break;
-            }
+        if (k >= 2 && !wait_or_abort(&S.tile_free[buf], ((k >> 1) - 1) & 1, S.abort, a.status)) {
+            ok = false;
+            break;
         }
         // neighbour lists and tap mask of this thread's rows (t0, t0+64)
         uint32_t m = 0;
@@ -231,20 +225,33 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
                     cp_async16(dst + p * C::A_PLANE, src, nbytes);
                 }
             }
-            cp_async_commit();
-            if (i + 1 - arrived > LAG) {
-                cp_async_wait<LAG>();
-                fence_proxy_async();
-                warp_arrive(&S.full[arrived % C::STAGES]);
-                ++arrived;
-            }
+            cp_async_mbar_arrive_noinc(&S.gathered[s]);
             ++kc;
         }
     }
     cp_async_wait_all();
-    if (ok) {
-        fence_proxy_async();
-        for (; arrived < i; ++arrived) warp_arrive(&S.full[arrived % C::STAGES]);
+    (void)ok;
+}
+
+// Publishes each stage to the MMA issuer once the producers' copies have
+// landed: a proxy fence (generic-proxy cp.async writes -> async-proxy MMA
+// reads) by a thread with no copies of its own in flight, so it never waits
+// on them.
+template <int CIN, int COUT, int NA, int NB, int KIND>
+__device__ void publisher(const ConvArgs& a, const Smem& S, int64_t ntiles) {
+    using C = Cfg<CIN, COUT, NA, NB, KIND>;
+    int64_t i = 0;
+    int k = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
+        const int buf = k & 1;
+        if (!wait_or_abort(&S.tile_ready[buf], (k >> 1) & 1, S.abort, a.status)) return;
+        const int nst = __popc(tile_mask(S, buf)) * C::KCH;
+        for (int st = 0; st < nst; ++st, ++i) {
+            const int s = static_cast<int>(i % C::STAGES);
+            if (!wait_or_abort(&S.gathered[s], static_cast<uint32_t>(i / C::STAGES) & 1, S.abort, a.status)) return;
+            fence_proxy_async();
+            mbar_arrive(&S.full[s]);
+        }
     }
 }
 
@@ -468,8 +475,7 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
     }
 }
 
-// Register budget: the launch check rounds the warp count up to a multiple of
-// four, so 19 warps are charged as 20 x 32 threads x 96 registers = 61440.
+// Register budget: 20 warps x 32 threads x 96 registers = 61440.
 template <int CIN, int COUT, int NA, int NB, int KIND>
 __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     using C = Cfg<CIN, COUT, NA, NB, KIND>;
@@ -487,7 +493,8 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
     S.full = bars;
     S.empty = S.full + C::STAGES;
-    S.acc_full = S.empty + C::STAGES;
+    S.gathered = S.empty + C::STAGES;
+    S.acc_full = S.gathered + C::STAGES;
     S.acc_empty = S.acc_full + C::NACC;
     S.tile_ready = S.acc_empty + C::NACC;
     S.tile_free = S.tile_ready + 2;
@@ -498,7 +505,8 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&S.full[s], kProducerWarps + 1);
+            mbar_init(&S.full[s], 2);  // publisher + weight tile
+            mbar_init(&S.gathered[s], 32 * kProducerWarps);
             mbar_init(&S.empty[s], 1);
         }
         for (int s = 0; s < C::NACC; ++s) {
@@ -534,6 +542,9 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
         producer<CIN, COUT, NA, NB, KIND>(a, S, ntiles);
     } else if (warp == kProducerWarps) {
         if ((threadIdx.x & 31) == 0) mma_issuer<CIN, COUT, NA, NB, KIND>(a, S, ntiles, tmem);
+        __syncwarp();
+    } else if (warp == kFenceWarp) {
+        if ((threadIdx.x & 31) == 0) publisher<CIN, COUT, NA, NB, KIND>(a, S, ntiles);
         __syncwarp();
     } else {
         drainer<CIN, COUT, NA, NB, KIND>(a, S, ntiles, tmem);
