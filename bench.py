@@ -388,8 +388,9 @@ def run_ours(args):
     achieved = flops_per_launch / (conv_ms / max(conv_launches, 1) * 1e-3) / 1e12 if conv_launches else None
     # launches per profiled call: make_level = clear + insert + neighbour kernels;
     # plan_build = header + Morton keys + the radix sort's kernels + subtiles
-    # (row-cache: + subtiles; tap order: header + mask keys + histogram, scan and 4 passes of a 27-bit sort)
-    plan_kernels = 3 + PLAN_SORT_KERNELS if cached else 2 + 6
+    # (row-cache: + subtiles; tap order: header + mask keys + histogram, scan and 4 passes of a 27-bit sort
+    # + the per-tile neighbour lists)
+    plan_kernels = 3 + PLAN_SORT_KERNELS if cached else 2 + 6 + 1
     kernels_per_family = {"make_level": 3, "plan_build": plan_kernels, "conv_tc": 1, "conv_cached": 1,
                           "act_prepare": 1}
     launches = sum(kernels_per_family.get(k, 1) * v[0] for k, v in prof.items())

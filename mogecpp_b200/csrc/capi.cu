@@ -167,6 +167,7 @@ void need_ws(size_t have, size_t want) {
 struct PlanUse {
     const void* cached = nullptr;
     const int32_t* order = nullptr;
+    msc::PlanTiles tiles{};
 };
 
 void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
@@ -211,6 +212,9 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
         return;
     }
     a.perm = pu.order;
+    a.tile_rows = pu.tiles.rows;
+    a.tile_nbr = nbr ? pu.tiles.nbr : nullptr;
+    a.tile_mask = pu.tiles.mask;
     ProfScope ps(ctx, nbr ? "conv_tc" : "linear_tc", st);
     cuda_ok(msc::launch_conv(a, st), "conv launch");
 }
@@ -232,7 +236,9 @@ PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n, const msc_context::
     if (pl.n != n)
         fail(MSC_E_INVALID, "conv plan covers " + std::to_string(pl.n) + " voxels, not " + std::to_string(n));
     if (pl.kind == MSC_PLAN_TAP_ORDER) {
-        pu.order = msc::plan_view(static_cast<uint8_t*>(const_cast<void*>(plan)), n, msc::plan_max_desc(n)).order;
+        uint8_t* pb = static_cast<uint8_t*>(const_cast<void*>(plan));
+        pu.order = msc::plan_view(pb, n, msc::plan_max_desc(n)).order;
+        pu.tiles = msc::plan_tiles(pb, n);
     } else if (msc::weight_has_cached(b.wtype, b.cin, b.ntaps) && msc::conv_cached_supported(b.cin, b.cout)) {
         pu.cached = plan;
     }

@@ -73,6 +73,12 @@ struct ConvArgs {
     int64_t n;               // output rows processed
     int64_t row_begin;       // output row k is row_begin + k (when perm is null)
     const int32_t* perm;     // [n] output rows to process, or null
+    // With a tap-order plan: the tile rows (-1 past n), their neighbour
+    // lists (-1 = missing) and each tile's tap mask (plan.h PlanTiles); the
+    // conv then stages each tile with bulk copies.  Null otherwise.
+    const int32_t* tile_rows;
+    const int32_t* tile_nbr;
+    const uint32_t* tile_mask;
     int cin;
     const int32_t* nbr;      // [rows][27] indexed by output row; null => linear (row i reads row i)
     const void* blob;        // prepared weights

@@ -155,37 +155,56 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
             ok = false;
             break;
         }
-        // neighbour lists and tap mask of this thread's rows (t0, t0+64)
-        uint32_t m = 0;
+        if (a.tile_nbr) {
+            // a tap-order plan holds this tile's rows, neighbour lists and tap
+            // mask: two bulk copies completing on tile_ready (no thread loads)
+            if (t0 == 0) {
+                S.wmask[buf * kProducerWarps] = __ldg(a.tile_mask + tile);
 #pragma unroll
-        for (int u = 0; u < kRowsPerProducer; ++u) {
-            const int r = t0 + u * kProducers;
-            const int64_t row = tile_row(a, tile * BM + r);
-            int* nb = S.nbr + buf * BM * 27 + r * 27;
-            if (row >= 0) {
-                if (a.nbr) {
-                    const int* src = a.nbr + row * 27;
+                for (int w = 1; w < kProducerWarps; ++w) S.wmask[buf * kProducerWarps + w] = 0u;
+                mbar_arrive_expect_tx(&S.tile_ready[buf], BM * 27 * 4 + BM * 4);
+                bulk_g2s(smem_u32(S.nbr + buf * BM * 27), a.tile_nbr + tile * BM * 27, BM * 27 * 4, &S.tile_ready[buf]);
+                bulk_g2s(smem_u32(S.rows + buf * BM), a.tile_rows + tile * BM, BM * 4, &S.tile_ready[buf]);
+            } else if ((t0 & 31) == 0) {
+                mbar_arrive(&S.tile_ready[buf]);
+            }
+            if (!wait_or_abort(&S.tile_ready[buf], (k >> 1) & 1, S.abort, a.status)) {
+                ok = false;
+                break;
+            }
+        } else {
+            // neighbour lists and tap mask of this thread's rows (t0, t0+64)
+            uint32_t m = 0;
+#pragma unroll
+            for (int u = 0; u < kRowsPerProducer; ++u) {
+                const int r = t0 + u * kProducers;
+                const int64_t row = tile_row(a, tile * BM + r);
+                int* nb = S.nbr + buf * BM * 27 + r * 27;
+                if (row >= 0) {
+                    if (a.nbr) {
+                        const int* src = a.nbr + row * 27;
 #pragma unroll 9
-                    for (int t = 0; t < 27; ++t) {
-                        const int j = __ldg(src + t);
-                        const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
-                        nb[t] = v ? j : -1;
-                        if (v) m |= 1u << t;
+                        for (int t = 0; t < 27; ++t) {
+                            const int j = __ldg(src + t);
+                            const bool v = static_cast<uint64_t>(j) < static_cast<uint64_t>(a.n_in);
+                            nb[t] = v ? j : -1;
+                            if (v) m |= 1u << t;
+                        }
+                    } else {
+                        nb[0] = static_cast<int>(row);
+                        m = 1u;
                     }
                 } else {
-                    nb[0] = static_cast<int>(row);
-                    m = 1u;
-                }
-            } else {
 #pragma unroll 9
-                for (int t = 0; t < 27; ++t) nb[t] = -1;
+                    for (int t = 0; t < 27; ++t) nb[t] = -1;
+                }
+                S.rows[buf * BM + r] = static_cast<int>(row);
             }
-            S.rows[buf * BM + r] = static_cast<int>(row);
+            m = __reduce_or_sync(0xffffffffu, m);
+            if (lane == 0) S.wmask[buf * kProducerWarps + warp] = m;
+            asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
+            warp_arrive(&S.tile_ready[buf]);
         }
-        m = __reduce_or_sync(0xffffffffu, m);
-        if (lane == 0) S.wmask[buf * kProducerWarps + warp] = m;
-        asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
-        warp_arrive(&S.tile_ready[buf]);
         const int rot = tap_rotation(tile, a.ntaps);
         uint32_t rem = rot_mask(tile_mask(S, buf), rot);
         const int nst = __popc(rem) * C::KCH;

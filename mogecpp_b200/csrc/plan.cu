@@ -110,6 +110,41 @@ __global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, TapBits tb,
     vals[i] = i;
 }
 
+// One block per 128-row tile, 16 warps of 8 rows, lane t = tap t: each
+// row's voxel, its neighbour list with -1 for missing taps (8 rows of loads
+// in flight per warp), and the tile's tap mask (ballots OR-ed in shared
+// memory, one plain store per tile).
+constexpr int kTileListWarps = 16;
+__global__ void __launch_bounds__(32 * kTileListWarps)
+    tile_lists_kernel(const int* __restrict__ order, const int* __restrict__ nbr, int n, PlanTiles T) {
+    constexpr int RPW = kPlanTileRows / kTileListWarps;
+    __shared__ uint32_t smask;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) smask = 0u;
+    __syncthreads();
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kPlanTileRows + warp * RPW;
+    int v[RPW], j[RPW];
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) v[u] = r0 + u < n ? __ldg(order + r0 + u) : -1;
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) j[u] = (v[u] >= 0 && lane < 27) ? __ldg(nbr + static_cast<int64_t>(v[u]) * 27 + lane) : -1;
+    uint32_t m = 0;
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) {
+        const bool ok = lane < 27 && static_cast<unsigned>(j[u]) < static_cast<unsigned>(n);
+        if (lane < 27) T.nbr[(r0 + u) * 27 + lane] = ok ? j[u] : -1;
+        m |= __ballot_sync(0xffffffffu, ok);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int u = 0; u < RPW; ++u) T.rows[r0 + u] = v[u];
+        if (m) atomicOr(&smask, m);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) T.mask[blockIdx.x] = smask;
+}
+
 __global__ void plan_header_kernel(PlanHeader* h, int64_t n, int64_t max_desc, int64_t pool_cap) {
     h->magic = kPlanMagic;
     h->n = n;
@@ -263,10 +298,31 @@ int64_t plan_max_desc(int64_t n) { return 16 * ((n + kBlockRows - 1) / kBlockRow
 // (+ up to 3 entries of padding per subtile).
 int64_t plan_pool_cap(int64_t n) { return 8 * n + 4 * plan_max_desc(n) + 65536; }
 
-size_t plan_bytes(int64_t n) {
+namespace {
+size_t plan_base_bytes(int64_t n) {
     return align256(sizeof(PlanHeader)) + align256(static_cast<size_t>(n) * 4) +
            align256(static_cast<size_t>(plan_max_desc(n)) * 16) + align256(static_cast<size_t>(n) * 27 * 2) +
            align256(static_cast<size_t>(n) * 4) + align256(static_cast<size_t>(plan_pool_cap(n)) * 4);
+}
+int64_t tiles_of(int64_t n) { return (n + kPlanTileRows - 1) / kPlanTileRows; }
+}  // namespace
+
+PlanTiles plan_tiles(uint8_t* plan, int64_t n) {
+    const int64_t np = tiles_of(n) * kPlanTileRows;
+    uint8_t* p = plan + plan_base_bytes(n);
+    PlanTiles t;
+    t.rows = reinterpret_cast<int*>(p);
+    p += align256(static_cast<size_t>(np) * 4);
+    t.nbr = reinterpret_cast<int*>(p);
+    p += align256(static_cast<size_t>(np) * 27 * 4);
+    t.mask = reinterpret_cast<uint32_t*>(p);
+    return t;
+}
+
+size_t plan_bytes(int64_t n) {
+    const int64_t np = tiles_of(n) * kPlanTileRows;
+    return plan_base_bytes(n) + align256(static_cast<size_t>(np) * 4) + align256(static_cast<size_t>(np) * 27 * 4) +
+           align256(static_cast<size_t>(tiles_of(n)) * 4);
 }
 
 size_t plan_workspace_bytes(int64_t n) {
@@ -296,7 +352,11 @@ cudaError_t launch_plan_build(const int32_t* coords, const int32_t* nbr, int64_t
         uint32_t* k_in = reinterpret_cast<uint32_t*>(keys_in);
         uint32_t* k_out = reinterpret_cast<uint32_t*>(keys_out);
         mask_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(nbr, ni, tb, k_in, vals_in);
-        return cub::DeviceRadixSort::SortPairs(temp, temp_bytes, k_in, k_out, vals_in, P.order, ni, 0, 27, st);
+        cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, temp_bytes, k_in, k_out, vals_in, P.order, ni, 0, 27, st);
+        if (e != cudaSuccess) return e;
+        const PlanTiles T = plan_tiles(static_cast<uint8_t*>(plan), n);
+        tile_lists_kernel<<<static_cast<unsigned>(tiles_of(n)), 32 * kTileListWarps, 0, st>>>(P.order, nbr, ni, T);
+        return cudaGetLastError();
     }
     morton_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<const int4*>(coords), ni, keys_in, vals_in);

@@ -54,6 +54,18 @@ __host__ __device__ inline PlanView plan_view(uint8_t* plan, int64_t n, int64_t 
     return v;
 }
 
+// Tap-order plans also hold, after the sections above, the tile rows of the
+// neighbour-map conv in 128-row tiles: each tile row's voxel (-1 past n),
+// its neighbour list in tap order (-1 = missing) and each tile's tap mask,
+// laid out so that the conv stages a tile with two bulk copies.
+constexpr int kPlanTileRows = 128;
+struct PlanTiles {
+    int* rows;        // [n_pad] voxel per tile row, -1 past n
+    int* nbr;         // [n_pad][27] neighbour lists, -1 = missing
+    uint32_t* mask;   // [n_pad / 128] tap mask of each tile
+};
+PlanTiles plan_tiles(uint8_t* plan, int64_t n);
+
 int64_t plan_max_desc(int64_t n);
 int64_t plan_pool_cap(int64_t n);
 size_t plan_bytes(int64_t n);

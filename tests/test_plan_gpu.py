@@ -148,6 +148,34 @@ def test_tap_order_is_a_stable_sort_by_mask(ex, oracle, case):
     np.testing.assert_array_equal(order, np.argsort(tap_order_keys(nbr), kind="stable"))
 
 
+def test_tap_order_tile_lists(ex, oracle):
+    """A tap-order plan also stores, per 128-row tile, the rows (-1 past n),
+    their neighbour lists in tap order (-1 = missing) and the tile's tap
+    mask, after the other sections (plan.h PlanTiles)."""
+    coords = synth.small_coords(31, extent=30, grid=32)[:1000]   # ragged last tile
+    n = coords.shape[0]
+    nbr, plan = _level(ex, oracle, coords, "tap_order")
+    order = parse_plan(plan, n)["order"]
+    b = plan.cpu().numpy()
+    ntiles = (n + 127) // 128
+    npad = ntiles * 128
+    base = len(b) - _align(4 * ntiles) - _align(4 * 27 * npad) - _align(4 * npad)
+    rows = b[base:base + 4 * npad].view(np.int32)
+    off = base + _align(4 * npad)
+    tnbr = b[off:off + 4 * 27 * npad].view(np.int32).reshape(npad, 27)
+    off += _align(4 * 27 * npad)
+    mask = b[off:off + 4 * ntiles].view(np.uint32)
+    exp_rows = np.full(npad, -1, np.int32)
+    exp_rows[:n] = order
+    np.testing.assert_array_equal(rows, exp_rows)
+    exp_nbr = np.full((npad, 27), -1, np.int32)
+    sel = nbr[order]
+    exp_nbr[:n] = np.where(sel < n, sel, -1)
+    np.testing.assert_array_equal(tnbr, exp_nbr)
+    bits = (exp_nbr >= 0).reshape(ntiles, 128, 27).any(1)
+    np.testing.assert_array_equal(mask, (bits * (1 << np.arange(27))).sum(1).astype(np.uint32))
+
+
 @pytest.mark.parametrize("tag", ["f32", "f16", "q8_0"])
 @pytest.mark.parametrize("cin,cout", [(64, 64), (128, 128)])
 def test_tap_ordered_conv_matches_oracle(ex, oracle, tag, cin, cout):
