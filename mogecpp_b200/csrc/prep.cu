@@ -325,8 +325,10 @@ __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, boo
     store_halves<EPL>(planes + plane + base, lo);
 }
 
+// 4 blocks of 256 per SM for C <= 128 (64 registers, half the warp slots
+// resident: the loads of more rows in flight); C = 256 needs its registers
 template <int C>
-__global__ void act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
+__global__ void __launch_bounds__(256, C <= 128 ? 4 : 1) act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
                                    const float* beta, float eps, int silu, int mode, __half* planes,
                                    const float2* gn, const int4* coords, int nsamples) {
     const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
