@@ -107,6 +107,32 @@ __device__ __forceinline__ void load_row_vec(const void* p, int dtype, int64_t o
     }
 }
 
+// 4 x 4 transpose of 16-byte chunks within each quad of lanes (4r..4r+3):
+// afterwards lane 4r+k holds in e[j] what lane 4r+j held in e[k].  Two
+// butterfly exchanges (lane bit 1, then lane bit 0), each moving the two
+// chunks whose index bit differs from the lane's.  All 32 lanes take part.
+__device__ __forceinline__ void quad_transpose(uint4 (&e)[4]) {
+    const int l = static_cast<int>(threadIdx.x & 3);
+#pragma unroll
+    for (int mask = 2; mask >= 1; mask >>= 1) {
+        const bool up = (l & mask) != 0;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int lo = mask == 2 ? t : 2 * t;
+            const int hi = lo + mask;
+            uint4 v = up ? e[lo] : e[hi];
+            v.x = __shfl_xor_sync(0xffffffffu, v.x, mask);
+            v.y = __shfl_xor_sync(0xffffffffu, v.y, mask);
+            v.z = __shfl_xor_sync(0xffffffffu, v.z, mask);
+            v.w = __shfl_xor_sync(0xffffffffu, v.w, mask);
+            if (up)
+                e[lo] = v;
+            else
+                e[hi] = v;
+        }
+    }
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }

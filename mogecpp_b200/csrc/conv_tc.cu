@@ -35,10 +35,15 @@
 //               16-byte cp.async (8 lanes per 128-byte row, swizzled straight
 //               into the UMMA layout; sentinel rows zero-filled), completion
 //               tracked by the stage's `gathered` barrier; thread 0
-//               bulk-copies the stage's pre-swizzled B tile.
+//               bulk-copies the stage's pre-swizzled B tile.  Q8I: the
+//               gathered rows' activation block scales (16 bytes a row) are
+//               copied into the stage too, so each scale is fetched from
+//               global memory once per tile rather than by every drain warp.
 //   warp 2      TMEM allocation and the single-thread MMA issue loop.
 //   warps 3-18  drain + epilogue: TMEM lane quarter (warp % 4) x column quarter;
 //               fp32 accumulators in registers, bias / SiLU / residual / store.
+//               Q8I: a stage is released by the MMA's commit and by every drain
+//               warp once it has read the stage's scales for the tap.
 //   warp 19     publisher: once a stage's copies have landed, the proxy fence
 //               and the stage's `full` arrival (a thread with no copies of its
 //               own in flight, so the fence does not wait on them).
@@ -87,11 +92,16 @@ struct Cfg {
     static constexpr int NBR_BYTES = 2 * BM * 27 * 4;
     static constexpr int ROWS_BYTES = 2 * BM * 4;
     static constexpr int SB_BYTES = KIND == KIND_Q8I ? 27 * NBLK * COUT * 4 : 0;  // weight block scales
+    // Q8I: the gathered rows' activation block scales ride with each stage
+    // ([BM][NBLK] floats) and the drainers release the stage after reading them
+    static constexpr bool STAGED_SCALES = KIND == KIND_Q8I;
+    static constexpr int SC_STAGE = STAGED_SCALES ? BM * NBLK * 4 : 0;
     static constexpr int BAR_BYTES = 512;
-    static constexpr int FIXED = NBR_BYTES + ROWS_BYTES + SB_BYTES + BAR_BYTES;
-    static constexpr int STAGES_FIT = (kSmemLimit - 1024 - FIXED) / STAGE;
+    static constexpr int BIAS_BYTES = COUT * 4;
+    static constexpr int FIXED = NBR_BYTES + ROWS_BYTES + SB_BYTES + BIAS_BYTES + BAR_BYTES;
+    static constexpr int STAGES_FIT = (kSmemLimit - 1024 - FIXED) / (STAGE + SC_STAGE);
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
-    static constexpr int SMEM = 1024 + STAGES * STAGE + FIXED;
+    static constexpr int SMEM = 1024 + STAGES * (STAGE + SC_STAGE) + FIXED;
     static_assert(STAGES >= 2, "at least two pipeline stages");
     static_assert(ROW_BYTES % 128 == 0, "activation rows must be whole 128-byte chunks");
     static_assert(COUT % 64 == 0 && COUT <= 256, "cout must be 64..256 in steps of 64");
@@ -99,6 +109,7 @@ struct Cfg {
     static_assert(KIND != KIND_Q8F || (NA == 1 && NB == 2), "Q8F: code plane x exact weight pair");
     static_assert(KIND != KIND_Q8I || (NA == 1 && NB == 1 && CIN == 128), "Q8I: int8 planes, cin 128");
     static_assert(SMEM <= kSmemLimit, "shared memory budget");
+    static_assert(!STAGED_SCALES || (NBLK * 4 == 16 && KCH == 1), "staged scales: one 16-byte copy per row and tap");
 };
 
 struct Smem {
@@ -106,6 +117,8 @@ struct Smem {
     int* nbr;        // [2][BM*27], missing neighbour = -1
     int* rows;       // [2][BM]
     float* sB;       // [27][NBLK][COUT] weight block scales (Q8I)
+    float* sA;       // [STAGES][BM][NBLK] gathered activation block scales (Q8I)
+    float* bias;     // [COUT] output bias (zeros without one)
     uint64_t* full;
     uint64_t* empty;
     uint64_t* gathered;
@@ -244,6 +257,16 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
                     cp_async16(dst + p * C::A_PLANE, src, nbytes);
                 }
             }
+            if constexpr (C::STAGED_SCALES) {
+                // the block scales of the rows gathered for this tap (zero
+                // where the neighbour is missing or the row is padding)
+#pragma unroll
+                for (int r = t0; r < BM; r += kProducers) {
+                    const int j = S.nbr[buf * BM * 27 + r * 27 + tap];
+                    cp_async16(smem_u32(S.sA + (s * BM + r) * C::NBLK),
+                               j >= 0 ? a.a_scale + static_cast<int64_t>(j) * C::NBLK : a.a_scale, j >= 0 ? 16u : 0u);
+                }
+            }
             cp_async_mbar_arrive_noinc(&S.gathered[s]);
             ++kc;
         }
@@ -347,7 +370,7 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
     const int c_base = part * COLS;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const float oscale = static_cast<const WeightHeader*>(a.blob)->oscale;
-    int64_t g = 0;
+    int64_t g = 0, i = 0;  // accumulator groups and pipeline stages seen
     int k = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
         const int buf = k & 1;
@@ -371,19 +394,25 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
             for (int b = 0; b < C::NBLK; ++b)
                 dst[b] = j >= 0 ? __ldg(a.a_scale + static_cast<int64_t>(j) * C::NBLK + b) : 0.f;
         };
-        if (Q8) fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
+        if (Q8 && !C::STAGED_SCALES) fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
         while (rem) {
             const int tap = rot_tap(__ffs(rem) - 1, rot);
             rem &= rem - 1;
-            if (Q8) {
-#pragma unroll
-                for (int b = 0; b < C::NBLK; ++b) sa[b] = sa_next[b];
-                fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
-            }
             // Q8 kinds: when none of this warp's 32 rows has a neighbour at
             // this tap, every block sum it would read is scaled by d_a = 0:
             // keep the slot protocol, skip the loads and the arithmetic
             const bool idle = Q8 && !__any_sync(0xffffffffu, row >= 0 && nb[tap] >= 0);
+            // staged scales: this tap's stage holds the row's activation block
+            // scales until every drain warp has released it after the tap
+            const int ss = static_cast<int>(i % C::STAGES);
+            if (C::STAGED_SCALES &&
+                !wait_or_abort(&S.full[ss], static_cast<uint32_t>(i / C::STAGES) & 1, S.abort, a.status))
+                return;
+            if (!C::STAGED_SCALES && Q8) {
+#pragma unroll
+                for (int b = 0; b < C::NBLK; ++b) sa[b] = sa_next[b];
+                fetch_scales(rem ? rot_tap(__ffs(rem) - 1, rot) : -1, sa_next);
+            }
 #pragma unroll 1
             for (int grp = 0; grp < C::KCH * C::GPS; ++grp, ++g) {
                 const int slot = static_cast<int>(g % C::NACC);
@@ -395,12 +424,17 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                     warp_arrive(&S.acc_empty[slot]);
                     continue;
                 }
+                float2 sg2 = make_float2(0.f, 0.f);
+                if constexpr (C::STAGED_SCALES)
+                    sg2 = *reinterpret_cast<const float2*>(S.sA + (ss * BM + m) * C::NBLK + grp * C::BPG);
 #pragma unroll
                 for (int b = 0; b < C::BPG; ++b) {
                     const int kb = grp * C::BPG + b;  // 32-channel block (Q8 kinds)
                     // this block's activation scale (select chain keeps sa in registers)
                     float sg = 0.f;
-                    if (Q8) {
+                    if constexpr (C::STAGED_SCALES) {
+                        sg = b == 0 ? sg2.x : sg2.y;
+                    } else if (Q8) {
                         sg = sa[0];
 #pragma unroll
                         for (int bb = 1; bb < C::NBLK; ++bb) sg = kb == bb ? sa[bb] : sg;
@@ -448,9 +482,66 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                     }
                 }
             }
+            if constexpr (C::STAGED_SCALES) {
+                warp_arrive(&S.empty[ss]);
+                ++i;
+            }
         }
         // epilogue for this tile row / column slice
-        if (row >= 0) {
+        bool quad_io = false;
+        if constexpr (COLS == 32)
+            quad_io = !a.q_codes && a.y_dtype == DT_F16 && (!a.residual || a.res_dtype == DT_F16);
+        if constexpr (COLS == 32) {
+            if (quad_io) {
+                // fp16 rows through quad transposes: each load / store
+                // instruction covers 8 rows x 64 contiguous bytes (this column
+                // slice of the row) instead of 32 rows x 16 bytes
+                const int qb = lane & ~3, qk = lane & 3;
+                int rj[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) rj[j] = __shfl_sync(0xffffffffu, row, qb + j);
+                uint4 h[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) h[j] = make_uint4(0u, 0u, 0u, 0u);
+                if (a.residual) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (rj[j] >= 0)
+                            h[j] = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.residual) +
+                                                                  static_cast<int64_t>(rj[j]) * COUT + c_base)[qk];
+                    quad_transpose(h);  // h[c] = 16-byte chunk c of this lane's row
+                }
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    const float* bv = S.bias + c_base + 8 * c8;
+                    uint32_t w[4] = {h[c8].x, h[c8].y, h[c8].z, h[c8].w};
+#pragma unroll
+                    for (int e2 = 0; e2 < 4; ++e2) {
+                        float t[2];
+                        unpack2(acc[4 * c8 + e2], t[0], t[1]);
+                        const float2 r2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e2]));
+                        const float r[2] = {r2.x, r2.y};
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            t[u] *= oscale;
+                            if (a.bias) t[u] += bv[2 * e2 + u];
+                            if (a.silu_out) t[u] = silu_fast(t[u]);
+                            if (a.residual) t[u] += r[u];
+                        }
+                        const __half2 o = __floats2half2_rn(t[0], t[1]);
+                        w[e2] = *reinterpret_cast<const uint32_t*>(&o);
+                    }
+                    h[c8] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                quad_transpose(h);  // h[j] = chunk qk of row rj[j]
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (rj[j] >= 0)
+                        reinterpret_cast<uint4*>(static_cast<__half*>(a.y) + static_cast<int64_t>(rj[j]) * COUT + c_base)[qk] =
+                            h[j];
+            }
+        }
+        if (row >= 0 && !quad_io) {
             constexpr int EC = COLS < 32 ? COLS : 32;
 #pragma unroll
             for (int c0 = 0; c0 < COLS; c0 += EC) {
@@ -461,13 +552,8 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                 // was prefetched to L2 at the start of the tile)
 #pragma unroll
                 for (int e8 = 0; e8 < EC; e8 += 8) {
-                    float bv[8], rv[8];
-                    if (a.bias) {
-                        const float4* b4 = reinterpret_cast<const float4*>(a.bias + c_base + c0 + e8);
-                        const float4 t0 = __ldg(b4), t1 = __ldg(b4 + 1);
-                        bv[0] = t0.x, bv[1] = t0.y, bv[2] = t0.z, bv[3] = t0.w;
-                        bv[4] = t1.x, bv[5] = t1.y, bv[6] = t1.z, bv[7] = t1.w;
-                    }
+                    const float* bv = S.bias + c_base + c0 + e8;
+                    float rv[8];
                     if (a.residual)
                         load_row_vec<8>(a.residual, a.res_dtype, static_cast<int64_t>(row) * COUT + c_base + c0 + e8, rv);
 #pragma unroll
@@ -509,6 +595,10 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     p += C::ROWS_BYTES;
     S.sB = reinterpret_cast<float*>(p);
     p += C::SB_BYTES;
+    S.sA = reinterpret_cast<float*>(p);
+    p += C::STAGES * C::SC_STAGE;
+    S.bias = reinterpret_cast<float*>(p);
+    p += C::BIAS_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
     S.full = bars;
     S.empty = S.full + C::STAGES;
@@ -526,7 +616,8 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&S.full[s], 2);  // publisher + weight tile
             mbar_init(&S.gathered[s], 32 * kProducerWarps);
-            mbar_init(&S.empty[s], 1);
+            // the MMA's commit, plus every drain warp when the stage holds scales
+            mbar_init(&S.empty[s], C::STAGED_SCALES ? 1 + kDrainWarps : 1);
         }
         for (int s = 0; s < C::NACC; ++s) {
             mbar_init(&S.acc_full[s], 1);
@@ -551,6 +642,7 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
         const int n4 = a.ntaps * C::NBLK * COUT / 4;
         for (int e = threadIdx.x; e < n4; e += kThreads) dst[e] = __ldg(src + e);
     }
+    for (int e = threadIdx.x; e < COUT; e += kThreads) S.bias[e] = a.bias ? __ldg(a.bias + e) : 0.f;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
