@@ -133,6 +133,21 @@ __device__ __forceinline__ void quad_transpose(uint4 (&e)[4]) {
     }
 }
 
+// 2 x 2 transpose of 16-byte chunks within each pair of lanes (2r, 2r+1):
+// afterwards lane 2r+k holds in e[j] what lane 2r+j held in e[k].
+__device__ __forceinline__ void pair_transpose(uint4 (&e)[2]) {
+    const bool up = (threadIdx.x & 1) != 0;
+    uint4 v = up ? e[0] : e[1];
+    v.x = __shfl_xor_sync(0xffffffffu, v.x, 1);
+    v.y = __shfl_xor_sync(0xffffffffu, v.y, 1);
+    v.z = __shfl_xor_sync(0xffffffffu, v.z, 1);
+    v.w = __shfl_xor_sync(0xffffffffu, v.w, 1);
+    if (up)
+        e[0] = v;
+    else
+        e[1] = v;
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
@@ -165,16 +180,15 @@ __device__ __forceinline__ void store_row(void* y, int dtype, int64_t off, const
 }
 
 // Quantises one 32-channel block with ggml's x86 Q8_0 rules (d = amax/127,
-// id = 127/amax, codes rounded half to even; quants.c:302) and stores the
-// 32 int8 codes (16-byte aligned) and fp32(fp16(d)), exactly as the
-// ACT_Q8I activation preparation does.
-__device__ __forceinline__ void quantize_store_block32(const float (&v)[32], int8_t* codes, float* scale) {
+// id = 127/amax, codes rounded half to even; quants.c:302), exactly as the
+// ACT_Q8I activation preparation does: the 32 int8 codes packed into w, the
+// scale fp32(fp16(d)) returned.
+__device__ __forceinline__ float quantize_block32(const float (&v)[32], uint32_t (&w)[8]) {
     float amax = 0.0f;
 #pragma unroll
     for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    uint32_t w[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         uint32_t t = 0;
@@ -183,9 +197,16 @@ __device__ __forceinline__ void quantize_store_block32(const float (&v)[32], int
             t |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[4 * k + j], id))) & 0xffu) << (8 * j);
         w[k] = t;
     }
+    return __half2float(__float2half_rn(d));
+}
+
+// The same, storing the codes (16-byte aligned) and the scale.
+__device__ __forceinline__ void quantize_store_block32(const float (&v)[32], int8_t* codes, float* scale) {
+    uint32_t w[8];
+    const float d = quantize_block32(v, w);
     reinterpret_cast<uint4*>(codes)[0] = make_uint4(w[0], w[1], w[2], w[3]);
     reinterpret_cast<uint4*>(codes)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    *scale = __half2float(__float2half_rn(d));
+    *scale = d;
 }
 
 }  // namespace msc

@@ -488,11 +488,75 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
             }
         }
         // epilogue for this tile row / column slice
-        bool quad_io = false;
-        if constexpr (COLS == 32)
-            quad_io = !a.q_codes && a.y_dtype == DT_F16 && (!a.residual || a.res_dtype == DT_F16);
+        // rows leave through lane transposes where the format allows:
+        // 1 = fp16 (residual fp16 or none), 2 = fp32 without residual,
+        // 3 = fused Q8_0 codes; 0 = one row per lane
+        int io = 0;
         if constexpr (COLS == 32) {
-            if (quad_io) {
+            if (a.q_codes)
+                io = 3;
+            else if (a.y_dtype == DT_F16 && (!a.residual || a.res_dtype == DT_F16))
+                io = 1;
+            else if (a.y_dtype == DT_F32 && !a.residual)
+                io = 2;
+        }
+        if constexpr (COLS == 32) {
+            if (io >= 2) {
+                float v[32];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    unpack2(acc[e], v[2 * e], v[2 * e + 1]);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        float t = v[2 * e + u] * oscale;
+                        if (a.bias) t += S.bias[c_base + 2 * e + u];
+                        if (a.silu_out) t = silu_fast(t);
+                        v[2 * e + u] = t;
+                    }
+                }
+                if (io == 3) {
+                    // this thread holds one whole 32-channel block of the row:
+                    // codes through a lane-pair transpose (each store covers 16
+                    // rows x 32 bytes), the scale per row
+                    uint32_t w[8];
+                    const float d = quantize_block32(v, w);
+                    const int64_t bcol = c_base / 32;
+                    if (row >= 0) a.q_scales[static_cast<int64_t>(row) * (COUT / 32) + bcol] = d;
+                    uint4 e[2] = {make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7])};
+                    pair_transpose(e);
+                    const int pb = lane & ~1, pk = lane & 1;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int r = __shfl_sync(0xffffffffu, row, pb + j);
+                        if (r >= 0)
+                            reinterpret_cast<uint4*>(a.q_codes + (static_cast<int64_t>(r) * (COUT / 32) + bcol) * 32)[pk] =
+                                e[j];
+                    }
+                } else {
+                    // fp32 rows: two quad transposes (columns 0-15, 16-31); each
+                    // store covers 8 rows x 64 contiguous bytes
+                    const int qb = lane & ~3, qk = lane & 3;
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        uint4 h[4];
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            const float* q = v + 16 * half + 4 * c4;
+                            h[c4] = make_uint4(__float_as_uint(q[0]), __float_as_uint(q[1]), __float_as_uint(q[2]),
+                                               __float_as_uint(q[3]));
+                        }
+                        quad_transpose(h);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int r = __shfl_sync(0xffffffffu, row, qb + j);
+                            if (r >= 0)
+                                reinterpret_cast<uint4*>(static_cast<float*>(a.y) + static_cast<int64_t>(r) * COUT +
+                                                         c_base + 16 * half)[qk] = h[j];
+                        }
+                    }
+                }
+            }
+            if (io == 1) {
                 // fp16 rows through quad transposes: each load / store
                 // instruction covers 8 rows x 64 contiguous bytes (this column
                 // slice of the row) instead of 32 rows x 16 bytes
@@ -541,7 +605,7 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                             h[j];
             }
         }
-        if (row >= 0 && !quad_io) {
+        if (row >= 0 && io == 0) {
             constexpr int EC = COLS < 32 ? COLS : 32;
 #pragma unroll
             for (int c0 = 0; c0 < COLS; c0 += EC) {
