@@ -8,11 +8,16 @@
 
 namespace msc {
 
-// Bounded wait that also gives up once another role has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* abort_flag, uint32_t* status) {
+// Bounded wait that also gives up once another role has aborted.  Roles
+// that run ahead of the pipeline's pace (the gather producers, the
+// publisher) pass sleep_ns: between polls they yield their issue slots to
+// the drain warps.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* abort_flag, uint32_t* status,
+                                              uint32_t sleep_ns = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 0;; ++it) {
+        if (sleep_ns) __nanosleep(sleep_ns);
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 31u) == 31u) {
             if (*reinterpret_cast<volatile int*>(abort_flag)) return false;

@@ -67,6 +67,7 @@ constexpr int kThreads = 32 * (kProducerWarps + 2 + kDrainWarps);
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kRowsPerProducer = BM / kProducers;
 constexpr int kSmemLimit = 227 * 1024;  // max dynamic shared memory per block on sm_100
+constexpr uint32_t kLazyWaitNs = 128;    // poll interval of the producers' and the publisher's waits
 
 enum Kind : int { KIND_F = 0, KIND_Q8F = 1, KIND_Q8I = 2 };
 
@@ -164,7 +165,7 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
     int k = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++k) {
         const int buf = k & 1;
-        if (k >= 2 && !wait_or_abort(&S.tile_free[buf], ((k >> 1) - 1) & 1, S.abort, a.status)) {
+        if (k >= 2 && !wait_or_abort(&S.tile_free[buf], ((k >> 1) - 1) & 1, S.abort, a.status, kLazyWaitNs)) {
             ok = false;
             break;
         }
@@ -231,7 +232,8 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
             }
             const int s = static_cast<int>(i % C::STAGES);
             if (i >= C::STAGES &&
-                !wait_or_abort(&S.empty[s], static_cast<uint32_t>((i / C::STAGES) - 1) & 1, S.abort, a.status)) {
+                !wait_or_abort(&S.empty[s], static_cast<uint32_t>((i / C::STAGES) - 1) & 1, S.abort, a.status,
+                               kLazyWaitNs)) {
                 ok = false;
                 break;
             }
@@ -290,7 +292,8 @@ __device__ void publisher(const ConvArgs& a, const Smem& S, int64_t ntiles) {
         const int nst = __popc(tile_mask(S, buf)) * C::KCH;
         for (int st = 0; st < nst; ++st, ++i) {
             const int s = static_cast<int>(i % C::STAGES);
-            if (!wait_or_abort(&S.gathered[s], static_cast<uint32_t>(i / C::STAGES) & 1, S.abort, a.status)) return;
+            if (!wait_or_abort(&S.gathered[s], static_cast<uint32_t>(i / C::STAGES) & 1, S.abort, a.status, kLazyWaitNs))
+                return;
             fence_proxy_async();
             mbar_arrive(&S.full[s]);
         }
