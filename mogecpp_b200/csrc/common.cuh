@@ -66,6 +66,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
         : "memory");
 }
 
+// The int8 code of v * id as the low byte of a float's bits: fl(v * id) +
+// 1.5 * 2^23 rounds the product to the nearest integer, ties to even (the
+// sum's unit in the last place is 1), as cvt.rni does for |v * id| <= 2^22;
+// a negative integer k leaves k mod 256 in the low byte.
+__device__ __forceinline__ uint32_t code_bits(float v, float id) {
+    return __float_as_uint(__fadd_rn(__fmul_rn(v, id), 12582912.0f));
+}
+
+// Packs the low bytes of four code_bits words, first in the lowest byte.
+__device__ __forceinline__ uint32_t pack_code_bytes(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+    return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

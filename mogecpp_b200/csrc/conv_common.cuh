@@ -195,13 +195,9 @@ __device__ __forceinline__ float quantize_block32(const float (&v)[32], uint32_t
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        uint32_t t = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            t |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[4 * k + j], id))) & 0xffu) << (8 * j);
-        w[k] = t;
-    }
+    for (int k = 0; k < 8; ++k)
+        w[k] = pack_code_bytes(code_bits(v[4 * k], id), code_bits(v[4 * k + 1], id), code_bits(v[4 * k + 2], id),
+                               code_bits(v[4 * k + 3], id));
     return __half2float(__float2half_rn(d));
 }
 

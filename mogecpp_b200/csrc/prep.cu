@@ -291,21 +291,18 @@ __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, boo
         for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        int q[EPL];
-#pragma unroll
-        for (int k = 0; k < EPL; ++k) q[k] = __float2int_rn(__fmul_rn(v[k], id));
         if (!valid) return;
         if (mode == ACT_Q8I) {
             uint32_t w[EPL / 4];
 #pragma unroll
             for (int k = 0; k < EPL / 4; ++k)
-                w[k] = (static_cast<uint32_t>(q[4 * k]) & 0xffu) | ((static_cast<uint32_t>(q[4 * k + 1]) & 0xffu) << 8) |
-                       ((static_cast<uint32_t>(q[4 * k + 2]) & 0xffu) << 16) | (static_cast<uint32_t>(q[4 * k + 3]) << 24);
+                w[k] = pack_code_bytes(code_bits(v[4 * k], id), code_bits(v[4 * k + 1], id),
+                                       code_bits(v[4 * k + 2], id), code_bits(v[4 * k + 3], id));
             store_words<EPL / 4>(reinterpret_cast<int8_t*>(planes) + base, w);
         } else {
             __half h[EPL];
 #pragma unroll
-            for (int k = 0; k < EPL; ++k) h[k] = __int2half_rn(q[k]);
+            for (int k = 0; k < EPL; ++k) h[k] = __int2half_rn(__float2int_rn(__fmul_rn(v[k], id)));
             store_halves<EPL>(planes + base, h);
         }
         if ((j * EPL) % 32 == 0) {
