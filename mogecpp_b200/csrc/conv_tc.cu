@@ -493,11 +493,11 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
         // epilogue for this tile row / column slice
         // rows leave through lane transposes where the format allows:
         // 1 = fp16 (residual fp16 or none), 2 = fp32 without residual,
-        // 3 = fused Q8_0 codes; 0 = one row per lane
+        // 3 = fused Q8_0 codes without residual; 0 = one row per lane
         int io = 0;
         if constexpr (COLS == 32) {
             if (a.q_codes)
-                io = 3;
+                io = a.residual ? 0 : 3;
             else if (a.y_dtype == DT_F16 && (!a.residual || a.res_dtype == DT_F16))
                 io = 1;
             else if (a.y_dtype == DT_F32 && !a.residual)
