@@ -108,8 +108,12 @@ int msc_make_level(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr
  * n <= 524288 voxels; larger n fails with MSC_E_INVALID.  No context:
  * device-side failure bits go to *status (a caller-owned device word, may be
  * NULL).  The first call on a device looks up the array's device address
- * with that device current; make it before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race and must be serialised.
+ * with that device current; make it before any stream capture.  The address
+ * is cached per device for the life of the process: after a device reset
+ * (cudaDeviceReset, which destroys the primary context and the array with
+ * it) the cached address is stale and this entry point must not be called
+ * again in that process.  All calls share the array: calls that overlap on
+ * the GPU race and must be serialised.
  * No counterpart in the reference. */
 int msc_make_level_noalloc(const int32_t* coords, int64_t n, int32_t* nbr, uint32_t* status, void* stream);
 
@@ -157,30 +161,24 @@ int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int ci
  * to every conv on the level.  No counterpart in the reference (its CPU
  * gather walks the neighbour map directly, src/sparse.cpp:579-627); results
  * match the unplanned calls within the features tolerance (the tap
- * summation order differs).  Two kinds:
+ * summation order differs).  One kind:
  *   MSC_PLAN_TAP_ORDER  the voxels sorted by their 27-bit tap mask (rarest
  *                       taps first), so that each 128-row tile of the conv
- *                       runs over fewer taps; used for every weight type.
- *   MSC_PLAN_ROW_CACHE  voxels in Morton order of (x, y, z), cut into
- *                       subtiles of at most 128 rows that reference at most
- *                       384 distinct input rows, with those rows' list and a
- *                       16-bit (row, tap) -> list position map; used by the
- *                       row-cached conv (Q8_0 weights, cin = 128). */
+ *                       runs over fewer taps, with each tile's rows,
+ *                       neighbour lists and tap mask; any weight type. */
 #define MSC_PLAN_TAP_ORDER 0
-#define MSC_PLAN_ROW_CACHE 1
 
 /* Bytes of the plan buffer (256-byte aligned) and of the build workspace. */
 size_t msc_conv_plan_bytes(int64_t n);
 size_t msc_conv_plan_workspace_bytes(int64_t n);
 
-/* Builds a plan of the given kind from a level's coords and neighbour map.
- * Device failures (MSC_DEV_PLAN_OVERFLOW) are reported by msc_check. */
+/* Builds a plan from a level's neighbour map (coords is not read and may be
+ * NULL). */
 int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const int32_t* nbr, int kind, void* plan,
                         size_t plan_bytes, void* ws, size_t ws_bytes, void* stream);
 
-/* msc_sparse_conv with an optional plan (NULL = msc_sparse_conv).  With a
- * row-cache plan, Q8_0 weights and cin = 128 the row-cached conv runs and
- * nbr may be NULL; otherwise nbr is required. */
+/* msc_sparse_conv with an optional plan (NULL = msc_sparse_conv); nbr is
+ * required either way. */
 int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
                             const void* plan, const void* blob, const float* bias, void* y, int y_dtype, void* ws,
                             size_t ws_bytes, void* stream);

@@ -18,7 +18,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libmoge_sparse_cuda.so")
-SOURCES = ["topology.cu", "prep.cu", "gn.cu", "conv_tc.cu", "conv_cached.cu", "plan.cu", "ops.cu", "capi.cu",
+SOURCES = ["topology.cu", "prep.cu", "gn.cu", "conv_tc.cu", "plan.cu", "ops.cu", "capi.cu",
            "noalloc.cu"]
 HEADERS = ["common.cuh", "conv.h", "conv_common.cuh", "gn.h", "ops.h", "plan.h", "topology.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

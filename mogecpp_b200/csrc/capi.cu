@@ -141,10 +141,9 @@ msc_context::Blob blob_info(msc_ctx_t ctx, const void* blob) {
     return it->second;
 }
 
-// Operand preparation mode for a weight type; `planned` selects the row-cached
-// Q8_0 conv, which gathers int8 codes for every cin.
-int act_mode(int wtype, int x_dtype, int cin, bool planned = false) {
-    if (wtype == MSC_W_Q8_0) return (planned || msc::weight_is_i8(wtype, cin)) ? msc::ACT_Q8I : msc::ACT_Q8;
+// Operand preparation mode for a weight type.
+int act_mode(int wtype, int x_dtype, int cin) {
+    if (wtype == MSC_W_Q8_0) return msc::weight_is_i8(wtype, cin) ? msc::ACT_Q8I : msc::ACT_Q8;
     if (wtype == MSC_W_F16) return msc::ACT_FP16;
     return x_dtype == MSC_F16 ? msc::ACT_FP16 : msc::ACT_SPLIT;
 }
@@ -162,10 +161,9 @@ void need_ws(size_t have, size_t want) {
         fail(MSC_E_WORKSPACE, "workspace too small: " + std::to_string(have) + " < " + std::to_string(want));
 }
 
-// What a conv plan contributes to one conv: the row-cached kernel's plan, or
-// the tap order for the neighbour-map kernel, or nothing.
+// What a conv plan contributes to one conv: the tap order and the per-tile
+// lists for the neighbour-map kernel, or nothing.
 struct PlanUse {
-    const void* cached = nullptr;
     const int32_t* order = nullptr;
     msc::PlanTiles tiles{};
 };
@@ -198,19 +196,15 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
     a.y = y;
     a.y_dtype = y_dtype;
     if (q_out) {
-        // fused re-quantisation: the ACT_Q8I operand of the next conv
+        // fused re-quantisation: the ACT_Q8I operand of the next conv (no
+        // caller combines it with a residual; the epilogue is only built and
+        // tested without one)
+        if (residual) fail(MSC_E_UNSUPPORTED, "fused Q8_0 output with a residual is not supported");
         a.q_codes = static_cast<int8_t*>(q_out);
         a.q_scales = reinterpret_cast<float*>(static_cast<char*>(q_out) +
                                               msc::act_scale_offset(msc::ACT_Q8I, n, b.cout));
     }
     a.status = ctx->status;
-    if (pu.cached) {
-        a.blob = static_cast<const char*>(blob) + msc::weight_cached_offset(b.wtype, b.cin, b.cout, b.ntaps);
-        a.nbr = nullptr;
-        ProfScope ps(ctx, "conv_cached", st);
-        cuda_ok(msc::launch_conv_cached(a, pu.cached, st), "cached conv launch");
-        return;
-    }
     a.perm = pu.order;
     a.tile_rows = pu.tiles.rows;
     a.tile_nbr = nbr ? pu.tiles.nbr : nullptr;
@@ -220,10 +214,9 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
 }
 
 // The plan, when given, must come from msc_conv_plan_build on this context
-// for n voxels.  A tap-order plan reorders the neighbour-map conv's tiles for
-// every weight type; a row-cache plan runs the row-cached conv for Q8_0 conv
-// weights with cin = 128 and is ignored for other weights.
-PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n, const msc_context::Blob& b) {
+// for n voxels; it reorders the neighbour-map conv's tiles for every weight
+// type.
+PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n) {
     PlanUse pu;
     if (!plan) return pu;
     msc_context::Plan pl{};
@@ -235,13 +228,8 @@ PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n, const msc_context::
     }
     if (pl.n != n)
         fail(MSC_E_INVALID, "conv plan covers " + std::to_string(pl.n) + " voxels, not " + std::to_string(n));
-    if (pl.kind == MSC_PLAN_TAP_ORDER) {
-        uint8_t* pb = static_cast<uint8_t*>(const_cast<void*>(plan));
-        pu.order = msc::plan_view(pb, n, msc::plan_max_desc(n)).order;
-        pu.tiles = msc::plan_tiles(pb, n);
-    } else if (msc::weight_has_cached(b.wtype, b.cin, b.ntaps) && msc::conv_cached_supported(b.cin, b.cout)) {
-        pu.cached = plan;
-    }
+    pu.tiles = msc::plan_tiles(static_cast<uint8_t*>(const_cast<void*>(plan)), n);
+    pu.order = pu.tiles.order;
     return pu;
 }
 
@@ -424,21 +412,20 @@ int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const i
                         size_t plan_bytes, void* ws, size_t ws_bytes, void* stream) {
     return guard([&] {
         need_ctx(ctx);
-        need(kind == MSC_PLAN_TAP_ORDER || kind == MSC_PLAN_ROW_CACHE, "unknown plan kind");
+        (void)coords;
+        need(kind == MSC_PLAN_TAP_ORDER, "unknown plan kind");
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         need(plan != nullptr, "null plan pointer");
         need_aligned(plan, 256, "plan");
         need_ws(plan_bytes, msc::plan_bytes(n));
         if (n > 0) {
-            need(coords && nbr && ws, "null pointer");
-            need_aligned(coords, 16, "coords");
+            need(nbr && ws, "null pointer");
             need_aligned(ws, 256, "workspace");
             need_ws(ws_bytes, msc::plan_workspace_bytes(n));
         }
         {
             ProfScope ps(ctx, "plan_build", S(stream));
-            cuda_ok(msc::launch_plan_build(coords, nbr, n, kind, plan, ws, ctx->status, S(stream)),
-                    "plan build launch");
+            cuda_ok(msc::launch_plan_build(nbr, n, plan, ws, S(stream)), "plan build launch");
         }
         std::lock_guard<std::mutex> lk(ctx->mu);
         ctx->plans[plan] = msc_context::Plan{n, kind};
@@ -456,12 +443,12 @@ int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n
         check_conv_shape(b, cin, 27);
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0) return;
-        const PlanUse pl = use_plan(ctx, plan, n, b);
-        need(x && (nbr || pl.cached) && y && ws, "null pointer");
+        const PlanUse pl = use_plan(ctx, plan, n);
+        need(x && nbr && y && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(y, 16, "y");
         need_aligned(ws, 256, "workspace");
-        const int mode = act_mode(b.wtype, x_dtype, b.cin, pl.cached != nullptr);
+        const int mode = act_mode(b.wtype, x_dtype, b.cin);
         need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
@@ -519,31 +506,30 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
         need(w1.cout == c && w2.cout == c, "res_block convs must map c -> c");
         need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0) return;
-        const PlanUse p1 = use_plan(ctx, plan, n, w1);
-        const PlanUse p2 = use_plan(ctx, plan, n, w2);
-        need(x && ((p1.cached && p2.cached) || nbr) && ws, "null pointer");
+        const PlanUse pl = use_plan(ctx, plan, n);
+        need(x && nbr && ws, "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(ws, 256, "workspace");
         const size_t planes_bytes = align256(static_cast<size_t>(n) * c * 4);
         need_ws(ws_bytes, planes_bytes + static_cast<size_t>(n) * c * 4);
         void* planes = ws;
         float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
-        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1.cached != nullptr);
+        const int m1 = act_mode(w1.wtype, x_dtype, w1.cin);
         cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, norm_w, norm_b, 1e-6f, 1, m1, planes, S(stream)),
                 "norm1 prepare");
-        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2.cached != nullptr);
-        if (m2 == msc::ACT_Q8I && !p1.cached && c == 128) {
+        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin);
+        if (m2 == msc::ACT_Q8I && c == 128) {
             // conv1's epilogue quantises SiLU(conv1 + b1) for conv2 in place of
             // an fp32 intermediate and a separate preparation pass (same ggml
             // quantiser, same values: identical operand)
-            run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1, h);
-            run_conv(ctx, h, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);
+            run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), pl, h);
+            run_conv(ctx, h, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), pl);
             return;
         }
-        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), p1);
+        run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 1, nullptr, 0, h, MSC_F32, S(stream), pl);
         cuda_ok(act_prepare(ctx, h, MSC_F32, n, c, 0, nullptr, nullptr, 0.f, 0, m2, planes, S(stream)),
                 "conv2 prepare");
-        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), p2);
+        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, S(stream), pl);
     });
 }
 
@@ -565,9 +551,8 @@ int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_s
         need(nsamples >= 1 && nsamples <= (1 << 20), "nsamples out of range");
         need(eps > 0.0f, "eps must be positive");
         if (n == 0 && !allreduce) return;
-        const PlanUse p1 = use_plan(ctx, plan, n, w1);
-        const PlanUse p2 = use_plan(ctx, plan, n, w2);
-        need(stats && ws && (n == 0 || (x && coords && ((p1.cached && p2.cached) || nbr))), "null pointer");
+        const PlanUse pl = use_plan(ctx, plan, n);
+        need(stats && ws && (n == 0 || (x && coords && nbr)), "null pointer");
         need_aligned(x, 16, "x");
         need_aligned(coords, 16, "coords");
         need_aligned(stats, 8, "stats");
@@ -584,9 +569,9 @@ int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_s
         };
         // conv1 + b1 on the raw features
         if (n > 0) {
-            const int m1 = act_mode(w1.wtype, x_dtype, w1.cin, p1.cached != nullptr);
+            const int m1 = act_mode(w1.wtype, x_dtype, w1.cin);
             cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 0, nullptr, nullptr, 0.f, 0, m1, planes, st), "conv1 prepare");
-            run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 0, nullptr, 0, h, MSC_F32, st, p1);
+            run_conv(ctx, planes, m1, n, c, nbr, w1, blob1, b1, 0, nullptr, 0, h, MSC_F32, st, pl);
         }
         // sample-wide statistics of the owned rows (sums, counts, sums of
         // squares), summed over the ranks by the hook
@@ -604,14 +589,14 @@ int msc_res_block_gn(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int64_t n_s
         }
         // GroupNorm + SiLU fused into conv2's operand preparation, then
         // conv2 + b2 + x into x
-        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin, p2.cached != nullptr);
+        const int m2 = act_mode(w2.wtype, MSC_F32, w2.cin);
         {
             ProfScope ps(ctx, "act_prepare", st);
             cuda_ok(msc::launch_act_prepare(h, MSC_F32, n, c, 0, gn_w, gn_b, eps, 1, m2, planes, st, gn, coords,
                                             nsamples),
                     "GroupNorm apply");
         }
-        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, st, p2);
+        run_conv(ctx, planes, m2, n, c, nbr, w2, blob2, b2, 0, x, x_dtype, x, x_dtype, st, pl);
     });
 }
 

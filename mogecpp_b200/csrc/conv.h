@@ -27,8 +27,7 @@ struct WeightHeader {
     int32_t planes;
     float oscale;     // multiply accumulators by this (power of two)
     float amax;       // max |dequantised weight|
-    uint32_t cached_off;  // Q8_0: byte offset of the row-cached conv section, else 0
-    uint32_t reserved[55];
+    uint32_t reserved[56];
 };
 static_assert(sizeof(WeightHeader) == 256, "header is 256 bytes");
 constexpr uint32_t kWeightMagic = 0x4d534357u;  // "WCSM"
@@ -40,12 +39,6 @@ constexpr uint32_t kWeightMagic = 0x4d534357u;  // "WCSM"
 bool weight_is_i8(int wtype, int cin);
 int weight_planes(int wtype, int cin);
 size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps);
-// Q8_0 conv weights with cin = 128 also carry, at this byte offset, the
-// operand of the row-cached conv (conv_cached.cu): per tap, int8 codes
-// [cout][128] (128-byte swizzled rows) then fp32 block scales [4][cout].
-// 0 for other weights.
-bool weight_has_cached(int wtype, int cin, int ntaps);
-size_t weight_cached_offset(int wtype, int cin, int cout, int ntaps);
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob, cudaStream_t st);
 
 int act_planes(int mode);
@@ -94,18 +87,12 @@ struct ConvArgs {
     // When set (cout = 128), the output is re-quantised for the next Q8_0
     // conv instead of stored in y: int8 codes [rows][cout] and fp32(fp16(d))
     // block scales [rows][cout/32] of ggml's x86 quantiser (the ACT_Q8I
-    // operand).  Only the neighbour-map kernel (conv_tc.cu) supports it.
+    // operand).
     int8_t* q_codes;
     float* q_scales;
     uint32_t* status;
 };
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t st);
-// Row-cached Q8_0 conv over a conv plan (plan.h), cin = 128 and cout 64 or
-// 128; a.planes are ACT_Q8I int8 codes, a.blob points at the blob's
-// row-cached section, a.nbr / a.perm / a.row_begin are unused (the plan
-// orders the rows).
-bool conv_cached_supported(int cin, int cout);
-cudaError_t launch_conv_cached(const ConvArgs& a, const void* plan, cudaStream_t st);
 bool conv_supported(int cin, int cout);
 
 }  // namespace msc

@@ -40,12 +40,16 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
     if (static_cast<int>(threadIdx.x & 31) == __ffs(m) - 1) mbar_arrive(bar);
 }
 
-// Taps are visited in a per-tile rotated order so that the CTAs, which all
-// stream the same small weight tensor, do not request the same weight tile
-// from L2 at the same moment.  rot_mask() rotates the tap mask so that bit 0
-// is tap `r`; rot_tap() maps a rotated bit back to the tap.
+// Taps are visited in ascending order in every tile.  A row's output is
+// then the fp32 sum of its taps' block products in one fixed order, whatever
+// tile the row lands in, so a tap-order plan, a different tiling or a z-slab
+// split over GPUs gives bit-identical rows.  (Rotating the order per tile
+// spreads the CTAs' requests for the same weight tile over time, but makes
+// the rounding depend on the tile.)  rot_mask() / rot_tap() map the tile's
+// mask to the visiting order and a visited bit back to its tap.
+constexpr bool kRotateTaps = false;
 __device__ __forceinline__ int tap_rotation(int64_t tile, int ntaps) {
-    return ntaps == 27 ? static_cast<int>(tile % 27) : 0;
+    return (kRotateTaps && ntaps == 27) ? static_cast<int>(tile % 27) : 0;
 }
 __device__ __forceinline__ uint32_t rot_mask(uint32_t m, int r) {
     return r ? ((m >> r) | (m << (27 - r))) & 0x7ffffffu : m;

@@ -56,6 +56,8 @@
 #include "conv.h"
 #include "conv_common.cuh"
 
+#include <mutex>
+
 namespace msc {
 namespace {
 
@@ -127,6 +129,7 @@ struct Smem {
     uint64_t* acc_empty;
     uint64_t* tile_ready;  // [2]
     uint64_t* tile_free;   // [2]
+    uint64_t* drained;     // MMA completion on the abort path (before TMEM release)
     uint32_t* wmask;       // [2][kProducerWarps]
     uint32_t* tmem;
     int* abort;
@@ -274,7 +277,14 @@ __device__ void producer(const ConvArgs& a, const Smem& S, int64_t ntiles) {
         }
     }
     cp_async_wait_all();
-    (void)ok;
+    if (!ok && t0 == 0) {
+        // aborted: the weight-tile bulk copies this thread issued complete on
+        // `full` barriers that may never finish their phase now; a bulk copy
+        // of at most 32 KB lands within microseconds, so wait 100 us before
+        // the CTA (and its shared memory) can go away
+        const uint64_t t_end = global_timer_ns() + 100000ull;
+        while (global_timer_ns() < t_end) __nanosleep(1000);
+    }
 }
 
 // Publishes each stage to the MMA issuer once the producers' copies have
@@ -674,7 +684,8 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     S.acc_empty = S.acc_full + C::NACC;
     S.tile_ready = S.acc_empty + C::NACC;
     S.tile_free = S.tile_ready + 2;
-    S.wmask = reinterpret_cast<uint32_t*>(S.tile_free + 2);
+    S.drained = S.tile_free + 2;
+    S.wmask = reinterpret_cast<uint32_t*>(S.drained + 1);
     S.tmem = S.wmask + 2 * kProducerWarps;
     S.abort = reinterpret_cast<int*>(S.tmem + 1);
 
@@ -694,6 +705,7 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
             mbar_init(&S.tile_ready[b], kProducerWarps);
             mbar_init(&S.tile_free[b], kDrainWarps);
         }
+        mbar_init(S.drained, 1);
         *S.abort = 0;
         fence_mbar_init();
     }
@@ -732,6 +744,16 @@ __global__ void __maxnreg__(96) conv_tc_kernel(const ConvArgs a) {
     __syncthreads();
     if (warp == kProducerWarps) {
         tc_fence_after();
+        if (*reinterpret_cast<volatile int*>(S.abort)) {
+            // a role gave up after a wait ran out: MMAs the issuer sent before
+            // it stopped may still be writing TMEM; a commit tracks all of
+            // them, so wait (bounded) for it before releasing the columns
+            if ((threadIdx.x & 31) == 0) {
+                umma_commit(S.drained);
+                (void)mbar_wait(S.drained, 0);
+            }
+            __syncwarp();
+        }
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
@@ -740,21 +762,29 @@ template <int CIN, int COUT, int NA, int NB, int KIND>
 cudaError_t launch_t(const ConvArgs& a, cudaStream_t st) {
     using C = Cfg<CIN, COUT, NA, NB, KIND>;
     auto kern = conv_tc_kernel<CIN, COUT, NA, NB, KIND>;
+    // per device and instantiation: the shared-memory opt-in and the SM
+    // count, set up once under a lock (host threads may launch concurrently)
+    static std::mutex mu;
     static int num_sms[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!num_sms[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
-        int sms = 0;
-        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        num_sms[dev] = sms;
+    int sms = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!num_sms[dev]) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+            if (e != cudaSuccess) return e;
+            int count = 0;
+            e = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+            num_sms[dev] = count;
+        }
+        sms = num_sms[dev];
     }
     const int64_t ntiles = (a.n + BM - 1) / BM;
-    const unsigned grid = static_cast<unsigned>(ntiles < num_sms[dev] ? ntiles : num_sms[dev]);
+    const unsigned grid = static_cast<unsigned>(ntiles < sms ? ntiles : sms);
     kern<<<grid, kThreads, C::SMEM, st>>>(a);
     return cudaGetLastError();
 }

@@ -119,32 +119,6 @@ __global__ void weight_q8i_kernel(const BlockQ8* w, int cin, int cout, int ntaps
     }
 }
 
-// Q8_0 weights for the row-cached conv (conv_cached.cu), one record per tap
-// so that a single bulk copy brings a tap in: int8 codes [cout][128] in
-// 128-byte swizzled rows, then fp32(fp16(d)) block scales [cin/32][cout].
-__global__ void weight_q8c_kernel(const BlockQ8* w, int cin, int cout, int ntaps, uint8_t* out) {
-    const int64_t nblocks = static_cast<int64_t>(cout) * ntaps * (cin / 32);
-    const int64_t tap_bytes = static_cast<int64_t>(cout) * cin + static_cast<int64_t>(cin / 32) * cout * 4;
-    for (int64_t bi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; bi < nblocks;
-         bi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t per_row = static_cast<int64_t>(ntaps) * (cin / 32);
-        const int o = static_cast<int>(bi / per_row);
-        const int64_t rb = bi % per_row;
-        const int t = static_cast<int>(rb / (cin / 32));
-        const int b = static_cast<int>(rb % (cin / 32));
-        const BlockQ8 blk = w[bi];
-        uint8_t* rec = out + t * tap_bytes;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            const int ci = b * 32 + e;
-            reinterpret_cast<int8_t*>(rec)[sw128_offset(o, ci >> 4) + (ci & 15)] = blk.qs[e];
-        }
-        reinterpret_cast<float*>(rec + static_cast<int64_t>(cout) * cin)[b * cout + o] = __half2float(blk.d);
-    }
-}
-
-__global__ void weight_cached_off_kernel(WeightHeader* h, uint32_t off) { h->cached_off = off; }
-
 // EPL consecutive 32-bit words <-> memory at p, in the widest aligned
 // accesses (the row part of a lane is EPL elements at an EPL-aligned offset).
 template <int NW>
@@ -357,26 +331,11 @@ bool weight_is_i8(int wtype, int cin) { return wtype == WT_Q8_0 && cin == 128; }
 
 int weight_planes(int wtype, int cin) { return (wtype == WT_F16 || weight_is_i8(wtype, cin)) ? 1 : 2; }
 
-namespace {
-size_t base_blob_bytes(int wtype, int cin, int cout, int ntaps) {
+size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
     if (weight_is_i8(wtype, cin))
         return sizeof(WeightHeader) + static_cast<size_t>(ntaps) * cin * cout +
                static_cast<size_t>(ntaps) * (cin / 32) * cout * 4;
     return sizeof(WeightHeader) + static_cast<size_t>(weight_planes(wtype, cin)) * ntaps * cin * cout * 2;
-}
-}  // namespace
-
-bool weight_has_cached(int wtype, int cin, int ntaps) { return wtype == WT_Q8_0 && cin == 128 && ntaps == 27; }
-
-size_t weight_cached_offset(int wtype, int cin, int cout, int ntaps) {
-    if (!weight_has_cached(wtype, cin, ntaps)) return 0;
-    return (base_blob_bytes(wtype, cin, cout, ntaps) + 255) / 256 * 256;
-}
-
-size_t weight_blob_bytes(int wtype, int cin, int cout, int ntaps) {
-    if (!weight_has_cached(wtype, cin, ntaps)) return base_blob_bytes(wtype, cin, cout, ntaps);
-    return weight_cached_offset(wtype, cin, cout, ntaps) +
-           static_cast<size_t>(ntaps) * (static_cast<size_t>(cin) * cout + static_cast<size_t>(cin / 32) * cout * 4);
 }
 
 cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, int ntaps, void* blob,
@@ -385,14 +344,6 @@ cudaError_t launch_weight_prepare(int wtype, const void* w, int cin, int cout, i
     const int planes = weight_planes(wtype, cin);
     const int64_t row_len = static_cast<int64_t>(ntaps) * cin;
     weight_header_kernel<<<1, 1, 0, st>>>(h, wtype, cin, cout, ntaps, planes);
-    if (weight_has_cached(wtype, cin, ntaps)) {
-        const size_t off = weight_cached_offset(wtype, cin, cout, ntaps);
-        const int64_t nblocks = row_len / 32 * cout;
-        const unsigned grid = static_cast<unsigned>(std::min<int64_t>((nblocks + 255) / 256, 148 * 16));
-        weight_cached_off_kernel<<<1, 1, 0, st>>>(h, static_cast<uint32_t>(off));
-        weight_q8c_kernel<<<grid, 256, 0, st>>>(static_cast<const BlockQ8*>(w), cin, cout, ntaps,
-                                                static_cast<uint8_t*>(blob) + off);
-    }
     if (weight_is_i8(wtype, cin)) {
         const int64_t nblocks = row_len / 32 * cout;
         const unsigned grid = static_cast<unsigned>(std::min<int64_t>((nblocks + 255) / 256, 148 * 16));

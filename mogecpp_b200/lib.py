@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(PKG, "libmoge_sparse_cuda.so")
 
 MSC_OK = 0
 MSC_F32, MSC_F16, MSC_BF16 = 0, 1, 2
-MSC_PLAN_TAP_ORDER, MSC_PLAN_ROW_CACHE = 0, 1
+MSC_PLAN_TAP_ORDER = 0
 MSC_W_F32, MSC_W_F16, MSC_W_Q8_0 = 0, 1, 8
 DEV_TIMEOUT, DEV_HASH_FULL, DEV_BAD_COORD, DEV_DUP_COORD, DEV_POOL_OVERFLOW, DEV_BAD_INDEX = 1, 2, 4, 8, 16, 32
 

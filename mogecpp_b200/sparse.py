@@ -7,7 +7,7 @@ refiner's operators with the reference's names and argument meaning
 (src/sparse.cpp):
 
     make_level(coords)                    -> nbr [n, 27]          (:238-272)
-    conv_plan(coords, nbr)                -> plan (no counterpart: row-cached Q8_0 conv)
+    conv_plan(coords, nbr)                -> plan (no counterpart: tap-ordered conv tiles)
     downsample(coords)                    -> Transition           (:312-357)
     sparse_conv(x, nbr, w, bias)          -> y [n, cout]          (:579-627)
     res_block(x, nbr, block)              -> x (in place)         (:629-642)
@@ -51,6 +51,7 @@ class Transition:
     up_rows: torch.Tensor     # [nfine] int32
     np: int
     nfine: int
+    np_dev: torch.Tensor | None = None  # [1] int32 parent count on the device
 
 
 @dataclass
@@ -127,7 +128,10 @@ class SparseCudaExecutor:
         L.check(self.lib.msc_make_level(self.ctx, _p(coords), n, _p(nbr), _p(ws), wsb, _stream()))
         return nbr
 
-    def downsample(self, coords: torch.Tensor) -> Transition:
+    def downsample(self, coords: torch.Tensor, sync: bool = True) -> Transition:
+        """Stride-2 maps.  With sync=False the parent count stays on the
+        device (no stream sync): the returned tensors are then sized for the
+        worst case (np = nfine) and ``np`` is -1; read ``np_dev``."""
         n = coords.shape[0]
         dev = coords.device
         parent = torch.empty((max(n, 1), 4), dtype=torch.int32, device=dev)
@@ -139,21 +143,22 @@ class SparseCudaExecutor:
         ws = self.workspace(wsb)
         np_host = C.c_int64(0)
         L.check(self.lib.msc_downsample(self.ctx, _p(coords), n, _p(parent), _p(np_dev), _p(pool), _p(inv), _p(up),
-                                        C.byref(np_host), _p(ws), wsb, _stream()))
+                                        C.byref(np_host) if sync else None, _p(ws), wsb, _stream()))
+        if not sync:
+            return Transition(parent, pool, inv, up[:n], -1, n, np_dev)
         m = np_host.value
-        return Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n)
+        return Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n, np_dev)
 
     def conv_plan(self, coords: torch.Tensor, nbr: torch.Tensor, kind: str = "tap_order") -> torch.Tensor:
         """Conv plan of a level (``msc_conv_plan_build``) for sparse_conv /
-        res_block on the same level: "tap_order" (tiles of rows with similar
-        neighbourhoods, any weights) or "row_cache" (the row-cached Q8_0
-        conv)."""
+        res_block on the same level: the voxels in tiles of rows with similar
+        neighbourhoods (any weights)."""
         n = coords.shape[0]
         pb = self.lib.msc_conv_plan_bytes(n)
         plan = torch.empty(pb, dtype=torch.uint8, device=coords.device)
         wsb = self.lib.msc_conv_plan_workspace_bytes(n)
         ws = self.workspace(wsb)
-        code = {"tap_order": L.MSC_PLAN_TAP_ORDER, "row_cache": L.MSC_PLAN_ROW_CACHE}[kind]
+        code = {"tap_order": L.MSC_PLAN_TAP_ORDER}[kind]
         L.check(self.lib.msc_conv_plan_build(self.ctx, _p(coords), n, _p(nbr), code, _p(plan), pb, _p(ws), wsb,
                                              _stream()))
         return plan

@@ -33,14 +33,11 @@ def test_abi_version():
 def test_size_queries_are_host_only():
     from mogecpp_b200 import lib as L
     lib = L.load()
-    # Q8_0 with cin 128: int8 tiles + block scales, then at a 256-byte
-    # boundary the row-cached conv's per-tap records (codes, then scales);
-    # Q8_0 with cin 64: an exact fp16 hi/lo pair, no row-cached section
+    # Q8_0 with cin 128: int8 tiles + block scales; Q8_0 with cin 64: an
+    # exact fp16 hi/lo pair
     def r256(v):
         return (v + 255) // 256 * 256
-    cached128 = 27 * (128 * 128 + 4 * 128 * 4)
-    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == \
-        r256(256 + 27 * 128 * 128 + 27 * 4 * 128 * 4) + cached128
+    assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 128, 27) == 256 + 27 * 128 * 128 + 27 * 4 * 128 * 4
     assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 128, 64, 1) == 256 + 128 * 64 + 4 * 64 * 4
     assert lib.msc_weight_blob_bytes(L.MSC_W_Q8_0, 64, 64, 27) == 256 + 2 * 27 * 64 * 64 * 2
     assert lib.msc_weight_blob_bytes(L.MSC_W_F32, 64, 64, 27) == 256 + 2 * 27 * 64 * 64 * 2
@@ -48,10 +45,11 @@ def test_size_queries_are_host_only():
     assert lib.msc_weight_blob_bytes(99, 64, 64, 27) == 0
     assert lib.msc_topology_workspace_bytes(1000) > 2048 * 16
     assert lib.msc_op_workspace_bytes(1000, 128) >= 1000 * 128 * 8
-    # conv plan: header + perm + descriptors + (row, tap) slots + U-list pool
-    assert lib.msc_conv_plan_bytes(1000) >= 1000 * 4 + 1000 * 27 * 2 + 4 * 1000 * 4
+    # conv plan: header + order + tile rows + tile neighbour lists + tile masks
+    npad = 8 * 128
+    assert lib.msc_conv_plan_bytes(1000) == r256(16) + r256(4000) + r256(4 * npad) + r256(4 * 27 * npad) + r256(4 * 8)
     assert lib.msc_conv_plan_bytes(-1) == 0
-    assert lib.msc_conv_plan_workspace_bytes(1000) >= 1000 * 20
+    assert lib.msc_conv_plan_workspace_bytes(1000) >= 1000 * 12
     # GroupNorm statistics: 32 sums, 1 count, 32 squared deviations per sample
     assert lib.msc_gn_stats_doubles(3) == 3 * 65
     assert lib.msc_gn_stats_doubles(0) == 0
