@@ -15,6 +15,11 @@ Workloads (seeded synthetic surfaces, mogecpp_b200/synth.py):
 * ``unet_c64`` - one encoder-decoder level, batch 2 (two surfaces):
   conv 64 -> pool + linear 64->128 -> conv 128 -> linear + nearest up + skip,
   bf16 activations, fp32 weights.
+* ``refine_640x480`` - one whole refiner pass (SparseRefiner::refine_once):
+  a five-level refiner (channels 64/64/128/128/128, F16 weights as the
+  converter stores refiner tensors) on a 640 x 480 point map; two point maps
+  alternate so that every pass rebuilds its topology, as the refine loop's
+  passes do when log z moves.
 
 One step = rebuild the topology (as the refiner does on every refine pass)
 and run the workload's operators.  ``value`` is active voxels x sparse convs
@@ -62,6 +67,7 @@ WORKLOADS = {
     "topo_4m": dict(kind="topo", coords="topo_4m_coords", grid=1024),
     "conv_c64": dict(kind="conv", coords="conv_c64_coords", grid=128, c=64),
     "unet_c64": dict(kind="unet", coords="unet_coords", grid=256),
+    "refine_640x480": dict(kind="refine", width=640, height=480, grid=None),
 }
 # DRAM bytes per voxel of one sparse-conv launch, by residual-block kind:
 # dram__bytes_read.sum + dram__bytes_write.sum from ncu captures of a block's
@@ -274,11 +280,27 @@ def run_reference(args):
         return
     from mogecpp_b200 import synth
     w = WORKLOADS[args.workload]
-    coords = getattr(synth, w["coords"])()
+    coords = getattr(synth, w["coords"])() if "coords" in w else np.zeros((0, 4), np.int32)
     threads = os.cpu_count() or 1
     R, kind, cores = open_reference(threads)
     budget = 150.0 / max(1, args.steps + args.warmup)   # seconds per step so the run ends in minutes
-    if w["kind"] == "stack":
+    if w["kind"] == "refine":
+        img, (fa, ea, ew, eh), (fb, eb, _, _) = refine_inputs(w)
+        W_, H_ = w["width"], w["height"]
+        if kind != "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference CPU build (oracle/_ref) is not built"}))
+            return
+        cfgs = synth.REFINER_5L
+        runs = [0]
+
+        def run():
+            runs[0] += 1
+            src = (fa, ea) if runs[0] % 2 else (fb, eb)
+            return R.refine_once(img, src[0], W_, H_, src[1], ew, eh)[1]
+        units = None
+        sample = f"one refine_once pass, {W_}x{H_} point map, five-level refiner (F16 weights)"
+        cfg_n = W_ * H_
+    elif w["kind"] == "stack":
         blocks = block_params(w["blocks"], w["c"])
         x0 = synth.features_rows(2, np.arange(min(coords.shape[0], 1 << 18)), w["c"], np.float16)
         ns, _ = stack_sample(coords, x0, blocks, args.block, R, kind, min(8.0, budget))
@@ -299,6 +321,8 @@ def run_reference(args):
         if i >= args.warmup:
             times.append(sec)
     t = sum(times) / len(times)
+    if units is None:   # refine: voxel-convs of the pass, from the GPU-side level sizes when known
+        units = refine_units_cpu(img, fa, W_, H_, cfgs)
     value = units / t
     unit = "voxels/s"
     line = {"impl": "reference", "metric": workload_metric(w), "value": value, "unit": unit, "n_gpus": args.gpus,
@@ -312,6 +336,25 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def refine_units_cpu(img, fc, width, height, cfg):
+    """Voxel-convs of one refine pass: level sizes of the point map's pyramid
+    (the reference's quantize_topology_z + stride-2 chain) times the convs per
+    level."""
+    from oracle.oracle import Oracle
+    O = Oracle()
+    z = O.quantize_topology_z(fc, 256.0)
+    yy, xx = np.divmod(np.arange(width * height), width)
+    c = np.stack([yy, xx, z, 0 * z], 1).astype(np.int32)
+    L = len(cfg["model_channels"])
+    sizes = [c.shape[0]]
+    for _ in range(L - 1):
+        c = O.downsample(c)[0]
+        sizes.append(c.shape[0])
+    convs = [2 * (cfg["encoder_blocks"][l] + (cfg["decoder_blocks"][L - 2 - l] if l < L - 1 else cfg["bottleneck_blocks"]))
+             for l in range(L)]
+    return sum(n * k for n, k in zip(sizes, convs))
+
+
 def workload_metric(w):
     if w["kind"] == "topo":
         return "active voxels/s (hash build + 27-tap neighbour map + stride-2 maps)"
@@ -320,7 +363,7 @@ def workload_metric(w):
 
 def workload_ref_dtype(w):
     return {"stack": "q8_0 x fp32 (ggml CPU)", "topo": "int32 / int64 keys", "conv": "fp32 (ggml CPU)",
-            "unet": "fp32 (ggml CPU)"}[w["kind"]]
+            "unet": "fp32 (ggml CPU)", "refine": "f16 weights x fp32 state (ggml CPU)"}[w["kind"]]
 
 
 def other_step_name(w):
@@ -374,7 +417,7 @@ def run_ours(args):
 
     ex = SparseCudaExecutor(local)
     dev = torch.device("cuda", local)
-    coords = getattr(synth, w["coords"])()
+    coords = getattr(synth, w["coords"])() if "coords" in w else np.zeros((w["width"] * w["height"], 4), np.int32)
     n = coords.shape[0]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
@@ -445,7 +488,7 @@ def run_ours(args):
             "metric": workload_metric(w), "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": W["dtype"], "data": "synthetic",
-            "config": {"workload": args.workload, "voxels": n, "grid": w["grid"], **W["config"],
+            "config": {"workload": args.workload, "voxels": n, "grid": w.get("grid"), **W["config"],
                        "l2": "flushed between steps (256 MiB write)"},
             "e2e": {"value": W["units"] / (e2e_t * 1e-3), "unit": "voxels/s",
                     "h2d_bytes_per_step": W["h2d_bytes"], "d2h_bytes_per_step": W["d2h_bytes"], "ms_per_step": e2e_t,
@@ -471,6 +514,7 @@ def run_ours(args):
 def e2e_run(W, args, flush, barrier):
     import torch
     h_in, d_bufs, out_dev, h_out = W["e2e_buffers"]()
+    h_ins = h_in if W.get("alternate_inputs") else [h_in]
     comp = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -487,7 +531,7 @@ def e2e_run(W, args, flush, barrier):
             with torch.cuda.stream(s_in):
                 if i == 0:
                     t0.record(s_in)
-                for d, h in zip(d_bufs[bi], h_in):
+                for d, h in zip(d_bufs[bi], h_ins[i % len(h_ins)]):
                     d.copy_(h, non_blocking=True)
                 ev_in[bi].record(s_in)
 
@@ -518,7 +562,93 @@ def e2e_run(W, args, flush, barrier):
 def build_workload(args, w, ex, dev, coords, rank, world):
     if w["kind"] == "stack":
         return build_stack(args, w, ex, dev, coords, rank, world)
+    if w["kind"] == "refine":
+        return build_refine(args, w, ex, dev)
     return build_other(args, w, ex, dev, coords)
+
+
+def refine_inputs(w):
+    from mogecpp_b200 import synth
+    cfg = synth.REFINER_5L
+    a = synth.refiner_inputs(40, w["width"], w["height"], 16, cfg["encoder_channels"])
+    b = synth.refiner_inputs(41, w["width"], w["height"], 16, cfg["encoder_channels"])
+    return synth.refiner_mogg(42, cfg, "f16"), a, b
+
+
+def build_refine(args, w, ex, dev):
+    import torch
+    from mogecpp_b200.sparse import SparseRefiner
+    img, (fa, ea, ew, eh), (fb, eb, _, _) = refine_inputs(w)
+    R = SparseRefiner(ex, img)
+    W, H = w["width"], w["height"]
+    inputs = [(torch.from_numpy(fa).to(dev), torch.from_numpy(ea).to(dev)),
+              (torch.from_numpy(fb).to(dev), torch.from_numpy(eb).to(dev))]
+    fc_d, enc_d = torch.empty_like(inputs[0][0]), torch.empty_like(inputs[0][1])
+    state = {"i": 0}
+    cfg = R.config
+    L = cfg.num_levels
+    convs = [2 * (cfg.encoder_blocks[l] + (cfg.decoder_blocks[L - 2 - l] if l < L - 1 else cfg.bottleneck_blocks))
+             for l in range(L)]
+
+    def reset():
+        src = inputs[state["i"] % 2]
+        state["i"] += 1
+        fc_d.copy_(src[0])
+        enc_d.copy_(src[1])
+
+    def step(fc_t=fc_d, enc_t=enc_d):
+        R.refine_once(fc_t, W, H, enc_t, ew, eh)
+
+    reset()
+    step()
+    sizes = R.level_sizes()
+    units = sum(n * k for n, k in zip(sizes, convs))
+
+    def e2e_buffers():
+        h_in = (torch.from_numpy(fa).pin_memory(), torch.from_numpy(ea).pin_memory())
+        h_alt = (torch.from_numpy(fb).pin_memory(), torch.from_numpy(eb).pin_memory())
+        bufs = [(torch.empty_like(fc_d), torch.empty_like(enc_d)), (torch.empty_like(fc_d), torch.empty_like(enc_d))]
+        h_out = [torch.empty_like(h_in[0]).pin_memory() for _ in range(2)]
+        # the two point maps alternate so that every pass rebuilds its topology
+        return [h_in, h_alt], bufs, (lambda bi: bufs[bi][0]), h_out
+
+    def roofline(prof):
+        peak_tf, peak_hbm, peak_src = load_peaks()
+        launches, ms = prof.get("conv_tc", (0, 0.0))
+        # F16 weights: activations rounded to fp16, one kind::f16 MMA per product
+        flops = sum(2.0 * cfg.model_channels[l] ** 2 * 27 * sizes[l] * convs[l] for l in range(L))
+        t = ms * 1e-3 / max(args.steps, 1)
+        ach = flops / t / 1e12 if launches else None
+        return {"bound": "tensor", "achieved": ach, "peak": peak_tf, "unit": "TFLOP/s",
+                "frac": ach / peak_tf if ach else None, "traffic": None,
+                "kernel": "conv_tc (F16 weights, kind::f16), all convs of a pass",
+                "peak_source": f"{peak_src} bf16 peak",
+                "flops_note": "dense-equivalent 2*C*C*27*N per conv (the tap-skipping kernel does less)"}
+
+    def launches(prof):
+        per = {"make_level": 3, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "downsample": 8}
+        # + per pass: z quantisation (3), level-0 map, input rows, input_proj,
+        # encoder rows, fuse_proj.0, SiLU, out_proj, log z update, key compare
+        return sum(per.get(k, 1) * v[0] for k, v in prof.items()) + 12 * args.steps
+
+    def cpu_baseline():
+        threads = os.cpu_count() or 1
+        Rr, kind, cores = open_reference(threads)
+        if kind != "reference":
+            return {"cpu_baseline": None}
+        Rr.refine_once(img, fa, W, H, ea, ew, eh)
+        _, sec = Rr.refine_once(img, fb, W, H, eb, ew, eh)
+        return {"cpu_baseline": {"value": units / sec, "unit": "voxels/s", "cores": cores, "kind": kind,
+                                 "sample": f"one refine_once pass of the same model on the same {W}x{H} point map"}}
+
+    return dict(step=step, reset=reset, after_warmup=lambda: None, e2e_buffers=e2e_buffers, roofline=roofline,
+                tflops=None, launches=launches, parity=lambda: None, cpu_baseline=cpu_baseline, halo_events=[],
+                units=units, h2d_bytes=int(fa.nbytes + ea.nbytes), d2h_bytes=int(fa.nbytes),
+                dtype="fp32 state, F16 weights (activations rounded to fp16 as ggml does)",
+                config={"pixels": W * H, "levels": sizes, "channels": list(cfg.model_channels[:L]),
+                        "convs_per_level": convs, "weights": "f16",
+                        "step": "refine_once: quantise log z + topology rebuild + U-Net + log z update"},
+                alternate_inputs=True)
 
 
 def build_stack(args, w, ex, dev, coords, rank, world):

@@ -127,6 +127,78 @@ int msc_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* par
                    int32_t* pool_rows, float* inv_count, int32_t* up_rows, int64_t* np_host, void* ws,
                    size_t ws_bytes, void* stream);
 
+/* Log-depth voxel bins of an image: for every pixel i (factor_coord [n][3]
+ * floats: x/z, y/z, log z), q = nearbyint(double(log z * depth_resolution))
+ * (float product, round half to even), zbin[i] = q - min(q).  Syncs; fails
+ * with MSC_E_DEVICE on a non-finite z or a bin extent beyond 2^19 - 1 (the
+ * voxel keys hold 19 bits per axis).
+ * Replaces: quantize_topology_z (src/sparse.cpp:363-406). */
+int msc_quantize_topology_z(msc_ctx_t ctx, const float* factor_coord, int64_t n, float depth_resolution,
+                            int32_t* zbin, void* stream);
+
+/* Level-0 topology of an image (one voxel per pixel): coords [n][4] =
+ * (row, column, zbin, 0) for pixel i = row * width + column, and the
+ * neighbour map nbr [n][27] from the pixel grid (a neighbour pixel is at tap
+ * (drow+1)*9 + (dcol+1)*3 + (dz+1) when its bin differs by at most 1).
+ * Replaces: make_dense_image_level (src/sparse.cpp:274-310) with the level-0
+ * coordinates of build_topology_from_key (src/sparse.cpp:408-431). */
+int msc_make_dense_image_level(msc_ctx_t ctx, const int32_t* zbin, int width, int height, int32_t* coords,
+                               int32_t* nbr, void* stream);
+
+/* ----------------------------------------------------------------- refiner
+ * The whole sparse refiner pass on the device.  Mirrors SparseRefiner
+ * (src/sparse.hpp:21-66): the configuration is SparseConfig (read from the
+ * MOGG image's refiner.* metadata, read_sparse_config src/sparse.cpp:985-1007)
+ * and refine_once (src/sparse.cpp:1014-1296) updates log z in place.
+ * Topology is cached across calls as get_topology_cached
+ * (src/sparse.cpp:443-472) does: a pass whose quantised bins equal the
+ * previous pass's reuses its levels, neighbour maps and stride-2 maps.
+ * Supported: model channels 64 or 128, downsample factors 2, F32 / F16 /
+ * Q8_0 weights, identity residual skips (others fail with
+ * MSC_E_UNSUPPORTED).  The feature state is fp32 on every level. */
+#define MSC_REFINER_MAX_LEVELS 8
+typedef struct {
+    int in_channels;
+    int out_channels;
+    int encoder_channels;
+    int num_levels;
+    int model_channels[MSC_REFINER_MAX_LEVELS];
+    int encoder_blocks[MSC_REFINER_MAX_LEVELS];
+    int decoder_blocks[MSC_REFINER_MAX_LEVELS];     /* num_levels - 1 used */
+    int downsample_factors[MSC_REFINER_MAX_LEVELS]; /* num_levels - 1 used */
+    int bottleneck_blocks;
+    int encoder_downsample;
+    float depth_resolution;
+} msc_sparse_config;
+
+typedef struct msc_refiner* msc_refiner_t;
+
+/* Loads the refiner.* tensors of a MOGG v1 image held in host memory
+ * (src/mogg.cpp:247-312; sparse conv weights "*.weight.mogg_sparse27") to the
+ * context's device and prepares them for the tensor cores.  Syncs.
+ * Replaces: SparseRefiner::SparseRefiner + WeightStore (src/sparse.cpp:1010,
+ * src/dense.cpp:198-270). */
+int msc_refiner_create(msc_ctx_t ctx, const void* mogg, size_t mogg_bytes, void* stream, msc_refiner_t* out);
+int msc_refiner_destroy(msc_refiner_t r);
+int msc_refiner_config(msc_refiner_t r, msc_sparse_config* out);
+/* Topology cache hits and misses so far (the reference's
+ * moge_sparse_topology_cache trace counters). */
+int msc_refiner_cache_stats(msc_refiner_t r, uint64_t* hits, uint64_t* misses);
+/* Voxels per level of the cached topology (count = 0 before the first pass). */
+int msc_refiner_level_sizes(msc_refiner_t r, int64_t* sizes, int capacity, int* count);
+
+/* One refine pass.  factor_coord: device [height * width][3] floats, log z
+ * updated in place; encoder_feature: device [encoder_height *
+ * encoder_width][encoder_channels] floats (the reference's [C, ew * eh]).
+ * width = encoder_width * encoder_downsample, likewise height.  Syncs.
+ * Replaces: SparseRefiner::refine_once (src/sparse.cpp:1014-1296). */
+int msc_refiner_refine_once(msc_refiner_t r, float* factor_coord, int width, int height, const float* encoder_feature,
+                            int encoder_width, int encoder_height, void* stream);
+/* The same with host buffers (copied in and out inside the call), as the
+ * reference's refine_once takes factor_coord as a host vector. */
+int msc_refiner_refine_once_host(msc_refiner_t r, float* factor_coord, int width, int height,
+                                 const float* encoder_feature, int encoder_width, int encoder_height, void* stream);
+
 /* ----------------------------------------------------------------- weights */
 
 /* Bytes of a prepared-weight blob (tensor-core layout). */

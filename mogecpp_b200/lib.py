@@ -51,6 +51,15 @@ SIGNATURES = {
     "msc_pool_down": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
     "msc_nearest_up": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _sz,
                                  _vp]),
+    "msc_quantize_topology_z": (C.c_int, [_vp, _vp, _i64, C.c_float, _vp, _vp]),
+    "msc_make_dense_image_level": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _vp, _vp]),
+    "msc_refiner_create": (C.c_int, [_vp, C.c_char_p, _sz, _vp, C.POINTER(_vp)]),
+    "msc_refiner_destroy": (C.c_int, [_vp]),
+    "msc_refiner_config": (C.c_int, [_vp, _vp]),
+    "msc_refiner_cache_stats": (C.c_int, [_vp, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "msc_refiner_level_sizes": (C.c_int, [_vp, C.POINTER(_i64), _i32, C.POINTER(_i32)]),
+    "msc_refiner_refine_once": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
+    "msc_refiner_refine_once_host": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
     "msc_profile_enable": (C.c_int, [_vp, _i32]),
     "msc_profile_read": (C.c_int, [_vp, _vp, _i32, C.POINTER(_i32)]),
 }
@@ -58,6 +67,18 @@ SIGNATURES = {
 
 # int (*)(double* buf, int64_t count, void* stream, void* user)
 ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, _vp, _i64, _vp, _vp)
+
+
+MAX_LEVELS = 8
+
+
+class SparseConfig(C.Structure):
+    """msc_sparse_config (the reference's SparseConfig, src/sparse.hpp:21-33)."""
+    _fields_ = [("in_channels", C.c_int), ("out_channels", C.c_int), ("encoder_channels", C.c_int),
+                ("num_levels", C.c_int), ("model_channels", C.c_int * MAX_LEVELS),
+                ("encoder_blocks", C.c_int * MAX_LEVELS), ("decoder_blocks", C.c_int * MAX_LEVELS),
+                ("downsample_factors", C.c_int * MAX_LEVELS), ("bottleneck_blocks", C.c_int),
+                ("encoder_downsample", C.c_int), ("depth_resolution", C.c_float)]
 
 
 class ProfileEntry(C.Structure):

@@ -15,6 +15,12 @@ refiner's operators with the reference's names and argument meaning
     pool_down(x, tr, w, bias)             -> y [np, cout]         (:646-668)
     nearest_up(x, tr, w, bias, skip)      -> y [nfine, cout]      (:670-674)
     linear(x, w, bias)                    -> y [n, cout]          (:515-518)
+    quantize_topology_z(factor_coord, r)  -> zbin [h*w]           (:363-406)
+    make_dense_image_level(zbin, w, h)    -> coords, nbr          (:274-310)
+
+``SparseRefiner`` is the refiner itself (SparseRefiner, src/sparse.hpp:41-66):
+built from a MOGG image, ``refine_once`` updates log z of a point map in
+place with every step on the GPU.
 
 Every call goes through the C ABI of ``libmoge_sparse_cuda.so``; tensors are
 torch CUDA tensors used only as device memory.  Errors raise ``MscError``
@@ -163,6 +169,24 @@ class SparseCudaExecutor:
                                              _stream()))
         return plan
 
+    def quantize_topology_z(self, factor_coord: torch.Tensor, depth_resolution: float) -> torch.Tensor:
+        """Log-depth voxel bins of an image: factor_coord [h*w, 3] float32 on
+        the device -> zbin [h*w] int32 (syncs)."""
+        n = factor_coord.shape[0]
+        z = torch.empty(n, dtype=torch.int32, device=factor_coord.device)
+        L.check(self.lib.msc_quantize_topology_z(self.ctx, _p(factor_coord), n, depth_resolution, _p(z), _stream()))
+        return z
+
+    def make_dense_image_level(self, zbin: torch.Tensor, width: int, height: int):
+        """Level 0 of the refiner's pyramid: coords [n, 4] (row, column, zbin,
+        0) and the neighbour map [n, 27] from the pixel grid."""
+        n = width * height
+        coords = torch.empty((n, 4), dtype=torch.int32, device=zbin.device)
+        nbr = torch.empty((n, 27), dtype=torch.int32, device=zbin.device)
+        L.check(self.lib.msc_make_dense_image_level(self.ctx, _p(zbin), width, height, _p(coords), _p(nbr),
+                                                    _stream()))
+        return coords, nbr
+
     # ---------------------------------------------------------- weights
     def prepare_weight(self, w: torch.Tensor, wtype: str, cin: int, cout: int, ntaps: int) -> PreparedWeight:
         """w: packed [cout, ntaps*cin] float32 / float16, or uint8 block_q8_0 rows."""
@@ -254,3 +278,54 @@ class SparseCudaExecutor:
                                         _DT[skip.dtype] if skip is not None else 0, _p(y), _DT[out_dtype], _p(ws),
                                         wsb, _stream()))
         return y
+
+
+class SparseRefiner:
+    """The MoGe-3 sparse refiner on the device (the reference's SparseRefiner,
+    src/sparse.hpp:41-66, and refine_once, src/sparse.cpp:1014-1296).
+
+    Built from a MOGG image held in memory (its refiner.* metadata and
+    tensors); the topology of the last pass is cached and reused when the
+    quantised log-depth bins are unchanged (get_topology_cached,
+    src/sparse.cpp:443-472)."""
+
+    def __init__(self, ex: SparseCudaExecutor, mogg: bytes):
+        self.ex = ex
+        self.lib = ex.lib
+        h = C.c_void_p()
+        L.check(self.lib.msc_refiner_create(ex.ctx, mogg, len(mogg), _stream(), C.byref(h)))
+        self.h = h
+        cfg = L.SparseConfig()
+        L.check(self.lib.msc_refiner_config(self.h, C.byref(cfg)))
+        self.config = cfg
+
+    def close(self):
+        if self.h:
+            self.lib.msc_refiner_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def refine_once(self, factor_coord: torch.Tensor, width: int, height: int, encoder_feature: torch.Tensor,
+                    encoder_width: int, encoder_height: int) -> torch.Tensor:
+        """factor_coord [h*w, 3] float32 (device: updated in place; host:
+        through the host-buffer entry point); encoder_feature [eh*ew, C]."""
+        fn = self.lib.msc_refiner_refine_once if factor_coord.is_cuda else self.lib.msc_refiner_refine_once_host
+        L.check(fn(self.h, _p(factor_coord), width, height, _p(encoder_feature), encoder_width, encoder_height,
+                   _stream()))
+        return factor_coord
+
+    def cache_stats(self) -> tuple[int, int]:
+        hits, misses = C.c_uint64(0), C.c_uint64(0)
+        L.check(self.lib.msc_refiner_cache_stats(self.h, C.byref(hits), C.byref(misses)))
+        return hits.value, misses.value
+
+    def level_sizes(self) -> list[int]:
+        buf = (C.c_int64 * L.MAX_LEVELS)()
+        cnt = C.c_int(0)
+        L.check(self.lib.msc_refiner_level_sizes(self.h, buf, L.MAX_LEVELS, C.byref(cnt)))
+        return [buf[i] for i in range(cnt.value)]

@@ -176,3 +176,82 @@ def describe(coords: np.ndarray) -> dict:
     return {"n": int(coords.shape[0]),
             "extent": [int(coords[:, i].max()) + 1 if coords.shape[0] else 0 for i in range(3)],
             "batch": int(coords[:, 3].max()) + 1 if coords.shape[0] else 0}
+
+
+# ------------------------------------------------------------ refiner models
+
+SMALL_REFINER = dict(model_channels=[64, 128, 128], encoder_blocks=[1, 1, 1], decoder_blocks=[1, 1],
+                     bottleneck_blocks=1, encoder_channels=64, fuse_channels=64, fuse_hidden=128)
+# A five-level refiner (four stride-2 levels, encoder_downsample 16) at the
+# channel widths the tensor-core convs run (64 / 128).
+REFINER_5L = dict(model_channels=[64, 64, 128, 128, 128], encoder_blocks=[1, 1, 1, 1, 1],
+                  decoder_blocks=[1, 1, 1, 1], bottleneck_blocks=1, encoder_channels=128, fuse_channels=128,
+                  fuse_hidden=128)
+
+
+def refiner_mogg(seed: int, cfg: dict, wdtype: str = "f32", depth_resolution: float = 256.0) -> bytes:
+    """A MOGG image of a MoGe-3 sparse refiner with seeded random weights:
+    the refiner.* metadata of SparseConfig (src/sparse.cpp:985-1007) and the
+    tensors SparseRefiner reads (sparse conv weights packed [cout][27 cin],
+    linear weights [cout][cin]).  wdtype: "f32" or "f16" weight storage
+    (biases and norm affines stay F32)."""
+    from . import mogg
+    rng = np.random.default_rng(seed)
+    wt = mogg.T_F32 if wdtype == "f32" else mogg.T_F16
+    mc = list(cfg["model_channels"])
+    L = len(mc)
+    t = []
+
+    def lin(name, cin, cout):
+        t.append(mogg.tensor(name + ".weight", rng.standard_normal((cout, cin)) / np.sqrt(cin), wt))
+        t.append(mogg.tensor(name + ".bias", 0.05 * rng.standard_normal(cout), mogg.T_F32))
+
+    def block(pfx, c):
+        t.append(mogg.tensor(pfx + ".norm1.weight", 1 + 0.1 * rng.standard_normal(c), mogg.T_F32))
+        t.append(mogg.tensor(pfx + ".norm1.bias", 0.1 * rng.standard_normal(c), mogg.T_F32))
+        for k in ("conv1", "conv2"):
+            t.append(mogg.tensor(f"{pfx}.{k}.weight.mogg_sparse27",
+                                 rng.standard_normal((c, 27 * c)) / np.sqrt(27.0 * c), wt))
+            t.append(mogg.tensor(f"{pfx}.{k}.bias", 0.05 * rng.standard_normal(c), mogg.T_F32))
+
+    lin("refiner.input_proj", 3, mc[0])
+    for lv in range(L):
+        for b in range(cfg["encoder_blocks"][lv]):
+            block(f"refiner.down_stages.{lv}.{b}", mc[lv])
+        if lv + 1 < L:
+            lin(f"refiner.downsample_blocks.{lv}.linear", mc[lv], mc[lv + 1])
+    lin("refiner.encoder_fuse", cfg["encoder_channels"], cfg["fuse_channels"])
+    lin("refiner.fuse_proj.0", mc[-1] + cfg["fuse_channels"], cfg["fuse_hidden"])
+    lin("refiner.fuse_proj.2", cfg["fuse_hidden"], mc[-1])
+    for b in range(cfg["bottleneck_blocks"]):
+        block(f"refiner.bottleneck_stage.{b}", mc[-1])
+    for u in range(L - 1):
+        tgt = L - 2 - u
+        lin(f"refiner.upsample_blocks.{u}.linear", mc[tgt + 1], mc[tgt])
+        for b in range(cfg["decoder_blocks"][u]):
+            block(f"refiner.up_stages.{u}.{b}", mc[tgt])
+    lin("refiner.out_proj", mc[0], 1)
+    meta = {"refiner.present": True, "refiner.in_channels": 3, "refiner.out_channels": 1,
+            "refiner.encoder_channels": cfg["encoder_channels"], "refiner.model_channels": mc,
+            "refiner.encoder_blocks_per_level": list(cfg["encoder_blocks"]),
+            "refiner.decoder_blocks_per_level": list(cfg["decoder_blocks"]),
+            "refiner.bottleneck_blocks": cfg["bottleneck_blocks"], "refiner.downsample_factors": [2] * (L - 1),
+            "refiner.encoder_downsample": 2 ** (L - 1), "refiner.depth_resolution": float(depth_resolution)}
+    return mogg.build(meta, t)
+
+
+def refiner_inputs(seed: int, width: int, height: int, encoder_downsample: int, encoder_channels: int):
+    """A predicted point map (factor_coord [h*w][3] = x/z, y/z, log z) of a
+    smooth depth surface with two depth steps (so that some neighbouring
+    pixels fall more than one bin apart), and a dense encoder feature matrix
+    [eh*ew][encoder_channels] ~ N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    v, u = np.meshgrid(np.arange(height, dtype=np.float64), np.arange(width, dtype=np.float64), indexing="ij")
+    z = 2.0 + 0.5 * np.sin(u / 97.0) * np.cos(v / 71.0) + 0.3 * (u > width * 0.6) - 0.2 * (v > height * 0.7)
+    z += rng.normal(0.0, 0.002, size=z.shape)
+    fx = (u - width / 2) / (0.8 * width)
+    fy = (v - height / 2) / (0.8 * width)
+    fc = np.stack([fx, fy, np.log(z)], axis=-1).reshape(-1, 3).astype(np.float32)
+    ew, eh = width // encoder_downsample, height // encoder_downsample
+    enc = rng.standard_normal((eh * ew, encoder_channels)).astype(np.float32)
+    return fc, enc, ew, eh

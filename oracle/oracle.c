@@ -497,3 +497,55 @@ void orc_nearest_up(const float *x, int64_t np, int c, const int32_t *up_rows, i
         memcpy(y + i * cout, t + (int64_t)up_rows[i] * cout, sizeof(float) * (size_t)cout);
     free(t);
 }
+
+/* ------------------------------------------------------ level-0 topology */
+
+/* quantize_topology_z (src/sparse.cpp:363-406): q = nearbyint((double)(z *
+ * depth_resolution)) with the product in float and the default rounding
+ * mode (half to even); zbin = q - min(q).  Returns 0, or -1 when the extent
+ * exceeds INT32_MAX (the reference throws). */
+int orc_quantize_topology_z(const float *coord, int64_t n, float depth_resolution, int32_t *zbin) {
+    if (n <= 0) return 0;
+    int64_t *q = (int64_t *)malloc((size_t)n * sizeof(int64_t));
+    if (!q) return -2;
+    int64_t zmin = INT64_MAX, zmax = INT64_MIN;
+    for (int64_t i = 0; i < n; ++i) {
+        const float z = coord[3 * i + 2] * depth_resolution;
+        q[i] = (int64_t)nearbyint((double)z);
+        if (q[i] < zmin) zmin = q[i];
+        if (q[i] > zmax) zmax = q[i];
+    }
+    if (zmax - zmin > INT32_MAX) {
+        free(q);
+        return -1;
+    }
+    for (int64_t i = 0; i < n; ++i) zbin[i] = (int32_t)(q[i] - zmin);
+    free(q);
+    return 0;
+}
+
+/* make_dense_image_level (src/sparse.cpp:274-310) on the level-0 coords of
+ * build_topology_from_key (:408-431): pixel i = y*width + x is voxel
+ * (y, x, zbin[i]); neighbour pixel j at (dy, dx) sits at tap
+ * (dy+1)*9 + (dx+1)*3 + (dz+1) when dz = zbin[j] - zbin[i] is in [-1, 1];
+ * other taps hold n. */
+void orc_dense_image_level(const int32_t *zbin, int32_t width, int32_t height, int32_t *nbr) {
+    const int64_t n = (int64_t)width * height;
+    for (int64_t i = 0; i < n * 27; ++i) nbr[i] = (int32_t)n;
+    for (int32_t y = 0; y < height; ++y)
+        for (int32_t x = 0; x < width; ++x) {
+            const int64_t i = (int64_t)y * width + x;
+            for (int dy = -1; dy <= 1; ++dy) {
+                const int32_t yy = y + dy;
+                if (yy < 0 || yy >= height) continue;
+                for (int dx = -1; dx <= 1; ++dx) {
+                    const int32_t xx = x + dx;
+                    if (xx < 0 || xx >= width) continue;
+                    const int64_t j = (int64_t)yy * width + xx;
+                    const int32_t dz = zbin[j] - zbin[i];
+                    if (dz < -1 || dz > 1) continue;
+                    nbr[i * 27 + (dy + 1) * 9 + (dx + 1) * 3 + (dz + 1)] = (int32_t)j;
+                }
+            }
+        }
+}

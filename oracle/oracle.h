@@ -81,6 +81,12 @@ void orc_pool_down(const float *x, int64_t nfine, int c, const int32_t *pool_row
 void orc_nearest_up(const float *x, int64_t np, int c, const int32_t *up_rows, int64_t nfine, int wtype, const void *w,
                     int cout, const float *bias, float *y);
 
+/* Log-depth bins of an image (factor_coord [n][3]); 0, or -1 when the bin
+ * extent exceeds INT32_MAX. */
+int orc_quantize_topology_z(const float *coord, int64_t n, float depth_resolution, int32_t *zbin);
+/* Level-0 neighbour map [width*height][27] from the pixel grid. */
+void orc_dense_image_level(const int32_t *zbin, int32_t width, int32_t height, int32_t *nbr);
+
 #ifdef __cplusplus
 }
 #endif

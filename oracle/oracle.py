@@ -62,6 +62,8 @@ class Oracle:
         L.orc_quantize_q8_0_act.argtypes = [_f32p, C.c_void_p, _i64]
         L.orc_fp32_to_fp16.argtypes = [C.c_float]
         L.orc_fp32_to_fp16.restype = C.c_uint16
+        L.orc_quantize_topology_z.argtypes = [_f32p, _i64, C.c_float, _i32p]
+        L.orc_dense_image_level.argtypes = [_i32p, C.c_int32, C.c_int32, _i32p]
 
     # -- weights --------------------------------------------------------
     def quantize_q8_0(self, w: np.ndarray) -> np.ndarray:
@@ -110,6 +112,18 @@ class Oracle:
             raise ValueError(f"orc_downsample failed ({rc})")
         np_ = npo.value
         return (parent[:4 * np_].reshape(np_, 4), pool[:8 * np_].reshape(8, np_), inv[:np_], up[:n])
+
+    def quantize_topology_z(self, factor_coord: np.ndarray, depth_resolution: float) -> np.ndarray:
+        fc = _c(factor_coord, np.float32).reshape(-1, 3)
+        z = np.empty(fc.shape[0], dtype=np.int32)
+        if self.lib.orc_quantize_topology_z(fc.ravel(), fc.shape[0], depth_resolution, z) != 0:
+            raise ValueError("z-bin extent overflow")
+        return z
+
+    def dense_image_level(self, zbin: np.ndarray, width: int, height: int) -> np.ndarray:
+        nbr = np.empty(27 * width * height, dtype=np.int32)
+        self.lib.orc_dense_image_level(_c(zbin, np.int32), width, height, nbr)
+        return nbr.reshape(-1, 27)
 
     # -- features -------------------------------------------------------
     def sparse_conv(self, x, nbr, w, wtype, bias=None):
@@ -216,6 +230,10 @@ class Reference:
         L.ref_nearest_up.argtypes = [C.c_int, _f32p, _i64, _i64, _i32p, _i64, C.c_int, _f32p, _i64, C.c_void_p, _f32p]
         L.ref_topology_timed.argtypes = [_i32p, C.c_int32, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]
         L.ref_group_norm.argtypes = [C.c_int, _f32p, _i64, _i64, C.c_int, C.c_float, _f32p]
+        L.ref_quantize_topology_z.argtypes = [_f32p, C.c_int32, C.c_int32, C.c_float, _i32p]
+        L.ref_make_dense_image_level.argtypes = [_i32p, C.c_int32, C.c_int32, _i32p]
+        L.ref_refine_once.argtypes = [C.c_int, C.c_char_p, C.c_size_t, _f32p, C.c_int32, C.c_int32, _f32p,
+                                      C.c_int32, C.c_int32, C.c_int, C.POINTER(C.c_double)]
 
     def _check(self, rc):
         if rc != 0:
@@ -234,6 +252,27 @@ class Reference:
         y = np.empty_like(x)
         self._check(self.lib.ref_group_norm(self.n_threads, x, x.shape[0], x.shape[1], groups, eps, y))
         return y
+
+    def quantize_topology_z(self, factor_coord, width, height, depth_resolution):
+        fc = _c(factor_coord, np.float32).reshape(-1)
+        z = np.empty(width * height, dtype=np.int32)
+        self._check(self.lib.ref_quantize_topology_z(fc, width, height, depth_resolution, z))
+        return z
+
+    def make_dense_image_level(self, zbin, width, height):
+        nbr = np.empty(27 * width * height, dtype=np.int32)
+        self._check(self.lib.ref_make_dense_image_level(_c(zbin, np.int32), width, height, nbr))
+        return nbr.reshape(-1, 27)
+
+    def refine_once(self, mogg: bytes, factor_coord, width, height, encoder_feature, ew, eh, passes=1):
+        """SparseRefiner::refine_once, `passes` times on one refiner; returns
+        (updated factor_coord [h*w][3], median seconds per pass)."""
+        fc = _c(factor_coord, np.float32).reshape(-1).copy()
+        enc = _c(encoder_feature, np.float32).reshape(-1)
+        sec = C.c_double(0.0)
+        self._check(self.lib.ref_refine_once(self.n_threads, mogg, len(mogg), fc, width, height, enc, ew, eh, passes,
+                                             C.byref(sec)))
+        return fc.reshape(-1, 3), sec.value
 
     def make_level(self, coords):
         c3 = self._xyz(coords)

@@ -19,6 +19,9 @@
 //   nearest_up          src/sparse.cpp:670-674
 //   linear, layer_norm  src/sparse.cpp:515-526
 //   run_phase           src/sparse.cpp:850-894
+//   quantize_topology_z src/sparse.cpp:363-406
+//   make_dense_image_level src/sparse.cpp:274-310
+//   SparseRefiner       src/sparse.cpp:985-1296 (read_sparse_config, refine_once)
 //   MOGG v1 layout      src/mogg.cpp:247-312 (header 40 B, metadata, tensor records)
 
 #include "sparse.cpp"
@@ -411,6 +414,66 @@ int ref_topology_timed(const int32_t * coords, int32_t n, int iters, double * ma
         std::sort(t2.begin(), t2.end());
         *make_level_s = t1[t1.size() / 2];
         *downsample_s = t2[t2.size() / 2];
+    });
+}
+
+// quantize_topology_z over factor_coord [w*h][3] with the given depth
+// resolution -> zbin [w*h].
+int ref_quantize_topology_z(const float * coord, int32_t width, int32_t height, float depth_resolution,
+                            int32_t * zbin) {
+    return guard([&] {
+        const size_t n = static_cast<size_t>(width) * height;
+        std::vector<float> fc(coord, coord + 3 * n);
+        moge::SparseConfig cfg;
+        cfg.depth_resolution = depth_resolution;
+        auto key = moge::quantize_topology_z(fc, width, height, cfg);
+        std::memcpy(zbin, key.z.data(), n * sizeof(int32_t));
+    });
+}
+
+// Level 0 of build_topology_from_key: coords (row, column, zbin) and
+// make_dense_image_level's neighbour map [w*h][27].
+int ref_make_dense_image_level(const int32_t * zbin, int32_t width, int32_t height, int32_t * nbr) {
+    return guard([&] {
+        const size_t n = static_cast<size_t>(width) * height;
+        std::vector<moge::Coord3> l0(n);
+        for (size_t i = 0; i < n; ++i) {
+            const int y = static_cast<int>(i / static_cast<size_t>(width));
+            const int x = static_cast<int>(i - static_cast<size_t>(y) * width);
+            l0[i] = moge::Coord3{y, x, zbin[i]};
+        }
+        auto l = moge::make_dense_image_level(std::move(l0), width, height);
+        std::memcpy(nbr, l.neighbors.data(), l.neighbors.size() * sizeof(int32_t));
+    });
+}
+
+// SparseRefiner::refine_once run `passes` times in a row on one refiner (so
+// the second pass exercises the topology cache) from a MOGG image in memory:
+// factor_coord [h*w][3] updated in place, encoder_feature [ew*eh][Cenc].
+int ref_refine_once(int n_threads, const uint8_t * mogg, size_t mogg_bytes, float * factor_coord, int32_t width,
+                    int32_t height, const float * encoder_feature, int32_t ew, int32_t eh, int passes,
+                    double * seconds) {
+    return guard([&] {
+        moge::MoggFile mf(mogg, mogg_bytes, true);
+        moge::SparseConfig cfg = moge::read_sparse_config(mf);
+        Runner r(n_threads);
+        moge::WeightStore ws(mf, r.cpu);
+        moge::SparseRefiner refiner(ws, cfg);
+        State s(2);
+        auto * enc = s.f32_2d(cfg.encoder_channels, static_cast<int64_t>(ew) * eh);
+        s.alloc(r.cpu);
+        ggml_backend_tensor_set(enc, encoder_feature, 0, ggml_nbytes(enc));
+        const size_t n = static_cast<size_t>(width) * height;
+        std::vector<float> fc(factor_coord, factor_coord + 3 * n);
+        std::vector<double> times;
+        for (int p = 0; p < (passes > 0 ? passes : 1); ++p) {
+            const auto t0 = std::chrono::steady_clock::now();
+            refiner.refine_once(r.sched, fc, width, height, enc, ew, eh);
+            times.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+        }
+        std::memcpy(factor_coord, fc.data(), 3 * n * sizeof(float));
+        std::sort(times.begin(), times.end());
+        if (seconds) *seconds = times[times.size() / 2];
     });
 }
 

@@ -8,6 +8,8 @@ in a checkout that has the reference tree next to it:
     make -f oracle/ref/Makefile REF=<path to mogecpp>
     python tests/golden/make_golden.py             # every fixture
     python tests/golden/make_golden.py groupnorm   # groupnorm.npz only
+    python tests/golden/make_golden.py image       # image_topology.npz only
+    python tests/golden/make_golden.py refiner     # refiner.npz only
 
 Fixtures are seeded synthetic inputs and the reference's outputs; the tests
 use them to pin the oracle port and the GPU path.  Inputs are rounded to
@@ -63,12 +65,74 @@ def groupnorm_fixture(R):
     print("groupnorm.npz", os.path.getsize(os.path.join(HERE, "groupnorm.npz")), "bytes")
 
 
+def image_cases():
+    """Point maps [h*w][3] for quantize_topology_z + make_dense_image_level."""
+    cases = {}
+    fc, _, _, _ = synth.refiner_inputs(5, 40, 32, 4, 8)
+    cases["surface"] = (fc, 40, 32, 256.0)
+    # log z exactly half-way between bins (z * 256 = k + 0.5): round half to even
+    w, h = 12, 10
+    k = np.arange(w * h) % 7 - 3
+    t = np.zeros((w * h, 3), np.float32)
+    t[:, 2] = (k + 0.5) / 256.0
+    cases["ties"] = (t, w, h, 256.0)
+    # negative log depths (z < 1) and a coarser resolution
+    fc2, _, _, _ = synth.refiner_inputs(6, 24, 20, 4, 8)
+    fc2[:, 2] -= 1.7
+    cases["negative"] = (fc2, 24, 20, 96.0)
+    flat = np.zeros((9 * 7, 3), np.float32)
+    flat[:, 2] = 0.25
+    cases["flat"] = (flat, 9, 7, 256.0)
+    one = np.array([[0.1, 0.2, 0.7]], np.float32)
+    cases["single"] = (one, 1, 1, 256.0)
+    line = np.zeros((5, 3), np.float32)
+    line[:, 2] = np.array([0.0, 1, 2, 4, 5], np.float32) / 256.0
+    cases["row"] = (line, 5, 1, 256.0)
+    return cases
+
+
+def image_fixture(R):
+    out = {}
+    for name, (fc, w, h, r) in image_cases().items():
+        z = R.quantize_topology_z(fc, w, h, r)
+        out[f"img_{name}_fc"] = fc
+        out[f"img_{name}_shape"] = np.array([w, h], np.int32)
+        out[f"img_{name}_res"] = np.array([r], np.float32)
+        out[f"img_{name}_zbin"] = z
+        out[f"img_{name}_nbr"] = R.make_dense_image_level(z, w, h)
+    np.savez_compressed(os.path.join(HERE, "image_topology.npz"), **out)
+    print("image_topology.npz", os.path.getsize(os.path.join(HERE, "image_topology.npz")), "bytes")
+
+
+REFINER_CASES = {"f32": (7, "f32"), "f16": (9, "f16")}   # model seed, weight storage
+
+
+def refiner_fixture(R):
+    """SparseRefiner::refine_once of the small synthetic refiner
+    (synth.SMALL_REFINER, weights regenerated from the seed) on a 64 x 48
+    point map: the updated log z of one pass."""
+    out = {}
+    fc, enc, ew, eh = synth.refiner_inputs(8, 64, 48, 4, synth.SMALL_REFINER["encoder_channels"])
+    out["fc"] = fc
+    out["enc"] = enc
+    out["shape"] = np.array([64, 48, ew, eh], np.int32)
+    for tag, (seed, wd) in REFINER_CASES.items():
+        img = synth.refiner_mogg(seed, synth.SMALL_REFINER, wd)
+        y, _ = R.refine_once(img, fc, 64, 48, enc, ew, eh)
+        out[f"{tag}_logz"] = y[:, 2]
+    np.savez_compressed(os.path.join(HERE, "refiner.npz"), **out)
+    print("refiner.npz", os.path.getsize(os.path.join(HERE, "refiner.npz")), "bytes")
+
+
 def main():
     R = Reference(n_threads=os.cpu_count() or 1)
-    if sys.argv[1:] == ["groupnorm"]:
-        groupnorm_fixture(R)
+    only = {"groupnorm": groupnorm_fixture, "image": image_fixture, "refiner": refiner_fixture}
+    if sys.argv[1:] and sys.argv[1] in only:
+        only[sys.argv[1]](R)
         return
     groupnorm_fixture(R)
+    image_fixture(R)
+    refiner_fixture(R)
     out = {}
     for name, c in topology_cases().items():
         c = np.ascontiguousarray(c, dtype=np.int32)
