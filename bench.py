@@ -702,8 +702,21 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         return nbr
 
     state = {}
+    # multi-GPU LayerNorm stacks: the exchange fused into each block's second
+    # conv (peer stores over NVLink); GroupNorm stacks keep the NCCL exchange
+    # (their statistics need an all-reduce per block anyway)
+    peer = world > 1 and args.block == "ln" and args.exchange == "peer"
+    pslab = slab.PeerSlab(ex, part, world, c) if peer else None
+    if peer:
+        state["nbr"] = ex.make_level(coords_d)
 
     def step(coords_t=coords_d, x_t=x_d):
+        if peer:
+            pslab.set_level(coords_t)
+            pslab.put_features(x_t)
+            for blk in blocks:
+                pslab.res_block(blk)
+            return
         state["nbr"] = run_stack(coords_t, x_t, part.n_owned)
 
     def reset():
@@ -717,6 +730,13 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         h_x = torch.from_numpy(lx0).pin_memory()
         h_out = [torch.empty((part.n_owned, c), dtype=x0_d.dtype).pin_memory() for _ in range(2)]
         bufs = [(coords_d, x_d), (torch.empty_like(coords_d), torch.empty_like(x_d))]
+        if peer:
+            outs = [torch.empty((part.n_owned, c), dtype=x0_d.dtype, device=dev) for _ in range(2)]
+
+            def out_dev(bi):
+                pslab.get_features(outs[bi])
+                return outs[bi]
+            return (h_coords, h_x), bufs, out_dev, h_out
         return (h_coords, h_x), bufs, (lambda bi: bufs[bi][1][:part.n_owned]), h_out
 
     int8_peak = {}
@@ -755,7 +775,8 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         # kernels per profiled family call: make_level = clear + insert +
         # neighbour; plan_build = header + mask keys + the radix sort's kernels
         # + tile lists; gn_stats/finalize/act_prepare/conv_tc = 1
-        per = {"make_level": 3, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "halo": 0}
+        per = {"make_level": 3, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "halo": 0,
+               "halo_wait": 2 if peer else 1}  # wait + signal kernels per block
         return sum(per.get(k, 1) * v[0] for k, v in prof.items())
 
     def parity():
@@ -763,12 +784,17 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         compared with the single-GPU stack over the whole set."""
         reset()
         step()
+        owned = torch.empty((part.n_owned, c), dtype=torch.float16, device=dev)
+        if peer:
+            pslab.get_features(owned)
+        else:
+            owned.copy_(x_d[:part.n_owned])
         torch.cuda.synchronize()
         parts = slab.partition(coords, world)
         res = None
         if rank == 0:
             full = torch.empty((n, c), dtype=torch.float16, device=dev)
-            full[part.lo:part.hi] = x_d[:part.n_owned]
+            full[part.lo:part.hi] = owned
             for r in range(1, world):
                 p = parts[r]
                 buf = torch.empty((p.n_owned, c), dtype=torch.float16, device=dev)
@@ -785,7 +811,7 @@ def build_stack(args, w, ex, dev, coords, rank, world):
                    "bit_exact": bool(torch.equal(full, xf)), "rows": int(n)}
             del full, xf, cf
         else:
-            dist.send(x_d[:part.n_owned].contiguous(), dst=0)
+            dist.send(owned, dst=0)
         return res
 
     def run_stack_single_gn(cf, xf):
@@ -808,7 +834,9 @@ def build_stack(args, w, ex, dev, coords, rank, world):
                                 f"{len(blocks_np)} res blocks" + (" (halo exchange before each)" if world > 1 else "") +
                                 (", GroupNorm statistics all-reduced" if world > 1 and args.block == "gn" else ""),
                         "conv": args.conv,
-                        "parallelism": f"z-slabs x{world}, 2-plane halo over NCCL" if world > 1 else "single GPU"})
+                        "parallelism": (f"z-slabs x{world}, 2-plane halo written by each block's second conv into "
+                                        f"the neighbours' buffers (peer stores over NVLink)" if peer else
+                                        f"z-slabs x{world}, 2-plane halo over NCCL") if world > 1 else "single GPU"})
 
 
 def stack_cpu_baseline(args, w, ex, dev, coords, blocks, blocks_np, convs):
@@ -1021,6 +1049,8 @@ def main():
     ap.add_argument("--workload", default="shell_4m", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--conv", default="ordered", choices=["ordered", "direct"])
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU halo exchange: fused peer stores (default) or NCCL send/recv per block")
     ap.add_argument("--block", default=None, choices=["ln", "gn"],
                     help="residual block (default: the one the workload is quoted on)")
     args = ap.parse_args()

@@ -317,6 +317,63 @@ int msc_nearest_up(msc_ctx_t ctx, const void* x, int x_dtype, int64_t np, int c,
                    int64_t nfine, const void* blob, const float* bias, const void* skip, int skip_dtype, void* y,
                    int y_dtype, void* ws, size_t ws_bytes, void* stream);
 
+/* ------------------------------------------------------------ multi-GPU
+ * A z-slab shard of a level for one GPU of a node (one process per GPU).
+ * No counterpart in the reference (its refiner is single-device,
+ * src/sparse.cpp:1100-1191); this is the sharded form of its per-level
+ * res_block loop.  Rows are laid out [owned | halo below | halo above]: the
+ * halos are the two z-planes on either side held by the neighbouring ranks;
+ * the first send_lo owned rows are the lower neighbour's halo above and the
+ * last send_hi owned rows the upper neighbour's halo below, in order.
+ *
+ * The exchange is fused into the conv: each block's second conv computes the
+ * owned rows only and its epilogue also stores the boundary rows straight
+ * into the neighbours' feature buffers (CUDA IPC memory over NVLink); a
+ * one-thread kernel per block waits, for at most 2 s, until both neighbours
+ * have finished the previous block (flags they set in this GPU's memory; a
+ * neighbour that never arrives raises MSC_DEV_TIMEOUT, read by msc_check).
+ * Two feature buffers alternate between blocks.
+ *
+ * Setup: msc_slab_create on every rank, msc_slab_get_handle, exchange the
+ * handles with the host's communicator (e.g. an all-gather), then
+ * msc_slab_connect with the lower and upper neighbours' handles (NULL at the
+ * ends).  Every rank must run the same number of blocks; call
+ * msc_slab_destroy only after all ranks are done (a barrier). */
+typedef struct {
+    int rank;
+    int world;
+    int channels;      /* 128 */
+    int64_t n_local;   /* n_owned + n_halo_lo + n_halo_hi */
+    int64_t n_owned;
+    int64_t n_halo_lo;
+    int64_t n_halo_hi;
+    int64_t send_lo;
+    int64_t send_hi;
+} msc_slab_desc;
+
+typedef struct {
+    unsigned char bytes[512];
+} msc_slab_handle;
+
+typedef struct msc_slab* msc_slab_t;
+
+int msc_slab_create(msc_ctx_t ctx, const msc_slab_desc* desc, msc_slab_t* out);
+int msc_slab_destroy(msc_slab_t s);
+int msc_slab_get_handle(msc_slab_t s, msc_slab_handle* out);
+int msc_slab_connect(msc_slab_t s, const msc_slab_handle* lower, const msc_slab_handle* upper);
+/* Topology of the local rows (coords [n_local][4], device): neighbour map
+ * and the conv plans of all rows and of the owned rows. */
+int msc_slab_set_level(msc_slab_t s, const int32_t* coords, void* stream);
+/* Loads [n_local][channels] fp16 features (device) into the current buffer;
+ * reads the owned rows [n_owned][channels] back (device or pinned host). */
+int msc_slab_put_features(msc_slab_t s, const void* x, void* stream);
+int msc_slab_get_features(msc_slab_t s, void* owned_out, void* stream);
+int msc_slab_features_ptr(msc_slab_t s, void** x);
+/* One LayerNorm residual block (as msc_res_block, Q8_0 weights, C = 128)
+ * over the shard, halo rows refreshed through the neighbours' conv2. */
+int msc_slab_res_block(msc_slab_t s, const float* norm_w, const float* norm_b, const void* blob1, const float* b1,
+                       const void* blob2, const float* b2, void* stream);
+
 /* ------------------------------------------------------------------ tracing */
 
 typedef struct {

@@ -19,7 +19,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libmoge_sparse_cuda.so")
 SOURCES = ["topology.cu", "prep.cu", "gn.cu", "conv_tc.cu", "plan.cu", "ops.cu", "capi.cu",
-           "noalloc.cu", "image_topo.cu", "refiner.cu"]
+           "noalloc.cu", "image_topo.cu", "refiner.cu", "slab.cu"]
 HEADERS = ["common.cuh", "conv.h", "conv_common.cuh", "gn.h", "ops.h", "plan.h", "topology.h", "image_topo.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",

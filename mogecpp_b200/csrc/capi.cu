@@ -246,6 +246,36 @@ void check_conv_shape(const msc_context::Blob& b, int cin, int ntaps) {
 namespace msc {
 // Records the calling thread's error message (for entry points in other files).
 void set_last_error(const std::string& msg) { g_err = msg; }
+
+// Context services for the executors in other files (slab.cu): the device
+// status word, the profiling event pair of one launch, a prepared blob's shape.
+uint32_t* ctx_status(msc_ctx_t ctx) { return ctx->status; }
+int ctx_device(msc_ctx_t ctx) { return ctx->device; }
+
+void* prof_begin(msc_ctx_t ctx, const char* name, cudaStream_t st) {
+    if (!ctx->prof) return nullptr;
+    auto* rec = new msc_context::Rec{name, take_event(ctx), nullptr};
+    cudaEventRecord(rec->a, st);
+    return rec;
+}
+
+void prof_end(msc_ctx_t ctx, void* token, cudaStream_t st) {
+    if (!token) return;
+    auto* rec = static_cast<msc_context::Rec*>(token);
+    rec->b = take_event(ctx);
+    cudaEventRecord(rec->b, st);
+    ctx->recs.push_back(*rec);
+    delete rec;
+}
+
+bool blob_shape(msc_ctx_t ctx, const void* blob, int* wtype, int* cin, int* cout, int* ntaps, int* planes) {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    auto it = ctx->blobs.find(blob);
+    if (it == ctx->blobs.end()) return false;
+    *wtype = it->second.wtype, *cin = it->second.cin, *cout = it->second.cout, *ntaps = it->second.ntaps,
+    *planes = it->second.planes;
+    return true;
+}
 }  // namespace msc
 
 extern "C" {
@@ -425,7 +455,7 @@ int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const i
         }
         {
             ProfScope ps(ctx, "plan_build", S(stream));
-            cuda_ok(msc::launch_plan_build(nbr, n, plan, ws, S(stream)), "plan build launch");
+            cuda_ok(msc::launch_plan_build(nbr, n, n, plan, ws, S(stream)), "plan build launch");
         }
         std::lock_guard<std::mutex> lk(ctx->mu);
         ctx->plans[plan] = msc_context::Plan{n, kind};

@@ -91,6 +91,20 @@ struct ConvArgs {
     int8_t* q_codes;
     float* q_scales;
     uint32_t* status;
+    // z-slab halo forwarding (multi-GPU), fp16 output with fp16 residual
+    // only: with store_limit > 0, output rows r < store_limit are stored
+    // locally; rows r < send_lo are also stored into the lower neighbour's
+    // feature buffer peer_lo at row peer_lo_off + r, rows send_hi_begin <= r
+    // < store_limit into the upper neighbour's peer_hi at row peer_hi_off +
+    // (r - send_hi_begin).  The peer buffers are the neighbours' device memory
+    // (CUDA IPC), written over NVLink.
+    int64_t store_limit;
+    void* peer_lo;
+    int64_t peer_lo_off;
+    int64_t send_lo;
+    void* peer_hi;
+    int64_t peer_hi_off;
+    int64_t send_hi_begin;
 };
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t st);
 bool conv_supported(int cin, int cout);

@@ -612,10 +612,23 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                 }
                 quad_transpose(h);  // h[j] = chunk qk of row rj[j]
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (rj[j] >= 0)
-                        reinterpret_cast<uint4*>(static_cast<__half*>(a.y) + static_cast<int64_t>(rj[j]) * COUT + c_base)[qk] =
+                for (int j = 0; j < 4; ++j) {
+                    const int r = rj[j];
+                    if (r < 0) continue;
+                    if (a.store_limit <= 0 || r < a.store_limit)
+                        reinterpret_cast<uint4*>(static_cast<__half*>(a.y) + static_cast<int64_t>(r) * COUT + c_base)[qk] =
                             h[j];
+                    if (a.store_limit > 0) {
+                        // boundary rows of a z-slab also go to the neighbour
+                        // that holds them as halo rows (peer memory over NVLink)
+                        if (a.peer_lo && r < a.send_lo)
+                            reinterpret_cast<uint4*>(static_cast<__half*>(a.peer_lo) +
+                                                     (a.peer_lo_off + r) * COUT + c_base)[qk] = h[j];
+                        if (a.peer_hi && r >= a.send_hi_begin && r < a.store_limit)
+                            reinterpret_cast<uint4*>(static_cast<__half*>(a.peer_hi) +
+                                                     (a.peer_hi_off + (r - a.send_hi_begin)) * COUT + c_base)[qk] = h[j];
+                    }
+                }
             }
         }
         if (row >= 0 && io == 0) {

@@ -41,7 +41,7 @@ TapBits make_tap_bits() {
     return tb;
 }
 
-__global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, TapBits tb, uint32_t* __restrict__ keys,
+__global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, int n_in, TapBits tb, uint32_t* __restrict__ keys,
                                  int* __restrict__ vals) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -49,7 +49,7 @@ __global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, TapBits tb,
     const int* r = nbr + static_cast<int64_t>(i) * 27;
 #pragma unroll
     for (int t = 0; t < 27; ++t)
-        if (static_cast<unsigned>(__ldg(r + t)) < static_cast<unsigned>(n)) k |= 1u << tb.bit[t];
+        if (static_cast<unsigned>(__ldg(r + t)) < static_cast<unsigned>(n_in)) k |= 1u << tb.bit[t];
     // position of the mask in the reflected Gray-code sequence (prefix xor
     // from the high bit): sorted in that order, neighbouring masks differ in
     // one tap, so a tile's (and a warp's) tap union stays small
@@ -68,7 +68,7 @@ __global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, TapBits tb,
 // memory, one plain store per tile).
 constexpr int kTileListWarps = 16;
 __global__ void __launch_bounds__(32 * kTileListWarps)
-    tile_lists_kernel(const int* __restrict__ order, const int* __restrict__ nbr, int n, PlanTiles T) {
+    tile_lists_kernel(const int* __restrict__ order, const int* __restrict__ nbr, int n, int n_in, PlanTiles T) {
     constexpr int RPW = kPlanTileRows / kTileListWarps;
     __shared__ uint32_t smask;
     const int lane = threadIdx.x & 31;
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(32 * kTileListWarps)
     uint32_t m = 0;
 #pragma unroll
     for (int u = 0; u < RPW; ++u) {
-        const bool ok = lane < 27 && static_cast<unsigned>(j[u]) < static_cast<unsigned>(n);
+        const bool ok = lane < 27 && static_cast<unsigned>(j[u]) < static_cast<unsigned>(n_in);
         if (lane < 27) T.nbr[(r0 + u) * 27 + lane] = ok ? j[u] : -1;
         m |= __ballot_sync(0xffffffffu, ok);
     }
@@ -144,7 +144,7 @@ size_t plan_workspace_bytes(int64_t n) {
            align256(sort_temp_bytes(n)) + 256;
 }
 
-cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, void* plan, void* ws, cudaStream_t st) {
+cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, int64_t n_in, void* plan, void* ws, cudaStream_t st) {
     plan_header_kernel<<<1, 1, 0, st>>>(static_cast<PlanHeader*>(plan), n);
     if (n == 0) return cudaGetLastError();
     uint8_t* w = static_cast<uint8_t*>(ws);
@@ -158,10 +158,11 @@ cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, void* plan, void* w
     const PlanTiles T = plan_tiles(static_cast<uint8_t*>(plan), n);
     const int ni = static_cast<int>(n);
     static const TapBits tb = make_tap_bits();
-    mask_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(nbr, ni, tb, k_in, vals_in);
+    const int nin = static_cast<int>(n_in);
+    mask_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(nbr, ni, nin, tb, k_in, vals_in);
     cudaError_t e = cub::DeviceRadixSort::SortPairs(w, temp_bytes, k_in, k_out, vals_in, T.order, ni, 0, 27, st);
     if (e != cudaSuccess) return e;
-    tile_lists_kernel<<<static_cast<unsigned>(tiles_of(n)), 32 * kTileListWarps, 0, st>>>(T.order, nbr, ni, T);
+    tile_lists_kernel<<<static_cast<unsigned>(tiles_of(n)), 32 * kTileListWarps, 0, st>>>(T.order, nbr, ni, nin, T);
     return cudaGetLastError();
 }
 

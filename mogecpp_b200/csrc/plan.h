@@ -34,6 +34,9 @@ PlanTiles plan_tiles(uint8_t* plan, int64_t n);
 
 size_t plan_bytes(int64_t n);
 size_t plan_workspace_bytes(int64_t n);
-cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, void* plan, void* ws, cudaStream_t st);
+// Plans rows [0, n) of the neighbour map; indices >= n_in (n_in >= n) are
+// missing taps (the sentinel).  n_in > n plans a subset of a level's rows,
+// e.g. the owned rows of a z-slab whose neighbours include halo rows.
+cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, int64_t n_in, void* plan, void* ws, cudaStream_t st);
 
 }  // namespace msc

@@ -60,6 +60,15 @@ SIGNATURES = {
     "msc_refiner_level_sizes": (C.c_int, [_vp, C.POINTER(_i64), _i32, C.POINTER(_i32)]),
     "msc_refiner_refine_once": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
     "msc_refiner_refine_once_host": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
+    "msc_slab_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
+    "msc_slab_destroy": (C.c_int, [_vp]),
+    "msc_slab_get_handle": (C.c_int, [_vp, _vp]),
+    "msc_slab_connect": (C.c_int, [_vp, _vp, _vp]),
+    "msc_slab_set_level": (C.c_int, [_vp, _vp, _vp]),
+    "msc_slab_put_features": (C.c_int, [_vp, _vp, _vp]),
+    "msc_slab_get_features": (C.c_int, [_vp, _vp, _vp]),
+    "msc_slab_features_ptr": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "msc_slab_res_block": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "msc_profile_enable": (C.c_int, [_vp, _i32]),
     "msc_profile_read": (C.c_int, [_vp, _vp, _i32, C.POINTER(_i32)]),
 }
@@ -79,6 +88,16 @@ class SparseConfig(C.Structure):
                 ("encoder_blocks", C.c_int * MAX_LEVELS), ("decoder_blocks", C.c_int * MAX_LEVELS),
                 ("downsample_factors", C.c_int * MAX_LEVELS), ("bottleneck_blocks", C.c_int),
                 ("encoder_downsample", C.c_int), ("depth_resolution", C.c_float)]
+
+
+class SlabDesc(C.Structure):
+    """msc_slab_desc: one rank's z-slab shard ([owned | halo below | halo above])."""
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("channels", C.c_int), ("n_local", C.c_int64),
+                ("n_owned", C.c_int64), ("n_halo_lo", C.c_int64), ("n_halo_hi", C.c_int64), ("send_lo", C.c_int64),
+                ("send_hi", C.c_int64)]
+
+
+SLAB_HANDLE_BYTES = 512
 
 
 class ProfileEntry(C.Structure):

@@ -166,3 +166,68 @@ class SlabExchange:
         if ops:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
+
+
+class PeerSlab:
+    """One rank's shard on the fused-exchange path (``msc_slab_*``): the
+    residual blocks run over the local rows and each block's second conv
+    writes the boundary rows straight into the neighbours' halo rows (CUDA
+    IPC memory over NVLink); no collective call per block.  The handles of
+    the two feature buffers are exchanged once, here, with an all-gather over
+    ``torch.distributed``."""
+
+    def __init__(self, ex, part: SlabPart, world: int, channels: int = 128, group=None):
+        import ctypes as C
+        from . import lib as L
+        self.ex, self.lib, self.p, self.world, self.c = ex, ex.lib, part, world, channels
+        d = L.SlabDesc(part.rank, world, channels, part.n_local, part.n_owned, len(part.halo_lo), len(part.halo_hi),
+                       part.send_lo, part.send_hi)
+        h = C.c_void_p()
+        L.check(self.lib.msc_slab_create(ex.ctx, C.byref(d), C.byref(h)))
+        self.h = h
+        buf = C.create_string_buffer(L.SLAB_HANDLE_BYTES)
+        L.check(self.lib.msc_slab_get_handle(self.h, buf))
+        mine = buf.raw
+        if world > 1:
+            import torch.distributed as dist
+            allh = [None] * world
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        r = part.rank
+        lower = C.create_string_buffer(allh[r - 1], L.SLAB_HANDLE_BYTES) if r > 0 else None
+        upper = C.create_string_buffer(allh[r + 1], L.SLAB_HANDLE_BYTES) if r < world - 1 else None
+        L.check(self.lib.msc_slab_connect(self.h, lower, upper))
+
+    def _stream(self):
+        import ctypes as C
+        import torch
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def set_level(self, coords) -> None:
+        import ctypes as C
+        from . import lib as L
+        L.check(self.lib.msc_slab_set_level(self.h, C.c_void_p(coords.data_ptr()), self._stream()))
+
+    def put_features(self, x) -> None:
+        import ctypes as C
+        from . import lib as L
+        L.check(self.lib.msc_slab_put_features(self.h, C.c_void_p(x.data_ptr()), self._stream()))
+
+    def get_features(self, out) -> None:
+        """The owned rows of the current features into out [n_owned, C]."""
+        import ctypes as C
+        from . import lib as L
+        L.check(self.lib.msc_slab_get_features(self.h, C.c_void_p(out.data_ptr()), self._stream()))
+
+    def res_block(self, blk: dict) -> None:
+        import ctypes as C
+        from . import lib as L
+        p = lambda t: None if t is None else C.c_void_p(t.data_ptr())
+        L.check(self.lib.msc_slab_res_block(self.h, p(blk.get("norm_w")), p(blk.get("norm_b")), p(blk["w1"].blob),
+                                            p(blk.get("b1")), p(blk["w2"].blob), p(blk.get("b2")), self._stream()))
+
+    def close(self):
+        if self.h:
+            self.lib.msc_slab_destroy(self.h)
+            self.h = None

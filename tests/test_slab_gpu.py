@@ -132,3 +132,67 @@ def test_two_gpu_slabs_match_single_gpu_stack(tmp_path, ex, oracle, block):
              else oracle.res_block(h, nbr, raw, W_Q8_0))
         h = h.astype(np.float16).astype(np.float32)
     assert rel_l2(got, h) < 3e-3 and max_abs(got, h) < 3e-2
+
+
+def _rank_main_peer(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from mogecpp_b200.sparse import SparseCudaExecutor
+    from mogecpp_b200.synth import quantize_q8_0
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    ps = None
+    try:
+        ex = SparseCudaExecutor(rank)
+        coords = _coords()
+        part = slab.partition(coords, world)[rank]
+        rows = part.local_rows()
+        dev = torch.device("cuda", rank)
+        cd = torch.from_numpy(np.ascontiguousarray(coords[rows])).to(dev)
+        x = torch.from_numpy(synth.features_rows(331, rows, 128, np.float16)).to(dev)
+        ps = slab.PeerSlab(ex, part, world)
+        ps.set_level(cd)
+        ps.put_features(x)
+        for blk in range(2):
+            raw = _raw_block(340 + blk, 128)
+            b = dict(norm_w=torch.from_numpy(raw["norm_w"]).to(dev), norm_b=torch.from_numpy(raw["norm_b"]).to(dev),
+                     b1=torch.from_numpy(raw["b1"]).to(dev), b2=torch.from_numpy(raw["b2"]).to(dev),
+                     w1=ex.prepare_weight(torch.from_numpy(quantize_q8_0(raw["w1"])).to(dev), "q8_0", 128, 128, 27),
+                     w2=ex.prepare_weight(torch.from_numpy(quantize_q8_0(raw["w2"])).to(dev), "q8_0", 128, 128, 27))
+            ps.res_block(b)
+        out = torch.empty((part.n_owned, 128), dtype=torch.float16, device=dev)
+        ps.get_features(out)
+        ex.check()
+        np.save(out_path, out.float().cpu().numpy())
+        dist.barrier()
+    finally:
+        if ps is not None:
+            ps.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_peer_halo_matches_single_gpu_stack(tmp_path, ex):
+    """The fused-exchange path (msc_slab_*): halo rows written by each
+    block's second conv into the neighbour's buffer over NVLink.  The owned
+    rows of both ranks equal the single-GPU stack bit for bit."""
+    import multiprocessing as mp
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    outs = [str(tmp_path / f"peer{r}.npy") for r in range(world)]
+    procs = [ctx.Process(target=_rank_main_peer, args=(r, world, port, outs[r])) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = np.concatenate([np.load(o) for o in outs])
+    coords = _coords()
+    single = _stack(ex, coords, synth.features(331, coords.shape[0], 128, np.float16), "ln", plan_kind="tap_order")
+    np.testing.assert_array_equal(got, single)
