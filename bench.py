@@ -689,11 +689,12 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         b.record()
         halo_events.append((a, b))
 
-    def run_stack(coords_t, x_t, n_stat):
+    def run_stack(coords_t, x_t, n_stat, single=False):
         nbr = ex.make_level(coords_t)
         plan = ex.conv_plan(coords_t, nbr, plan_kind) if plan_kind else None
         for blk in blocks:
-            exchange(x_t)
+            if not single:
+                exchange(x_t)
             if args.block == "gn":
                 ex.res_block_gn(x_t, nbr, coords_t, 1, blk, eps=GN_EPS, plan=plan, n_stat=n_stat,
                                 allreduce=gn_allreduce)
@@ -710,12 +711,14 @@ def build_stack(args, w, ex, dev, coords, rank, world):
     if peer:
         state["nbr"] = ex.make_level(coords_d)
 
-    def step(coords_t=coords_d, x_t=x_d):
+    def step(coords_t=coords_d, x_t=x_d, out_t=None):
         if peer:
             pslab.set_level(coords_t)
             pslab.put_features(x_t)
             for blk in blocks:
                 pslab.res_block(blk)
+            if out_t is not None:
+                pslab.get_features(out_t)   # on the compute stream: the next step reuses the buffer
             return
         state["nbr"] = run_stack(coords_t, x_t, part.n_owned)
 
@@ -732,11 +735,8 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         bufs = [(coords_d, x_d), (torch.empty_like(coords_d), torch.empty_like(x_d))]
         if peer:
             outs = [torch.empty((part.n_owned, c), dtype=x0_d.dtype, device=dev) for _ in range(2)]
-
-            def out_dev(bi):
-                pslab.get_features(outs[bi])
-                return outs[bi]
-            return (h_coords, h_x), bufs, out_dev, h_out
+            bufs = [b + (o,) for b, o in zip(bufs, outs)]
+            return (h_coords, h_x), bufs, (lambda bi: outs[bi]), h_out
         return (h_coords, h_x), bufs, (lambda bi: bufs[bi][1][:part.n_owned]), h_out
 
     int8_peak = {}
@@ -802,7 +802,7 @@ def build_stack(args, w, ex, dev, coords, rank, world):
                 full[p.lo:p.hi] = buf
             cf = torch.from_numpy(coords).to(dev)
             xf = torch.from_numpy(synth.features_rows(2, np.arange(n), c, np.float16)).to(dev)
-            run_stack(cf, xf, n) if args.block == "ln" else run_stack_single_gn(cf, xf)
+            run_stack(cf, xf, n, single=True) if args.block == "ln" else run_stack_single_gn(cf, xf)
             torch.cuda.synchronize()
             d = (full.float() - xf.float())
             res = {"reference": "single-GPU stack over all voxels (same kernels)",

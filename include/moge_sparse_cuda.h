@@ -374,6 +374,13 @@ int msc_slab_features_ptr(msc_slab_t s, void** x);
 int msc_slab_res_block(msc_slab_t s, const float* norm_w, const float* norm_b, const void* blob1, const float* b1,
                        const void* blob2, const float* b2, void* stream);
 
+/* Failure-detection probe: runs the bounded cross-GPU wait of the slab path
+ * on a flag that nothing sets, for budget_us microseconds (at most 2 s);
+ * the wait gives up, sets MSC_DEV_TIMEOUT in the context's status word (read
+ * and cleared by msc_check) and the context stays usable.  Lets a host test
+ * its handling of a neighbour that never arrives without a second GPU. */
+int msc_wait_probe(msc_ctx_t ctx, int64_t budget_us, void* stream);
+
 /* ------------------------------------------------------------------ tracing */
 
 typedef struct {

@@ -100,14 +100,15 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
 
 // One thread polls this GPU's flags (written by the neighbours over
 // NVLink) until both reach `target`, for at most 2 s.
-__global__ void slab_wait_kernel(const int* flags, int need_lo, int need_hi, int target, uint32_t* status) {
+__global__ void slab_wait_kernel(const int* flags, int need_lo, int need_hi, int target, uint32_t* status,
+                                 unsigned long long budget_ns) {
     if (threadIdx.x != 0) return;
     const unsigned long long t0 = timer_ns();
     for (;;) {
         const bool lo = !need_lo || ld_acquire_sys(flags) >= target;
         const bool hi = !need_hi || ld_acquire_sys(flags + 1) >= target;
         if (lo && hi) return;
-        if (timer_ns() - t0 > kWaitNs) {
+        if (timer_ns() - t0 > budget_ns) {
             atomicOr(status, MSC_DEV_TIMEOUT);
             return;
         }
@@ -327,7 +328,7 @@ int msc_slab_res_block(msc_slab_t s, const float* norm_w, const float* norm_b, c
         const int k = s->done;
         if (k > 0 && d.world > 1) {
             void* t = prof_begin(s->ctx, "halo_wait", st);
-            slab_wait_kernel<<<1, 32, 0, st>>>(s->flags, d.rank > 0, d.rank < d.world - 1, k, status);
+            slab_wait_kernel<<<1, 32, 0, st>>>(s->flags, d.rank > 0, d.rank < d.world - 1, k, status, kWaitNs);
             cuda(cudaGetLastError(), "halo wait");
             prof_end(s->ctx, t, st);
         }
@@ -385,6 +386,22 @@ int msc_slab_res_block(msc_slab_t s, const float* norm_w, const float* norm_b, c
         }
         s->cur ^= 1;
         ++s->done;
+    });
+}
+
+int msc_wait_probe(msc_ctx_t ctx, int64_t budget_us, void* stream) {
+    return guard([&] {
+        if (!ctx) fail(MSC_E_INVALID, "null context");
+        if (budget_us < 0 || budget_us > 2000000) fail(MSC_E_INVALID, "budget must be in [0, 2 s]");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        int* flag = nullptr;
+        cuda(cudaMallocAsync(reinterpret_cast<void**>(&flag), 256, st), "probe flag");
+        cuda(cudaMemsetAsync(flag, 0, 256, st), "probe flag clear");
+        // a flag nothing sets: the wait runs out and reports MSC_DEV_TIMEOUT
+        slab_wait_kernel<<<1, 32, 0, st>>>(flag, 1, 1, 1, ctx_status(ctx),
+                                           static_cast<unsigned long long>(budget_us) * 1000ull);
+        cuda(cudaGetLastError(), "probe wait");
+        cuda(cudaFreeAsync(flag, st), "probe flag free");
     });
 }
 

@@ -69,6 +69,7 @@ SIGNATURES = {
     "msc_slab_get_features": (C.c_int, [_vp, _vp, _vp]),
     "msc_slab_features_ptr": (C.c_int, [_vp, C.POINTER(_vp)]),
     "msc_slab_res_block": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "msc_wait_probe": (C.c_int, [_vp, _i64, _vp]),
     "msc_profile_enable": (C.c_int, [_vp, _i32]),
     "msc_profile_read": (C.c_int, [_vp, _vp, _i32, C.POINTER(_i32)]),
 }

@@ -7,6 +7,7 @@ oracle's residual block over its local rows between exchanges; the owned
 rows must equal the single-process oracle stack bit for bit (each output
 row depends only on its neighbours' values, in a fixed order)."""
 import os
+import time
 import socket
 
 import numpy as np
@@ -135,3 +136,48 @@ def test_two_gloo_ranks_match_the_single_process_stack(tmp_path, oracle):
         x = oracle.res_block(x, nbr, _raw_block(320 + blk, 64), W_Q8_0)
     got = np.concatenate([np.load(o) for o in outs])
     np.testing.assert_array_equal(got, x)
+
+
+def _rank_absent_peer(rank, world, port, out_path):
+    """Rank 1 leaves between steps without taking part in the halo exchange;
+    rank 0's exchange must end with an error after the process group's short
+    timeout instead of waiting for good."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    coords = _coords()
+    part = slab.partition(coords, world)[rank]
+    x = torch.zeros((part.n_local, 8), dtype=torch.float32)
+    if rank == 1:
+        with open(out_path, "w") as f:
+            f.write("left")
+        os._exit(0)  # gone before the exchange: no collective in flight
+    t0 = time.time()
+    try:
+        slab.SlabExchange(part, world).exchange(x)
+        outcome = "returned"
+    except Exception as e:  # noqa: BLE001 - the timeout is the expected outcome
+        outcome = "raised:" + type(e).__name__
+    with open(out_path, "w") as f:
+        f.write(f"{outcome} {time.time() - t0:.1f}")
+    os._exit(0)
+
+
+def test_absent_halo_peer_is_detected_on_the_host(tmp_path):
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    outs = [str(tmp_path / f"r{r}.txt") for r in range(2)]
+    procs = [ctx.Process(target=_rank_absent_peer, args=(r, 2, port, outs[r])) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert open(outs[1]).read() == "left"
+    outcome, secs = open(outs[0]).read().split()
+    assert outcome.startswith("raised"), outcome
+    assert float(secs) < 60
