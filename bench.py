@@ -692,6 +692,11 @@ def build_stack(args, w, ex, dev, coords, rank, world):
     def run_stack(coords_t, x_t, n_stat, single=False):
         nbr = ex.make_level(coords_t)
         plan = ex.conv_plan(coords_t, nbr, plan_kind) if plan_kind else None
+        if args.block == "ln" and (single or world == 1):
+            # one preparation pass: each block's second conv emits the next
+            # block's operand
+            ex.res_stack(x_t, nbr, blocks, plan=plan)
+            return nbr
         for blk in blocks:
             if not single:
                 exchange(x_t)

@@ -227,6 +227,26 @@ class SparseCudaExecutor:
                                                wsb, _stream()))
         return x
 
+    def res_stack(self, x, nbr, blocks: list, plan=None):
+        """In place on x: len(blocks) residual blocks in a row (``msc_res_stack``:
+        with fp16 x, C = 128 and Q8_0 weights each block's second conv also
+        prepares the next block's operand)."""
+        n, c = x.shape
+        k = len(blocks)
+        wsb = self.lib.msc_op_workspace_bytes(n, c)
+        ws = self.workspace(wsb)
+
+        def arr(key, attr=None):
+            vals = [b.get(key) for b in blocks]
+            if all(v is None for v in vals):
+                return None
+            ptrs = [None if v is None else (getattr(v, attr) if attr else v).data_ptr() for v in vals]
+            return (C.c_void_p * k)(*ptrs)
+        L.check(self.lib.msc_res_stack(self.ctx, _p(x), _DT[x.dtype], n, c, _p(nbr), _p(plan), k, arr("norm_w"),
+                                       arr("norm_b"), arr("w1", "blob"), arr("b1"), arr("w2", "blob"), arr("b2"),
+                                       _p(ws), wsb, _stream()))
+        return x
+
     def res_block_gn(self, x, nbr, coords, nsamples: int, blk: dict, eps: float = 1e-5, plan=None,
                      n_stat: int | None = None, allreduce=None):
         """In place on x: x + conv2(SiLU(GroupNorm_32(conv1(x) + b1))) + b2.

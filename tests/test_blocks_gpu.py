@@ -131,3 +131,47 @@ def test_unet_level_bf16_matches_oracle(ex, oracle):
     for got, ref in ((h0, r0), (h1, r1), (h2, r2)):
         assert rel_l2(host(got), ref) < 8e-3  # bf16 output rounding
     assert rel_l2(host(y), ry) < TOL_FP16[0] and max_abs(host(y), ry) < TOL_FP16[1]
+
+
+@pytest.mark.parametrize("n_cut", [None, 777])
+def test_res_stack_fused_operand_equals_blocks_one_by_one(ex, oracle, n_cut):
+    """msc_res_stack (each block's second conv emits the next block's
+    LayerNorm + SiLU + Q8_0 operand) against the same blocks run one by one:
+    identical bits; and every block against the oracle on its input."""
+    coords = synth.small_coords(140, extent=30, grid=32)
+    if n_cut:
+        coords = coords[:n_cut]   # a ragged last tile
+    nbr = oracle.make_level(coords)
+    nbrd = dev(nbr)
+    plan = ex.conv_plan(dev(coords), nbrd)
+    x0 = dev(synth.features(141, coords.shape[0], 128)).to(torch.float16)
+    raws = [raw_block(150 + 10 * b, 128) for b in range(3)]
+    blks = [make_block(ex, oracle, r, "q8_0", 128) for r in raws]
+    a = x0.clone()
+    ex.res_stack(a, nbrd, blks, plan=plan)
+    b = x0.clone()
+    ins = []
+    for blk in blks:
+        ins.append(host(b))
+        ex.res_block(b, nbrd, blk, plan=plan)
+    ex.check()
+    np.testing.assert_array_equal(host(a), host(b))
+    for r, xin, k in zip(raws, ins + [host(b)], range(3)):
+        ref = oracle.res_block(xin, nbr, r, W_Q8_0)
+        out = ins[k + 1] if k + 1 < len(ins) else host(b)
+        assert rel_l2(out, ref) < TOL_FP16[0] and max_abs(out, ref) < TOL_FP16[1], (k, rel_l2(out, ref))
+
+
+def test_res_stack_other_formats_run_block_by_block(ex, oracle):
+    coords = synth.small_coords(160, extent=20, grid=32)
+    nbr = oracle.make_level(coords)
+    x0 = dev(synth.features(161, coords.shape[0], 64))
+    raws = [raw_block(170 + 10 * b, 64) for b in range(2)]
+    blks = [make_block(ex, oracle, r, "f32", 64) for r in raws]
+    a = x0.clone()
+    ex.res_stack(a, dev(nbr), blks)
+    b = x0.clone()
+    for blk in blks:
+        ex.res_block(b, dev(nbr), blk)
+    ex.check()
+    np.testing.assert_array_equal(host(a), host(b))
