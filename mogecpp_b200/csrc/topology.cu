@@ -298,6 +298,170 @@ uint64_t table_capacity(int64_t n) {
     return cap;
 }
 
+// ---- brick map (make_level) ----------------------------------------------
+// Voxels are grouped into 4 x 4 x 4 bricks: a small hash table maps a brick
+// key (b, z >> 2, y >> 2, x >> 2) to a brick id (numbered in arrival order),
+// and a brick record holds the 64 voxel indices of its cells (INT_MAX =
+// empty; the smallest index of a duplicated coordinate, FlatCoordMap's
+// first-insert rule).  A neighbour query is one brick-table probe plus one
+// record read.  Surfaces fill a brick with ~15-40 voxels, so the table and
+// the records are a few tens of MB and stay in L2, and the 32 voxels of a
+// query warp (consecutive rows, mostly one or two bricks) probe the same
+// slots.  Inputs too sparse for the record budget (more than n / 4 + 1024
+// bricks) take the per-voxel hash instead; the choice is made on the device.
+constexpr int kBrickVox = 64;
+constexpr int kNoVoxel = 0x7fffffff;
+
+int64_t brick_budget(int64_t n) { return n / 4 + 1024; }
+uint64_t brick_capacity(int64_t n) {
+    uint64_t cap = 64;
+    while (cap < static_cast<uint64_t>(2 * brick_budget(n))) cap <<= 1;
+    return cap;
+}
+
+__device__ __forceinline__ unsigned long long brick_key(int x, int y, int z, int b) {
+    return pack_key(x >> 2, y >> 2, z >> 2, b);
+}
+__device__ __forceinline__ int brick_cell(int x, int y, int z) { return (x & 3) | ((y & 3) << 2) | ((z & 3) << 4); }
+
+// ctr[0] = bricks numbered so far (forced above the budget when the table
+// runs out, which selects the per-voxel hash)
+__global__ void brick_insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ t, uint64_t mask,
+                                    int* __restrict__ ctr, int budget, uint32_t* status) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int4 c = __ldg(coords + i);
+    if (!coord_ok(c)) {
+        set_status(status, MSC_DEV_BAD_COORD);
+        return;
+    }
+    const unsigned long long key = brick_key(c.x, c.y, c.z, c.w);
+    uint64_t h = mix64(key) & mask;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+        const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
+        if (prev == kEmpty) {
+            t[h].val = atomicAdd(ctr, 1);
+            return;
+        }
+        if (prev == key) return;
+        h = (h + 1) & mask;
+    }
+    atomicMax(ctr, budget + 1);
+}
+
+__global__ void brick_clear_kernel(int* __restrict__ rec, const int* __restrict__ ctr, int budget) {
+    const int nb = *ctr;
+    if (nb > budget) return;
+    const int64_t total = static_cast<int64_t>(nb) * kBrickVox;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        rec[e] = kNoVoxel;
+}
+
+__device__ __forceinline__ int brick_find(const Slot* __restrict__ t, uint64_t mask, unsigned long long key) {
+    return table_find(t, mask, key);
+}
+
+__global__ void brick_fill_kernel(const int4* __restrict__ coords, int n, const Slot* __restrict__ t, uint64_t mask,
+                                  int* __restrict__ rec, const int* __restrict__ ctr, int budget, uint32_t* status) {
+    if (*ctr > budget) return;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int4 c = __ldg(coords + i);
+    if (!coord_ok(c)) return;
+    const int id = brick_find(t, mask, brick_key(c.x, c.y, c.z, c.w));
+    if (id < 0) return;  // cannot happen: every voxel's brick was inserted
+    const int old = atomicMin(&rec[static_cast<int64_t>(id) * kBrickVox + brick_cell(c.x, c.y, c.z)], i);
+    if (old != kNoVoxel) set_status(status, MSC_DEV_DUP_COORD);
+}
+
+__global__ void __launch_bounds__(27 * kMapVox) brick_neighbor_kernel(const int4* __restrict__ coords, int n,
+                                                                      const Slot* __restrict__ t, uint64_t mask,
+                                                                      const int* __restrict__ rec,
+                                                                      const int* __restrict__ ctr, int budget,
+                                                                      int* __restrict__ nbr) {
+    if (*ctr > budget) return;
+    __shared__ int4 sc[kMapVox];
+    __shared__ int sn[kMapVox * 27];
+    const int base = blockIdx.x * kMapVox;
+    const int tid = threadIdx.x;
+    if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
+    __syncthreads();
+    const int v = tid % kMapVox;
+    const int tap = tid / kMapVox;
+    if (base + v < n) {
+        const int4 c = sc[v];
+        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+        const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
+        int found = n;
+        if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
+            const int id = brick_find(t, mask, brick_key(qx, qy, qz, c.w));
+            if (id >= 0) {
+                const int j = __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz));
+                if (j != kNoVoxel) found = j;
+            }
+        }
+        sn[v * 27 + tap] = found;
+    }
+    __syncthreads();
+    const int count = min(kMapVox, n - base) * 27;
+    int* out = nbr + static_cast<int64_t>(base) * 27;
+    for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
+}
+
+// The per-voxel hash path, run only when the brick count exceeded the budget.
+__global__ void gated_clear_kernel(Slot* __restrict__ t, uint64_t cap, const int* __restrict__ ctr, int budget) {
+    if (*ctr <= budget) return;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < cap;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        Slot s;
+        s.key = kEmpty;
+        s.val = 0x7fffffff;
+        s.pad = 0;
+        t[i] = s;
+    }
+}
+
+__global__ void gated_insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ t, uint64_t mask,
+                                    const int* __restrict__ ctr, int budget, uint32_t* status) {
+    if (*ctr <= budget) return;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int4 c = __ldg(coords + i);
+    if (!coord_ok(c)) return;  // reported by the brick insert
+    if (!table_insert(t, mask, pack_key(c.x, c.y, c.z, c.w), i, status)) set_status(status, MSC_DEV_HASH_FULL);
+}
+
+__global__ void __launch_bounds__(27 * kMapVox) gated_neighbor_kernel(const int4* __restrict__ coords, int n,
+                                                                      const Slot* __restrict__ t, uint64_t mask,
+                                                                      const int* __restrict__ ctr, int budget,
+                                                                      int* __restrict__ nbr) {
+    if (*ctr <= budget) return;
+    __shared__ int4 sc[kMapVox];
+    __shared__ int sn[kMapVox * 27];
+    const int base = blockIdx.x * kMapVox;
+    const int tid = threadIdx.x;
+    if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
+    __syncthreads();
+    const int v = tid % kMapVox;
+    const int tap = tid / kMapVox;
+    if (base + v < n) {
+        const int4 c = sc[v];
+        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+        const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
+        int found = n;
+        if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
+            const int idx = table_find(t, mask, pack_key(qx, qy, qz, c.w));
+            if (idx >= 0) found = idx;
+        }
+        sn[v * 27 + tap] = found;
+    }
+    __syncthreads();
+    const int count = min(kMapVox, n - base) * 27;
+    int* out = nbr + static_cast<int64_t>(base) * 27;
+    for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
+}
+
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
@@ -305,21 +469,45 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 size_t topology_workspace_bytes(int64_t n) {
     const uint64_t cap = table_capacity(n);
     const int64_t nblk = (n + kScanBlock - 1) / kScanBlock + 1;
-    return align_up(2 * cap * sizeof(Slot), 256) + align_up(static_cast<size_t>(n + 1) * 4, 256) +
-           align_up(static_cast<size_t>(nblk) * 4, 256) + 256;
+    // downsample: fine and parent tables + scan arrays; make_level: the
+    // per-voxel table (first half of the pair), then the brick table, the
+    // brick records and the counter
+    const size_t down = align_up(2 * cap * sizeof(Slot), 256) + align_up(static_cast<size_t>(n + 1) * 4, 256) +
+                        align_up(static_cast<size_t>(nblk) * 4, 256) + 256;
+    const size_t level = align_up(cap * sizeof(Slot), 256) + align_up(brick_capacity(n) * sizeof(Slot), 256) +
+                         align_up(static_cast<size_t>(brick_budget(n)) * kBrickVox * 4, 256) + 256;
+    return down > level ? down : level;
 }
 
 cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, void* ws, uint32_t* status,
                               cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     const uint64_t cap = table_capacity(n);
-    Slot* t = static_cast<Slot*>(ws);
-    table_clear_kernel<<<static_cast<unsigned>((cap + 255) / 256), 256, 0, st>>>(t, cap);
+    const uint64_t bcap = brick_capacity(n);
+    const int budget = static_cast<int>(brick_budget(n));
+    char* p = static_cast<char*>(ws);
+    Slot* t = reinterpret_cast<Slot*>(p);
+    p += align_up(cap * sizeof(Slot), 256);
+    Slot* bt = reinterpret_cast<Slot*>(p);
+    p += align_up(bcap * sizeof(Slot), 256);
+    int* rec = reinterpret_cast<int*>(p);
+    p += align_up(static_cast<size_t>(budget) * kBrickVox * 4, 256);
+    int* ctr = reinterpret_cast<int*>(p);
     const auto* c4 = reinterpret_cast<const int4*>(coords);
-    insert_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(c4, static_cast<int>(n), t, cap - 1,
-                                                                          status);
-    neighbor_kernel<<<static_cast<unsigned>((n + kMapVox - 1) / kMapVox), 27 * kMapVox, 0, st>>>(
-        c4, static_cast<int>(n), t, cap - 1, nbr);
+    const int ni = static_cast<int>(n);
+    const unsigned g = static_cast<unsigned>((n + 255) / 256);
+    const unsigned gm = static_cast<unsigned>((n + kMapVox - 1) / kMapVox);
+    cudaError_t e = cudaMemsetAsync(ctr, 0, sizeof(int), st);
+    if (e != cudaSuccess) return e;
+    table_clear_kernel<<<static_cast<unsigned>((bcap + 255) / 256), 256, 0, st>>>(bt, bcap);
+    brick_insert_kernel<<<g, 256, 0, st>>>(c4, ni, bt, bcap - 1, ctr, budget, status);
+    brick_clear_kernel<<<592, 256, 0, st>>>(rec, ctr, budget);
+    brick_fill_kernel<<<g, 256, 0, st>>>(c4, ni, bt, bcap - 1, rec, ctr, budget, status);
+    brick_neighbor_kernel<<<gm, 27 * kMapVox, 0, st>>>(c4, ni, bt, bcap - 1, rec, ctr, budget, nbr);
+    // too many bricks: the per-voxel hash (these kernels return at once otherwise)
+    gated_clear_kernel<<<592, 256, 0, st>>>(t, cap, ctr, budget);
+    gated_insert_kernel<<<g, 256, 0, st>>>(c4, ni, t, cap - 1, ctr, budget, status);
+    gated_neighbor_kernel<<<gm, 27 * kMapVox, 0, st>>>(c4, ni, t, cap - 1, ctr, budget, nbr);
     return cudaGetLastError();
 }
 

@@ -124,3 +124,19 @@ def test_out_of_range_coordinate_is_reported(ex):
     with pytest.raises(MscError, match="coordinate"):
         ex.check()
     ex.check()  # status was cleared
+
+
+@pytest.mark.parametrize("spacing", [4, 5])
+def test_sparse_input_takes_the_per_voxel_hash(ex, oracle, spacing):
+    """Voxels on a lattice of spacing >= 4 fill one 4x4x4 brick each: more
+    bricks than the record budget (n / 4 + 1024), so make_level switches to
+    the per-voxel hash on the device; plus a few dense clusters so that some
+    taps are present.  Bit-exact against the oracle either way."""
+    g = np.arange(0, 22 * spacing, spacing)
+    x, y, z = np.meshgrid(g, g, g[:12], indexing="ij")
+    lat = np.stack([x.ravel(), y.ravel(), z.ravel(), np.zeros(x.size, np.int64)], 1)
+    blob = np.array([(200 + a, 200 + b, 10 + c, 0) for a in range(3) for b in range(3) for c in range(3)])
+    coords = synth.dedup_sorted(np.concatenate([lat, blob]).astype(np.int32))
+    nbr = host(ex.make_level(dev(coords)))
+    ex.check()
+    np.testing.assert_array_equal(nbr, oracle.make_level(coords))
