@@ -693,9 +693,7 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         nbr = ex.make_level(coords_t)
         plan = ex.conv_plan(coords_t, nbr, plan_kind) if plan_kind else None
         if args.block == "ln" and (single or world == 1):
-            # one preparation pass: each block's second conv emits the next
-            # block's operand
-            ex.res_stack(x_t, nbr, blocks, plan=plan)
+            ex.res_stack(x_t, nbr, blocks, plan=plan)   # the level's block loop in one call
             return nbr
         for blk in blocks:
             if not single:

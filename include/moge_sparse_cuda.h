@@ -261,14 +261,10 @@ int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c,
                           const float* b1, const void* blob2, const float* b2, void* ws, size_t ws_bytes,
                           void* stream);
 
-/* nblocks residual blocks in a row (msc_res_block_planned per block), in
- * place on x.  Per-block parameters are arrays of nblocks pointers (norm_w,
- * norm_b, b1, b2 may be NULL arrays).  With fp16 x, C = 128 and Q8_0
- * weights, each block's second conv also emits the next block's
- * LayerNorm + SiLU + Q8_0 operand from the rows it writes, so the stack makes
- * one preparation pass instead of one per block; the result is identical to
- * the blocks run one by one (same operands, bit for bit).  Other formats run
- * the blocks one by one.  Workspace: msc_op_workspace_bytes(n, c).
+/* nblocks residual blocks in a row, in place on x: msc_res_block_planned
+ * per block (one call for a level's block loop).  Per-block parameters are
+ * arrays of nblocks pointers (norm_w, norm_b, b1, b2 may be NULL arrays).
+ * Workspace: msc_op_workspace_bytes(n, c).
  * Replaces: the level's res_block loop (src/sparse.cpp:1118-1121,
  * :1140-1143, :1173-1176). */
 int msc_res_stack(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr, const void* plan,

@@ -170,8 +170,7 @@ struct PlanUse {
 
 void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
               const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
-              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}, void* q_out = nullptr,
-              msc::NextOperand nx = {}) {
+              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}, void* q_out = nullptr) {
     msc::ConvArgs a{};
     a.planes = planes;
     a.q8 = mode == msc::ACT_Q8 || mode == msc::ACT_Q8I;
@@ -206,15 +205,6 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
                                               msc::act_scale_offset(msc::ACT_Q8I, n, b.cout));
     }
     a.status = ctx->status;
-    if (nx.codes) {
-        if (!(y_dtype == MSC_F16 && residual && res_dtype == MSC_F16 && b.cout == 128))
-            fail(MSC_E_UNSUPPORTED, "the fused next-block operand needs fp16 output and residual at 128 channels");
-        a.next_codes = nx.codes;
-        a.next_scales = nx.scales;
-        a.next_gamma = nx.gamma;
-        a.next_beta = nx.beta;
-        a.next_eps = nx.eps;
-    }
     a.perm = pu.order;
     a.tile_rows = pu.tiles.rows;
     a.tile_nbr = nbr ? pu.tiles.nbr : nullptr;
@@ -579,58 +569,14 @@ int msc_res_stack(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const i
                   void* stream) {
     return guard([&] {
         need_ctx(ctx);
-        need_dtype(x_dtype, "x");
         need(nblocks >= 0, "negative block count");
-        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
         if (n == 0 || nblocks == 0) return;
         need(blob1 && blob2, "null weight arrays");
         auto opt = [](const float* const* a, int i) { return a ? a[i] : nullptr; };
-        bool fused = x_dtype == MSC_F16 && c == 128;
         for (int i = 0; i < nblocks; ++i) {
-            const auto w1 = blob_info(ctx, blob1[i]);
-            const auto w2 = blob_info(ctx, blob2[i]);
-            check_conv_shape(w1, c, 27);
-            check_conv_shape(w2, c, 27);
-            need(w1.cout == c && w2.cout == c, "res_block convs must map c -> c");
-            fused = fused && w1.wtype == MSC_W_Q8_0 && w2.wtype == MSC_W_Q8_0;
-        }
-        if (!fused) {
-            // other formats: the blocks one by one
-            for (int i = 0; i < nblocks; ++i) {
-                const int rc = msc_res_block_planned(ctx, x, x_dtype, n, c, nbr, plan, opt(norm_w, i), opt(norm_b, i),
-                                                     blob1[i], opt(b1, i), blob2[i], opt(b2, i), ws, ws_bytes, stream);
-                if (rc != MSC_OK) fail(rc, g_err);
-            }
-            return;
-        }
-        const PlanUse pl = use_plan(ctx, plan, n);
-        need(x && nbr && ws, "null pointer");
-        need_aligned(x, 16, "x");
-        need_aligned(ws, 256, "workspace");
-        const size_t planes_bytes = align256(static_cast<size_t>(n) * c * 4);
-        need_ws(ws_bytes, planes_bytes + static_cast<size_t>(n) * c * 4);
-        void* planes = ws;
-        float* h = reinterpret_cast<float*>(static_cast<char*>(ws) + planes_bytes);
-        // block 0's operand by the preparation pass; every later block's
-        // by the previous block's second conv
-        cuda_ok(act_prepare(ctx, x, x_dtype, n, c, 1, opt(norm_w, 0), opt(norm_b, 0), 1e-6f, 1, msc::ACT_Q8I, planes,
-                            S(stream)),
-                "norm1 prepare");
-        for (int i = 0; i < nblocks; ++i) {
-            const auto w1 = blob_info(ctx, blob1[i]);
-            const auto w2 = blob_info(ctx, blob2[i]);
-            run_conv(ctx, planes, msc::ACT_Q8I, n, c, nbr, w1, blob1[i], opt(b1, i), 1, nullptr, 0, h, MSC_F32,
-                     S(stream), pl, h);
-            msc::NextOperand nx{};
-            if (i + 1 < nblocks) {
-                nx.codes = static_cast<int8_t*>(planes);
-                nx.scales = reinterpret_cast<float*>(static_cast<char*>(planes) + msc::act_scale_offset(msc::ACT_Q8I, n, c));
-                nx.gamma = opt(norm_w, i + 1);
-                nx.beta = opt(norm_b, i + 1);
-                nx.eps = 1e-6f;
-            }
-            run_conv(ctx, h, msc::ACT_Q8I, n, c, nbr, w2, blob2[i], opt(b2, i), 0, x, x_dtype, x, x_dtype, S(stream), pl,
-                     nullptr, nx);
+            const int rc = msc_res_block_planned(ctx, x, x_dtype, n, c, nbr, plan, opt(norm_w, i), opt(norm_b, i),
+                                                 blob1[i], opt(b1, i), blob2[i], opt(b2, i), ws, ws_bytes, stream);
+            if (rc != MSC_OK) fail(rc, "block " + std::to_string(i) + ": " + g_err);
         }
     });
 }

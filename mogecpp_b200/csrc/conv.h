@@ -98,17 +98,6 @@ struct ConvArgs {
     // < store_limit into the upper neighbour's peer_hi at row peer_hi_off +
     // (r - send_hi_begin).  The peer buffers are the neighbours' device memory
     // (CUDA IPC), written over NVLink.
-    // Fused operand of the next residual block (fp16 output with fp16
-    // residual, cout = 128): when next_codes is set, each output row y (as
-    // stored, fp16) also goes through LayerNorm (next_gamma, next_beta,
-    // next_eps), SiLU and ggml's Q8_0 quantiser into the ACT_Q8I operand
-    // next_codes [rows][128] / next_scales [rows][4], exactly as
-    // launch_act_prepare would compute it from the stored rows.
-    int8_t* next_codes;
-    float* next_scales;
-    const float* next_gamma;
-    const float* next_beta;
-    float next_eps;
     int64_t store_limit;
     void* peer_lo;
     int64_t peer_lo_off;
@@ -119,14 +108,6 @@ struct ConvArgs {
 };
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t st);
 
-// Where a conv's epilogue writes the next block's operand (ConvArgs::next_*).
-struct NextOperand {
-    int8_t* codes = nullptr;
-    float* scales = nullptr;
-    const float* gamma = nullptr;
-    const float* beta = nullptr;
-    float eps = 0.0f;
-};
 bool conv_supported(int cin, int cout);
 
 }  // namespace msc

@@ -368,89 +368,6 @@ __device__ void mma_issuer(const ConvArgs& a, const Smem& S, int64_t ntiles, uin
 constexpr int kMagicBits = 0x4B400000;
 constexpr float kMagic = 12582912.0f;
 
-__device__ __forceinline__ void quarter_sync(int q) {
-    // the four drain warps of TMEM lane quarter q (rows q*32 .. q*32+31);
-    // constant barrier ids (2..5)
-    switch (q) {
-        case 0: asm volatile("bar.sync 2, 128;" ::: "memory"); break;
-        case 1: asm volatile("bar.sync 3, 128;" ::: "memory"); break;
-        case 2: asm volatile("bar.sync 4, 128;" ::: "memory"); break;
-        default: asm volatile("bar.sync 5, 128;" ::: "memory"); break;
-    }
-}
-
-// The row's 32 fp16 outputs of this thread (h: 4 x 8 halves) as floats.
-__device__ __forceinline__ void halves_to_floats(const uint4 (&h)[4], float (&v)[32]) {
-#pragma unroll
-    for (int c8 = 0; c8 < 4; ++c8) {
-        const uint32_t w[4] = {h[c8].x, h[c8].y, h[c8].z, h[c8].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-            v[8 * c8 + 2 * e] = f.x;
-            v[8 * c8 + 2 * e + 1] = f.y;
-        }
-    }
-}
-
-// LayerNorm + SiLU + Q8_0 codes of the next block's first conv from this
-// thread's 32 output channels (v: the row's fp16 outputs as floats) of tile
-// row m; the row's other 96 channels are held by the three other
-// drain warps of lane quarter q.  Row sums are exchanged in the row's slot
-// of the tile's neighbour-list buffer (the drain no longer reads it; the
-// producers reuse it only after every drain warp has released the tile).
-// Summation order = launch_act_prepare's (16-channel lane sums combined as
-// ((s0+s4)+(s2+s6)) + ((s1+s5)+(s3+s7))), so the operand is bit-identical.
-__device__ __forceinline__ void next_operand(const ConvArgs& a, const Smem& S, int buf, int q, int part, int m, int row,
-                                          int c_base, float (&v)[32]) {
-    float* scr = reinterpret_cast<float*>(S.nbr + buf * BM * 27) + m * 27;
-    float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) s0 += v[k];
-#pragma unroll
-    for (int k = 16; k < 32; ++k) s1 += v[k];
-    quarter_sync(q);  // every warp of the quarter is done with the tile's lists
-    scr[2 * part] = s0;
-    scr[2 * part + 1] = s1;
-    quarter_sync(q);
-    const float mean = (((scr[0] + scr[4]) + (scr[2] + scr[6])) + ((scr[1] + scr[5]) + (scr[3] + scr[7]))) / 128;
-    float q0 = 0.0f, q1 = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        const float d = v[k] - mean;
-        q0 = fmaf(d, d, q0);
-    }
-#pragma unroll
-    for (int k = 16; k < 32; ++k) {
-        const float d = v[k] - mean;
-        q1 = fmaf(d, d, q1);
-    }
-    scr[8 + 2 * part] = q0;
-    scr[9 + 2 * part] = q1;
-    quarter_sync(q);
-    const float var = (((scr[8] + scr[12]) + (scr[10] + scr[14])) + ((scr[9] + scr[13]) + (scr[11] + scr[15]))) / 128;
-    const float scale = 1.0f / sqrtf(var + a.next_eps);
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-        float t = __fmul_rn(v[k] - mean, scale);
-        if (a.next_gamma) t = __fmul_rn(t, __ldg(a.next_gamma + c_base + k));
-        if (a.next_beta) t = __fadd_rn(t, __ldg(a.next_beta + c_base + k));
-        v[k] = silu_fast(t);
-    }
-    uint32_t w[8];
-    const float d = quantize_block32(v, w);
-    const int lane = threadIdx.x & 31;
-    if (row >= 0) a.next_scales[static_cast<int64_t>(row) * 4 + part] = d;
-    uint4 e[2] = {make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7])};
-    pair_transpose(e);
-    const int pb = lane & ~1, pk = lane & 1;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int r = __shfl_sync(0xffffffffu, row, pb + j);
-        if (r >= 0) reinterpret_cast<uint4*>(a.next_codes + (static_cast<int64_t>(r) * 4 + part) * 32)[pk] = e[j];
-    }
-}
-
 template <int CIN, int COUT, int NA, int NB, int KIND>
 __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32_t tmem) {
     using C = Cfg<CIN, COUT, NA, NB, KIND>;
@@ -693,8 +610,6 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                     }
                     h[c8] = make_uint4(w[0], w[1], w[2], w[3]);
                 }
-                float nv[32];
-                if (a.next_codes) halves_to_floats(h, nv);
                 quad_transpose(h);  // h[j] = chunk qk of row rj[j]
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -714,7 +629,6 @@ __device__ void drainer(const ConvArgs& a, const Smem& S, int64_t ntiles, uint32
                                                      (a.peer_hi_off + (r - a.send_hi_begin)) * COUT + c_base)[qk] = h[j];
                     }
                 }
-                if (a.next_codes) next_operand(a, S, buf, q, part, m, row, c_base, nv);
             }
         }
         if (row >= 0 && io == 0) {

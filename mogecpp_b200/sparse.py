@@ -228,9 +228,7 @@ class SparseCudaExecutor:
         return x
 
     def res_stack(self, x, nbr, blocks: list, plan=None):
-        """In place on x: len(blocks) residual blocks in a row (``msc_res_stack``:
-        with fp16 x, C = 128 and Q8_0 weights each block's second conv also
-        prepares the next block's operand)."""
+        """In place on x: len(blocks) residual blocks in a row (``msc_res_stack``)."""
         n, c = x.shape
         k = len(blocks)
         wsb = self.lib.msc_op_workspace_bytes(n, c)

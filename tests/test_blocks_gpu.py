@@ -134,10 +134,9 @@ def test_unet_level_bf16_matches_oracle(ex, oracle):
 
 
 @pytest.mark.parametrize("n_cut", [None, 777])
-def test_res_stack_fused_operand_equals_blocks_one_by_one(ex, oracle, n_cut):
-    """msc_res_stack (each block's second conv emits the next block's
-    LayerNorm + SiLU + Q8_0 operand) against the same blocks run one by one:
-    identical bits; and every block against the oracle on its input."""
+def test_res_stack_equals_blocks_one_by_one(ex, oracle, n_cut):
+    """msc_res_stack against the same blocks run one by one: identical bits;
+    and every block against the oracle on its input."""
     coords = synth.small_coords(140, extent=30, grid=32)
     if n_cut:
         coords = coords[:n_cut]   # a ragged last tile
