@@ -1,21 +1,31 @@
-// Sparse topology on the GPU: voxel hash, 27-tap submanifold neighbour map
-// and the stride-2 pool / upsample maps, bit-identical to the reference's
-// host code (mogecpp src/sparse.cpp:238-272 make_level, :312-357 downsample).
+// Sparse topology on the GPU: the 27-tap submanifold neighbour map and the
+// stride-2 pool / upsample maps, bit-identical to the reference's host code
+// (mogecpp src/sparse.cpp:238-272 make_level, :312-357 downsample).
 //
-// Keys: 64-bit packed (b, z, y, x), 7 + 3 x 19 bits (x in the low bits).
-// Table: open addressing, linear probing, 16-byte slots {key, value} so a
-// probe is one 16-byte load; capacity = power of two >= 2n (load <= 0.5).
-// The value of a key is the smallest voxel index holding it (atomicMin), the
-// "first insert wins" rule of FlatCoordMap::emplace (src/sparse.cpp:102-114).
+// Brick records (the default).  Voxels are grouped into 4 x 4 x 4 bricks: a
+// small hash table maps a brick key (b, z >> 2, y >> 2, x >> 2) to a brick id
+// (numbered in arrival order) and a brick record holds the 64 voxel indices
+// of its cells (empty cells INT_MAX; a duplicated coordinate keeps its
+// smallest index, FlatCoordMap's first-insert rule, src/sparse.cpp:102-114).
+// Surfaces put ~15-40 voxels in a brick, so the table and the records are a
+// few tens of MB and stay in L2.
+//   make_level: each voxel looks up the (at most 8) bricks its 27 taps reach
+//     once, then every tap is one record read;
+//   downsample: a voxel's 2 x 2 x 2 stride-2 cell lies inside its brick, so
+//     its siblings are the cell's 8 record entries: the parent's first child
+//     is their smallest index, the slot (arrival rank) the number of siblings
+//     with a smaller index and the count their number.
+// Parent ids follow the reference's serial loop exactly: the rank of the
+// parent's first child among all first children (first-occurrence order), by
+// a flag + exclusive scan; pool_rows is slot-major [8][np] with sentinel
+// nfine, inv_count = 1 / count, up_rows = fine -> parent id.
 //
-// Downsample numbering follows the reference's serial loop exactly:
-//   parent id   = rank of the parent's first child among first children
-//                 (first-occurrence order): flag + exclusive scan;
-//   slot        = number of siblings with a smaller fine index (the serial
-//                 arrival order), found by probing the parent's 8 child
-//                 coordinates in the fine table;
-//   pool_rows   = slot-major [8][np], sentinel nfine; inv_count = 1/count;
-//   up_rows     = fine -> parent id.
+// Per-voxel hash (inputs too sparse for the record budget, more than
+// n / 4 + 1024 bricks; the choice is made on the device from the brick
+// count, so both paths are launched and one returns at once).  Keys are the
+// 64-bit packed (b, z, y, x) (7 + 3 x 19 bits), open addressing with linear
+// probing in 16-byte slots {key, value}, capacity a power of two >= 2n.  The
+// allocation-free neighbour map (noalloc.cu) uses this path only.
 #include "common.cuh"
 #include "topology.h"
 
@@ -27,6 +37,11 @@ namespace {
 
 constexpr unsigned long long kEmpty = ~0ull;
 constexpr int kAxisMax = (1 << 19) - 1;
+constexpr int kNoVoxel = 0x7fffffff;
+constexpr int kBrickVox = 64;
+constexpr int kMapVox = 32;       // voxels per neighbour-map block (27 x 32 threads)
+constexpr int kScanBlock = 1024;
+constexpr unsigned kStrideGrid = 148 * 8;
 
 struct __align__(16) Slot {
     unsigned long long key;
@@ -53,15 +68,20 @@ __device__ __forceinline__ bool coord_ok(int4 c) {
            c.w < 127;
 }
 
-__global__ void table_clear_kernel(Slot* __restrict__ t, uint64_t cap) {
-    const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
-    if (i < cap) {
-        Slot s;
-        s.key = kEmpty;
-        s.val = 0x7fffffff;
-        s.pad = 0;
-        t[i] = s;
-    }
+// The per-voxel path's kernels run only while *gate > budget (the brick count
+// overflowed its budget), or always when gate is null.
+__device__ __forceinline__ bool gated_off(const int* gate, int budget) { return gate && *gate <= budget; }
+
+__device__ __forceinline__ uint64_t grid_index() { return blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; }
+__device__ __forceinline__ uint64_t grid_stride() { return static_cast<uint64_t>(gridDim.x) * blockDim.x; }
+
+__global__ void table_clear_kernel(Slot* __restrict__ t, uint64_t cap, const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
+    Slot s;
+    s.key = kEmpty;
+    s.val = kNoVoxel;
+    s.pad = 0;
+    for (uint64_t i = grid_index(); i < cap; i += grid_stride()) t[i] = s;
 }
 
 // Inserts key -> min(index).  Returns false when the table is full.
@@ -72,7 +92,7 @@ __device__ __forceinline__ bool table_insert(Slot* t, uint64_t mask, unsigned lo
         const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
         if (prev == kEmpty || prev == key) {
             const int old = atomicMin(&t[h].val, idx);
-            if (prev == key || old != 0x7fffffff) set_status(status, MSC_DEV_DUP_COORD);
+            if (prev == key || old != kNoVoxel) set_status(status, MSC_DEV_DUP_COORD);
             return true;
         }
         h = (h + 1) & mask;
@@ -93,92 +113,87 @@ __device__ __forceinline__ int table_find(const Slot* __restrict__ t, uint64_t m
     return -1;
 }
 
-// One thread per voxel: validate and insert (x, y, z, b) -> index.
+// Validate and insert (x, y, z, b) -> index.  Out-of-range coordinates are
+// reported here only when the kernel runs ungated (the brick insert reports
+// them otherwise).
 __global__ void insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ t, uint64_t mask,
-                              uint32_t* status) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) {
-        set_status(status, MSC_DEV_BAD_COORD);
-        return;
+                              uint32_t* status, const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
+    for (uint64_t i = grid_index(); i < static_cast<uint64_t>(n); i += grid_stride()) {
+        const int4 c = __ldg(coords + i);
+        if (!coord_ok(c)) {
+            if (!gate) set_status(status, MSC_DEV_BAD_COORD);
+            continue;
+        }
+        if (!table_insert(t, mask, pack_key(c.x, c.y, c.z, c.w), static_cast<int>(i), status))
+            set_status(status, MSC_DEV_HASH_FULL);
     }
-    if (!table_insert(t, mask, pack_key(c.x, c.y, c.z, c.w), i, status)) set_status(status, MSC_DEV_HASH_FULL);
 }
 
-// Neighbour map.  A block of 27 x 32 threads covers 32 consecutive voxels:
-// thread (tap, v) probes one neighbour, results are staged in shared memory
-// and written back as one contiguous [32][27] run.
-constexpr int kMapVox = 32;
-
+// Neighbour map over the per-voxel table.  A block of 27 x 32 threads covers
+// groups of 32 consecutive voxels: thread (tap, v) probes one neighbour; a
+// group's results are staged in shared memory and written back as one
+// contiguous [32][27] run.
 __global__ void __launch_bounds__(27 * kMapVox) neighbor_kernel(const int4* __restrict__ coords, int n,
                                                                 const Slot* __restrict__ t, uint64_t mask,
-                                                                int* __restrict__ nbr) {
+                                                                int* __restrict__ nbr, const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
     __shared__ int4 sc[kMapVox];
     __shared__ int sn[kMapVox * 27];
-    const int base = blockIdx.x * kMapVox;
     const int tid = threadIdx.x;
-    if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
-    __syncthreads();
     const int v = tid % kMapVox;
     const int tap = tid / kMapVox;
-    if (base + v < n) {
-        const int4 c = sc[v];
-        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-        const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
-        int found = n;
-        if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
-            const int idx = table_find(t, mask, pack_key(qx, qy, qz, c.w));
-            if (idx >= 0) found = idx;
+    const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kMapVox; base < n;
+         base += static_cast<int64_t>(gridDim.x) * kMapVox) {
+        if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
+        __syncthreads();
+        if (base + v < n) {
+            const int4 c = sc[v];
+            const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
+            int found = n;
+            if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
+                const int idx = table_find(t, mask, pack_key(qx, qy, qz, c.w));
+                if (idx >= 0) found = idx;
+            }
+            sn[v * 27 + tap] = found;
         }
-        sn[v * 27 + tap] = found;
+        __syncthreads();
+        const int64_t count = (n - base < kMapVox ? n - base : kMapVox) * 27;
+        int* out = nbr + base * 27;
+        for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
+        __syncthreads();
     }
-    __syncthreads();
-    const int count = min(kMapVox, n - base) * 27;
-    int* out = nbr + static_cast<int64_t>(base) * 27;
-    for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
 }
 
-// ---- downsample ----------------------------------------------------------
+// ---- downsample over the per-voxel tables ---------------------------------
 
 __global__ void parent_insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ tp, uint64_t pmask,
-                                     uint32_t* status) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) {
-        set_status(status, MSC_DEV_BAD_COORD);
-        return;
-    }
-    // the parent table only needs min-index semantics; duplicates of a
-    // parent key are the normal case, so no duplicate flag here
-    const unsigned long long key = pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
-    uint64_t h = mix64(key) & pmask;
-    for (uint64_t probe = 0; probe <= pmask; ++probe) {
-        const unsigned long long prev = atomicCAS(&tp[h].key, kEmpty, key);
-        if (prev == kEmpty || prev == key) {
-            atomicMin(&tp[h].val, i);
-            return;
+                                     uint32_t* status, const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
+    for (uint64_t i = grid_index(); i < static_cast<uint64_t>(n); i += grid_stride()) {
+        const int4 c = __ldg(coords + i);
+        if (!coord_ok(c)) continue;
+        // the parent table only needs min-index semantics; duplicates of a
+        // parent key are the normal case, so no duplicate flag here
+        const unsigned long long key = pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
+        uint64_t h = mix64(key) & pmask;
+        bool done = false;
+        for (uint64_t probe = 0; probe <= pmask && !done; ++probe) {
+            const unsigned long long prev = atomicCAS(&tp[h].key, kEmpty, key);
+            if (prev == kEmpty || prev == key) {
+                atomicMin(&tp[h].val, static_cast<int>(i));
+                done = true;
+            }
+            h = (h + 1) & pmask;
         }
-        h = (h + 1) & pmask;
+        if (!done) set_status(status, MSC_DEV_HASH_FULL);
     }
-    set_status(status, MSC_DEV_HASH_FULL);
 }
 
-constexpr int kScanBlock = 1024;
-
-// Pass 1: first[i] = (i is the first child of its parent); per-block
-// exclusive scan into excl[], block totals into bsum[].
-__global__ void __launch_bounds__(kScanBlock) first_scan_kernel(const int4* __restrict__ coords, int n,
-                                                                const Slot* __restrict__ tp, uint64_t pmask,
-                                                                int* __restrict__ excl, int* __restrict__ bsum) {
-    __shared__ int warp_tot[kScanBlock / 32];
-    const int i = blockIdx.x * kScanBlock + threadIdx.x;
-    int f = 0;
-    if (i < n) {
-        const int4 c = __ldg(coords + i);
-        if (coord_ok(c)) f = table_find(tp, pmask, pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w)) == i;
-    }
+// Block-level exclusive scan of flags f (one per thread): returns the
+// exclusive prefix within the block; the block total goes to *total.
+__device__ __forceinline__ int block_exclusive_scan(int f, int* warp_tot, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int inc = f;
 #pragma unroll
@@ -189,7 +204,7 @@ __global__ void __launch_bounds__(kScanBlock) first_scan_kernel(const int4* __re
     if (lane == 31) warp_tot[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        int w = warp_tot[lane];
+        const int w = warp_tot[lane];
         int wi = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -197,120 +212,104 @@ __global__ void __launch_bounds__(kScanBlock) first_scan_kernel(const int4* __re
             if (lane >= o) wi += v;
         }
         warp_tot[lane] = wi - w;
-        if (lane == 31) bsum[blockIdx.x] = wi;
+        if (lane == 31) *total = wi;
     }
     __syncthreads();
-    if (i < n) excl[i] = warp_tot[warp] + inc - f;
+    return warp_tot[warp] + inc - f;
 }
 
-// Pass 2: single block, exclusive scan of block totals; np -> *np_out.
+// first[i] = (i is the first child of its parent); per-block exclusive scan
+// into excl[], block totals into bsum[].
+__global__ void __launch_bounds__(kScanBlock) first_scan_kernel(const int4* __restrict__ coords, int n,
+                                                                const Slot* __restrict__ tp, uint64_t pmask,
+                                                                int* __restrict__ excl, int* __restrict__ bsum,
+                                                                const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
+    __shared__ int warp_tot[kScanBlock / 32];
+    const int i = blockIdx.x * kScanBlock + threadIdx.x;
+    int f = 0;
+    if (i < n) {
+        const int4 c = __ldg(coords + i);
+        if (coord_ok(c)) f = table_find(tp, pmask, pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w)) == i;
+    }
+    const int e = block_exclusive_scan(f, warp_tot, bsum + blockIdx.x);
+    if (i < n) excl[i] = e;
+}
+
+// Single block: exclusive scan of the block totals; np -> *np_out.
 __global__ void __launch_bounds__(kScanBlock) block_scan_kernel(int* __restrict__ bsum, int nblocks,
                                                                 int* __restrict__ np_out) {
     __shared__ int warp_tot[kScanBlock / 32];
-    __shared__ int carry;
+    __shared__ int carry, total;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int base = 0; base < nblocks; base += kScanBlock) {
         const int i = base + threadIdx.x;
         const int f = i < nblocks ? bsum[i] : 0;
-        int inc = f;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += v;
-        }
-        if (lane == 31) warp_tot[warp] = inc;
-        __syncthreads();
-        if (warp == 0) {
-            int w = warp_tot[lane];
-            int wi = w;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, wi, o);
-                if (lane >= o) wi += v;
-            }
-            warp_tot[lane] = wi - w;
-        }
-        __syncthreads();
+        const int e = block_exclusive_scan(f, warp_tot, &total);
         const int c0 = carry;
-        if (i < nblocks) bsum[i] = c0 + warp_tot[warp] + inc - f;
+        if (i < nblocks) bsum[i] = c0 + e;
         __syncthreads();
-        if (threadIdx.x == kScanBlock - 1) carry = c0 + warp_tot[warp] + inc;
+        if (threadIdx.x == 0) carry = c0 + total;
         __syncthreads();
     }
     if (threadIdx.x == 0) *np_out = carry;
 }
 
-// Pass 3: parent ids, up_rows, parent coordinates.
+// Parent ids, up_rows, parent coordinates.
 __global__ void assign_kernel(const int4* __restrict__ coords, int n, const Slot* __restrict__ tp, uint64_t pmask,
                               const int* __restrict__ excl, const int* __restrict__ bsum, int4* __restrict__ parent,
-                              int* __restrict__ up_rows) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) return;
-    const int first = table_find(tp, pmask, pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w));
-    if (first < 0 || first >= n) return;
-    const int pid = excl[first] + bsum[first / kScanBlock];
-    up_rows[i] = pid;
-    if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
+                              int* __restrict__ up_rows, const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
+    for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
+        const int i = static_cast<int>(u);
+        const int4 c = __ldg(coords + i);
+        if (!coord_ok(c)) continue;
+        const int first = table_find(tp, pmask, pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w));
+        if (first < 0 || first >= n) continue;
+        const int pid = excl[first] + bsum[first / kScanBlock];
+        up_rows[i] = pid;
+        if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
+    }
 }
 
 __global__ void pool_fill_kernel(int* __restrict__ pool_rows, const int* __restrict__ np_dev, int nfine) {
     const int64_t total = 8ll * (*np_dev);
-    for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; k < total;
-         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        pool_rows[k] = nfine;
+    for (int64_t k = grid_index(); k < total; k += grid_stride()) pool_rows[k] = nfine;
 }
 
-// Pass 4: slot = number of siblings with a smaller fine index.
+// slot = number of siblings with a smaller fine index.
 __global__ void slot_kernel(const int4* __restrict__ coords, int n, const Slot* __restrict__ tf, uint64_t fmask,
                             const int* __restrict__ up_rows, const int* __restrict__ np_dev, int* __restrict__ pool_rows,
-                            float* __restrict__ inv_count, uint32_t* status) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) return;
-    const int px = c.x >> 1, py = c.y >> 1, pz = c.z >> 1;
-    int count = 0, rank = 0;
-#pragma unroll
-    for (int o = 0; o < 8; ++o) {
-        const int j = table_find(tf, fmask, pack_key(2 * px + (o >> 2), 2 * py + ((o >> 1) & 1), 2 * pz + (o & 1), c.w));
-        if (j >= 0) {
-            ++count;
-            rank += j < i;
-        }
-    }
-    const int pid = up_rows[i];
+                            float* __restrict__ inv_count, uint32_t* status, const int* gate, int budget) {
+    if (gated_off(gate, budget)) return;
     const int np = *np_dev;
-    if (pid < 0 || pid >= np || rank >= 8) {
-        set_status(status, MSC_DEV_POOL_OVERFLOW);
-        return;
+    for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
+        const int i = static_cast<int>(u);
+        const int4 c = __ldg(coords + i);
+        if (!coord_ok(c)) continue;
+        const int px = c.x >> 1, py = c.y >> 1, pz = c.z >> 1;
+        int count = 0, rank = 0;
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+            const int j =
+                table_find(tf, fmask, pack_key(2 * px + (o >> 2), 2 * py + ((o >> 1) & 1), 2 * pz + (o & 1), c.w));
+            if (j >= 0) {
+                ++count;
+                rank += j < i;
+            }
+        }
+        const int pid = up_rows[i];
+        if (pid < 0 || pid >= np || rank >= 8) {
+            set_status(status, MSC_DEV_POOL_OVERFLOW);
+            continue;
+        }
+        pool_rows[static_cast<int64_t>(rank) * np + pid] = i;
+        if (rank == 0) inv_count[pid] = 1.0f / static_cast<float>(count);
     }
-    pool_rows[static_cast<int64_t>(rank) * np + pid] = i;
-    if (rank == 0) inv_count[pid] = 1.0f / static_cast<float>(count);
 }
 
-uint64_t table_capacity(int64_t n) {
-    uint64_t cap = 64;
-    while (cap < static_cast<uint64_t>(2 * n)) cap <<= 1;
-    return cap;
-}
-
-// ---- brick map (make_level) ----------------------------------------------
-// Voxels are grouped into 4 x 4 x 4 bricks: a small hash table maps a brick
-// key (b, z >> 2, y >> 2, x >> 2) to a brick id (numbered in arrival order),
-// and a brick record holds the 64 voxel indices of its cells (INT_MAX =
-// empty; the smallest index of a duplicated coordinate, FlatCoordMap's
-// first-insert rule).  A neighbour query is one brick-table probe plus one
-// record read.  Surfaces fill a brick with ~15-40 voxels, so the table and
-// the records are a few tens of MB and stay in L2, and the 32 voxels of a
-// query warp (consecutive rows, mostly one or two bricks) probe the same
-// slots.  Inputs too sparse for the record budget (more than n / 4 + 1024
-// bricks) take the per-voxel hash instead; the choice is made on the device.
-constexpr int kBrickVox = 64;
-constexpr int kNoVoxel = 0x7fffffff;
+// ---- brick records ---------------------------------------------------------
 
 int64_t brick_budget(int64_t n) { return n / 4 + 1024; }
 uint64_t brick_capacity(int64_t n) {
@@ -319,62 +318,61 @@ uint64_t brick_capacity(int64_t n) {
     return cap;
 }
 
-__device__ __forceinline__ unsigned long long brick_key(int x, int y, int z, int b) {
-    return pack_key(x >> 2, y >> 2, z >> 2, b);
-}
+__device__ __forceinline__ unsigned long long brick_key(int bx, int by, int bz, int b) { return pack_key(bx, by, bz, b); }
 __device__ __forceinline__ int brick_cell(int x, int y, int z) { return (x & 3) | ((y & 3) << 2) | ((z & 3) << 4); }
 
 // ctr[0] = bricks numbered so far (forced above the budget when the table
 // runs out, which selects the per-voxel hash)
 __global__ void brick_insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ t, uint64_t mask,
                                     int* __restrict__ ctr, int budget, uint32_t* status) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) {
-        set_status(status, MSC_DEV_BAD_COORD);
-        return;
-    }
-    const unsigned long long key = brick_key(c.x, c.y, c.z, c.w);
-    uint64_t h = mix64(key) & mask;
-    for (uint64_t probe = 0; probe <= mask; ++probe) {
-        const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
-        if (prev == kEmpty) {
-            t[h].val = atomicAdd(ctr, 1);
-            return;
+    for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
+        const int4 c = __ldg(coords + u);
+        if (!coord_ok(c)) {
+            set_status(status, MSC_DEV_BAD_COORD);
+            continue;
         }
-        if (prev == key) return;
-        h = (h + 1) & mask;
+        const unsigned long long key = brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w);
+        uint64_t h = mix64(key) & mask;
+        bool done = false;
+        for (uint64_t probe = 0; probe <= mask && !done; ++probe) {
+            const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
+            if (prev == kEmpty) t[h].val = atomicAdd(ctr, 1);
+            done = prev == kEmpty || prev == key;
+            h = (h + 1) & mask;
+        }
+        if (!done) atomicMax(ctr, budget + 1);
     }
-    atomicMax(ctr, budget + 1);
 }
 
 __global__ void brick_clear_kernel(int* __restrict__ rec, const int* __restrict__ ctr, int budget) {
     const int nb = *ctr;
     if (nb > budget) return;
     const int64_t total = static_cast<int64_t>(nb) * kBrickVox;
-    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
-         e += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        rec[e] = kNoVoxel;
-}
-
-__device__ __forceinline__ int brick_find(const Slot* __restrict__ t, uint64_t mask, unsigned long long key) {
-    return table_find(t, mask, key);
+    for (int64_t e = grid_index(); e < total; e += grid_stride()) rec[e] = kNoVoxel;
 }
 
 __global__ void brick_fill_kernel(const int4* __restrict__ coords, int n, const Slot* __restrict__ t, uint64_t mask,
                                   int* __restrict__ rec, const int* __restrict__ ctr, int budget, uint32_t* status) {
     if (*ctr > budget) return;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) return;
-    const int id = brick_find(t, mask, brick_key(c.x, c.y, c.z, c.w));
-    if (id < 0) return;  // cannot happen: every voxel's brick was inserted
-    const int old = atomicMin(&rec[static_cast<int64_t>(id) * kBrickVox + brick_cell(c.x, c.y, c.z)], i);
-    if (old != kNoVoxel) set_status(status, MSC_DEV_DUP_COORD);
+    for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
+        const int4 c = __ldg(coords + u);
+        if (!coord_ok(c)) continue;
+        const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
+        if (id < 0) continue;  // cannot happen: every voxel's brick was inserted
+        const int old = atomicMin(&rec[static_cast<int64_t>(id) * kBrickVox + brick_cell(c.x, c.y, c.z)],
+                                  static_cast<int>(u));
+        if (old != kNoVoxel) set_status(status, MSC_DEV_DUP_COORD);
+    }
 }
 
+// Neighbour map over the brick records.  Per group of 32 consecutive voxels:
+//   1. 8 x 32 threads look up, per voxel, the bricks its taps can reach:
+//      offset bits (ox, oy, oz); on an axis with the bit set the neighbour
+//      brick is the one below when the voxel sits on the brick's low face
+//      (cell coordinate 0), above on the high face (3), none otherwise;
+//   2. 27 x 32 threads: tap t of voxel v reads the record entry of its
+//      neighbour cell in the brick looked up in step 1;
+//   3. the [32][27] results leave as one contiguous run.
 __global__ void __launch_bounds__(27 * kMapVox) brick_neighbor_kernel(const int4* __restrict__ coords, int n,
                                                                       const Slot* __restrict__ t, uint64_t mask,
                                                                       const int* __restrict__ rec,
@@ -382,132 +380,223 @@ __global__ void __launch_bounds__(27 * kMapVox) brick_neighbor_kernel(const int4
                                                                       int* __restrict__ nbr) {
     if (*ctr > budget) return;
     __shared__ int4 sc[kMapVox];
+    __shared__ int sb[kMapVox * 8];
     __shared__ int sn[kMapVox * 27];
-    const int base = blockIdx.x * kMapVox;
     const int tid = threadIdx.x;
-    if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
-    __syncthreads();
     const int v = tid % kMapVox;
     const int tap = tid / kMapVox;
-    if (base + v < n) {
-        const int4 c = sc[v];
-        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-        const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
-        int found = n;
-        if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
-            const int id = brick_find(t, mask, brick_key(qx, qy, qz, c.w));
-            if (id >= 0) {
-                const int j = __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz));
-                if (j != kNoVoxel) found = j;
+    const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kMapVox; base < n;
+         base += static_cast<int64_t>(gridDim.x) * kMapVox) {
+        if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
+        __syncthreads();
+        if (tid < 8 * kMapVox) {
+            const int o = tid / kMapVox;  // offset bits
+            int id = -1;
+            if (base + v < n) {
+                const int4 c = sc[v];
+                if (coord_ok(c)) {
+                    const int lx = c.x & 3, ly = c.y & 3, lz = c.z & 3;
+                    const int ox = (o & 1) ? (lx == 0 ? -1 : (lx == 3 ? 1 : 2)) : 0;
+                    const int oy = (o & 2) ? (ly == 0 ? -1 : (ly == 3 ? 1 : 2)) : 0;
+                    const int oz = (o & 4) ? (lz == 0 ? -1 : (lz == 3 ? 1 : 2)) : 0;
+                    const int bx = (c.x >> 2) + ox, by = (c.y >> 2) + oy, bz = (c.z >> 2) + oz;
+                    if (ox != 2 && oy != 2 && oz != 2 && bx >= 0 && by >= 0 && bz >= 0 && bx <= (kAxisMax >> 2) &&
+                        by <= (kAxisMax >> 2) && bz <= (kAxisMax >> 2))
+                        id = table_find(t, mask, brick_key(bx, by, bz, c.w));
+                }
             }
+            sb[v * 8 + o] = id;
         }
-        sn[v * 27 + tap] = found;
+        __syncthreads();
+        if (base + v < n) {
+            const int4 c = sc[v];
+            const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
+            int found = n;
+            if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
+                const int o = ((qx >> 2) != (c.x >> 2)) | (((qy >> 2) != (c.y >> 2)) << 1) |
+                              (((qz >> 2) != (c.z >> 2)) << 2);
+                const int id = sb[v * 8 + o];
+                if (id >= 0) {
+                    const int j = __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz));
+                    if (j != kNoVoxel) found = j;
+                }
+            }
+            sn[v * 27 + tap] = found;
+        }
+        __syncthreads();
+        const int64_t count = (n - base < kMapVox ? n - base : kMapVox) * 27;
+        int* out = nbr + base * 27;
+        for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
+        __syncthreads();
     }
-    __syncthreads();
-    const int count = min(kMapVox, n - base) * 27;
-    int* out = nbr + static_cast<int64_t>(base) * 27;
-    for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
 }
 
-// The per-voxel hash path, run only when the brick count exceeded the budget.
-__global__ void gated_clear_kernel(Slot* __restrict__ t, uint64_t cap, const int* __restrict__ ctr, int budget) {
-    if (*ctr <= budget) return;
-    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < cap;
-         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        Slot s;
-        s.key = kEmpty;
-        s.val = 0x7fffffff;
-        s.pad = 0;
-        t[i] = s;
+// The 8 record entries of voxel c's stride-2 cell (the 2 x 2 x 2 block of
+// cells with the same parent, inside c's brick): first child (smallest
+// index), the count, and the number with a smaller index than i.
+struct CellInfo {
+    int first, count, rank;
+};
+__device__ __forceinline__ CellInfo cell_info(const int* __restrict__ rec, int id, int4 c, int i) {
+    const int* r = rec + static_cast<int64_t>(id) * kBrickVox;
+    const int x0 = c.x & 2, y0 = c.y & 2, z0 = c.z & 2;
+    CellInfo ci{kNoVoxel, 0, 0};
+#pragma unroll
+    for (int o = 0; o < 8; ++o) {
+        const int j = __ldg(r + brick_cell(x0 + (o >> 2), y0 + ((o >> 1) & 1), z0 + (o & 1)));
+        if (j != kNoVoxel) {
+            ++ci.count;
+            ci.rank += j < i;
+            ci.first = min(ci.first, j);
+        }
     }
+    return ci;
 }
 
-__global__ void gated_insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ t, uint64_t mask,
-                                    const int* __restrict__ ctr, int budget, uint32_t* status) {
-    if (*ctr <= budget) return;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int4 c = __ldg(coords + i);
-    if (!coord_ok(c)) return;  // reported by the brick insert
-    if (!table_insert(t, mask, pack_key(c.x, c.y, c.z, c.w), i, status)) set_status(status, MSC_DEV_HASH_FULL);
-}
-
-__global__ void __launch_bounds__(27 * kMapVox) gated_neighbor_kernel(const int4* __restrict__ coords, int n,
+// first_idx[i] = the first child of i's parent; per-block exclusive scan of
+// the flags (i == first) into excl[], block totals into bsum[].
+__global__ void __launch_bounds__(kScanBlock) brick_first_scan_kernel(const int4* __restrict__ coords, int n,
                                                                       const Slot* __restrict__ t, uint64_t mask,
+                                                                      const int* __restrict__ rec,
                                                                       const int* __restrict__ ctr, int budget,
-                                                                      int* __restrict__ nbr) {
-    if (*ctr <= budget) return;
-    __shared__ int4 sc[kMapVox];
-    __shared__ int sn[kMapVox * 27];
-    const int base = blockIdx.x * kMapVox;
-    const int tid = threadIdx.x;
-    if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
-    __syncthreads();
-    const int v = tid % kMapVox;
-    const int tap = tid / kMapVox;
-    if (base + v < n) {
-        const int4 c = sc[v];
-        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-        const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
-        int found = n;
-        if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
-            const int idx = table_find(t, mask, pack_key(qx, qy, qz, c.w));
-            if (idx >= 0) found = idx;
+                                                                      int* __restrict__ first_idx,
+                                                                      int* __restrict__ excl, int* __restrict__ bsum) {
+    if (*ctr > budget) return;
+    __shared__ int warp_tot[kScanBlock / 32];
+    const int i = blockIdx.x * kScanBlock + threadIdx.x;
+    int f = 0;
+    if (i < n) {
+        const int4 c = __ldg(coords + i);
+        int first = -1;
+        if (coord_ok(c)) {
+            const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
+            if (id >= 0) first = cell_info(rec, id, c, i).first;
         }
-        sn[v * 27 + tap] = found;
+        first_idx[i] = first;
+        f = first == i;
     }
-    __syncthreads();
-    const int count = min(kMapVox, n - base) * 27;
-    int* out = nbr + static_cast<int64_t>(base) * 27;
-    for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
+    const int e = block_exclusive_scan(f, warp_tot, bsum + blockIdx.x);
+    if (i < n) excl[i] = e;
+}
+
+// Parent ids, up_rows, parent coordinates, pool_rows slots and inv_count.
+__global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, const Slot* __restrict__ t, uint64_t mask,
+                                    const int* __restrict__ rec, const int* __restrict__ ctr, int budget,
+                                    const int* __restrict__ first_idx, const int* __restrict__ excl,
+                                    const int* __restrict__ bsum, const int* __restrict__ np_dev,
+                                    int4* __restrict__ parent, int* __restrict__ up_rows, int* __restrict__ pool_rows,
+                                    float* __restrict__ inv_count, uint32_t* status) {
+    if (*ctr > budget) return;
+    const int np = *np_dev;
+    for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
+        const int i = static_cast<int>(u);
+        const int first = first_idx[i];
+        if (first < 0 || first >= n) continue;
+        const int4 c = __ldg(coords + i);
+        const int pid = excl[first] + bsum[first / kScanBlock];
+        up_rows[i] = pid;
+        if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
+        const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
+        const CellInfo ci = cell_info(rec, id, c, i);
+        if (pid < 0 || pid >= np || ci.rank >= 8) {
+            set_status(status, MSC_DEV_POOL_OVERFLOW);
+            continue;
+        }
+        pool_rows[static_cast<int64_t>(ci.rank) * np + pid] = i;
+        if (ci.rank == 0) inv_count[pid] = 1.0f / static_cast<float>(ci.count);
+    }
+}
+
+uint64_t table_capacity(int64_t n) {
+    uint64_t cap = 64;
+    while (cap < static_cast<uint64_t>(2 * n)) cap <<= 1;
+    return cap;
 }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+unsigned stride_grid(int64_t n, int per) {
+    const int64_t g = (n + per - 1) / per;
+    return static_cast<unsigned>(g < kStrideGrid ? (g > 0 ? g : 1) : kStrideGrid);
+}
+
+}  // namespace
+
+// Workspace layout (shared by make_level and downsample):
+//   per-voxel tables: 2 x cap slots (make_level uses the first; downsample
+//   the fine and parent tables) | excl [n + 1] | bsum | brick table (bcap
+//   slots) | brick records [budget][64] | counter | first child [n]
+namespace {
+struct TopoWs {
+    Slot* t;
+    int* excl;
+    int* bsum;
+    Slot* bt;
+    int* rec;
+    int* ctr;
+    int* first;
+    uint64_t cap, bcap;
+    int budget;
+};
+
+TopoWs carve(void* ws, int64_t n) {
+    TopoWs w;
+    w.cap = table_capacity(n);
+    w.bcap = brick_capacity(n);
+    w.budget = static_cast<int>(brick_budget(n));
+    const int64_t nblk = (n + kScanBlock - 1) / kScanBlock + 1;
+    char* p = static_cast<char*>(ws);
+    w.t = reinterpret_cast<Slot*>(p);
+    p += align_up(2 * w.cap * sizeof(Slot), 256);
+    w.excl = reinterpret_cast<int*>(p);
+    p += align_up(static_cast<size_t>(n + 1) * 4, 256);
+    w.bsum = reinterpret_cast<int*>(p);
+    p += align_up(static_cast<size_t>(nblk) * 4, 256);
+    w.bt = reinterpret_cast<Slot*>(p);
+    p += align_up(w.bcap * sizeof(Slot), 256);
+    w.rec = reinterpret_cast<int*>(p);
+    p += align_up(static_cast<size_t>(w.budget) * kBrickVox * 4, 256);
+    w.ctr = reinterpret_cast<int*>(p);
+    p += 256;
+    w.first = reinterpret_cast<int*>(p);
+    return w;
+}
+
+// Brick table + records of the n voxels (counter, clear, insert, fill).
+cudaError_t launch_brick_build(const int4* c4, int n, const TopoWs& w, uint32_t* status, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(w.ctr, 0, sizeof(int), st);
+    if (e != cudaSuccess) return e;
+    table_clear_kernel<<<stride_grid(static_cast<int64_t>(w.bcap), 256), 256, 0, st>>>(w.bt, w.bcap, nullptr, 0);
+    brick_insert_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, n, w.bt, w.bcap - 1, w.ctr, w.budget, status);
+    brick_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.rec, w.ctr, w.budget);
+    brick_fill_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, n, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, status);
+    return cudaGetLastError();
+}
 }  // namespace
 
 size_t topology_workspace_bytes(int64_t n) {
-    const uint64_t cap = table_capacity(n);
     const int64_t nblk = (n + kScanBlock - 1) / kScanBlock + 1;
-    // downsample: fine and parent tables + scan arrays; make_level: the
-    // per-voxel table (first half of the pair), then the brick table, the
-    // brick records and the counter
-    const size_t down = align_up(2 * cap * sizeof(Slot), 256) + align_up(static_cast<size_t>(n + 1) * 4, 256) +
-                        align_up(static_cast<size_t>(nblk) * 4, 256) + 256;
-    const size_t level = align_up(cap * sizeof(Slot), 256) + align_up(brick_capacity(n) * sizeof(Slot), 256) +
-                         align_up(static_cast<size_t>(brick_budget(n)) * kBrickVox * 4, 256) + 256;
-    return down > level ? down : level;
+    return align_up(2 * table_capacity(n) * sizeof(Slot), 256) + align_up(static_cast<size_t>(n + 1) * 4, 256) +
+           align_up(static_cast<size_t>(nblk) * 4, 256) + align_up(brick_capacity(n) * sizeof(Slot), 256) +
+           align_up(static_cast<size_t>(brick_budget(n)) * kBrickVox * 4, 256) + 256 +
+           align_up(static_cast<size_t>(n) * 4, 256);
 }
 
 cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, void* ws, uint32_t* status,
                               cudaStream_t st) {
     if (n == 0) return cudaSuccess;
-    const uint64_t cap = table_capacity(n);
-    const uint64_t bcap = brick_capacity(n);
-    const int budget = static_cast<int>(brick_budget(n));
-    char* p = static_cast<char*>(ws);
-    Slot* t = reinterpret_cast<Slot*>(p);
-    p += align_up(cap * sizeof(Slot), 256);
-    Slot* bt = reinterpret_cast<Slot*>(p);
-    p += align_up(bcap * sizeof(Slot), 256);
-    int* rec = reinterpret_cast<int*>(p);
-    p += align_up(static_cast<size_t>(budget) * kBrickVox * 4, 256);
-    int* ctr = reinterpret_cast<int*>(p);
+    const TopoWs w = carve(ws, n);
     const auto* c4 = reinterpret_cast<const int4*>(coords);
     const int ni = static_cast<int>(n);
-    const unsigned g = static_cast<unsigned>((n + 255) / 256);
-    const unsigned gm = static_cast<unsigned>((n + kMapVox - 1) / kMapVox);
-    cudaError_t e = cudaMemsetAsync(ctr, 0, sizeof(int), st);
+    cudaError_t e = launch_brick_build(c4, ni, w, status, st);
     if (e != cudaSuccess) return e;
-    table_clear_kernel<<<static_cast<unsigned>((bcap + 255) / 256), 256, 0, st>>>(bt, bcap);
-    brick_insert_kernel<<<g, 256, 0, st>>>(c4, ni, bt, bcap - 1, ctr, budget, status);
-    brick_clear_kernel<<<592, 256, 0, st>>>(rec, ctr, budget);
-    brick_fill_kernel<<<g, 256, 0, st>>>(c4, ni, bt, bcap - 1, rec, ctr, budget, status);
-    brick_neighbor_kernel<<<gm, 27 * kMapVox, 0, st>>>(c4, ni, bt, bcap - 1, rec, ctr, budget, nbr);
-    // too many bricks: the per-voxel hash (these kernels return at once otherwise)
-    gated_clear_kernel<<<592, 256, 0, st>>>(t, cap, ctr, budget);
-    gated_insert_kernel<<<g, 256, 0, st>>>(c4, ni, t, cap - 1, ctr, budget, status);
-    gated_neighbor_kernel<<<gm, 27 * kMapVox, 0, st>>>(c4, ni, t, cap - 1, ctr, budget, nbr);
+    brick_neighbor_kernel<<<stride_grid(n, kMapVox), 27 * kMapVox, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr,
+                                                                            w.budget, nbr);
+    // too many bricks: the per-voxel hash (these return at once otherwise)
+    table_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.t, w.cap, w.ctr, w.budget);
+    insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, w.t, w.cap - 1, status, w.ctr, w.budget);
+    neighbor_kernel<<<stride_grid(n, kMapVox), 27 * kMapVox, 0, st>>>(c4, ni, w.t, w.cap - 1, nbr, w.ctr, w.budget);
     return cudaGetLastError();
 }
 
@@ -519,40 +608,42 @@ cudaError_t launch_make_level_in_table(const int32_t* coords, int64_t n, int32_t
     const uint64_t cap = table_capacity(n);
     if (cap * sizeof(Slot) > table_bytes) return cudaErrorInvalidValue;
     Slot* t = static_cast<Slot*>(table);
-    table_clear_kernel<<<static_cast<unsigned>((cap + 255) / 256), 256, 0, st>>>(t, cap);
     const auto* c4 = reinterpret_cast<const int4*>(coords);
-    insert_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(c4, static_cast<int>(n), t, cap - 1,
-                                                                          status);
-    neighbor_kernel<<<static_cast<unsigned>((n + kMapVox - 1) / kMapVox), 27 * kMapVox, 0, st>>>(
-        c4, static_cast<int>(n), t, cap - 1, nbr);
+    const int ni = static_cast<int>(n);
+    table_clear_kernel<<<stride_grid(static_cast<int64_t>(cap), 256), 256, 0, st>>>(t, cap, nullptr, 0);
+    insert_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, ni, t, cap - 1, status, nullptr, 0);
+    neighbor_kernel<<<stride_grid(n, kMapVox), 27 * kMapVox, 0, st>>>(c4, ni, t, cap - 1, nbr, nullptr, 0);
     return cudaGetLastError();
 }
 
 cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
                               float* inv_count, int32_t* up_rows, void* ws, uint32_t* status, cudaStream_t st) {
-    if (n == 0) {
-        return cudaMemsetAsync(np_dev, 0, sizeof(int32_t), st);
-    }
-    const uint64_t cap = table_capacity(n);
-    char* p = static_cast<char*>(ws);
-    Slot* tf = reinterpret_cast<Slot*>(p);
-    Slot* tp = tf + cap;
-    p += align_up(2 * cap * sizeof(Slot), 256);
-    int* excl = reinterpret_cast<int*>(p);
-    p += align_up(static_cast<size_t>(n + 1) * 4, 256);
-    int* bsum = reinterpret_cast<int*>(p);
+    if (n == 0) return cudaMemsetAsync(np_dev, 0, sizeof(int32_t), st);
+    const TopoWs w = carve(ws, n);
+    Slot* tf = w.t;
+    Slot* tp = w.t + w.cap;
     const int nblk = static_cast<int>((n + kScanBlock - 1) / kScanBlock);
     const auto* c4 = reinterpret_cast<const int4*>(coords);
     const int ni = static_cast<int>(n);
-    const unsigned g = static_cast<unsigned>((n + 255) / 256);
-    table_clear_kernel<<<static_cast<unsigned>((2 * cap + 255) / 256), 256, 0, st>>>(tf, 2 * cap);
-    insert_kernel<<<g, 256, 0, st>>>(c4, ni, tf, cap - 1, status);
-    parent_insert_kernel<<<g, 256, 0, st>>>(c4, ni, tp, cap - 1, status);
-    first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, tp, cap - 1, excl, bsum);
-    block_scan_kernel<<<1, kScanBlock, 0, st>>>(bsum, nblk, np_dev);
-    assign_kernel<<<g, 256, 0, st>>>(c4, ni, tp, cap - 1, excl, bsum, reinterpret_cast<int4*>(parent), up_rows);
-    pool_fill_kernel<<<592, 256, 0, st>>>(pool_rows, np_dev, ni);
-    slot_kernel<<<g, 256, 0, st>>>(c4, ni, tf, cap - 1, up_rows, np_dev, pool_rows, inv_count, status);
+    auto* par = reinterpret_cast<int4*>(parent);
+    cudaError_t e = launch_brick_build(c4, ni, w, status, st);
+    if (e != cudaSuccess) return e;
+    // per-voxel tables only when the bricks overflowed (gated kernels)
+    table_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.t, 2 * w.cap, w.ctr, w.budget);
+    insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tf, w.cap - 1, status, w.ctr, w.budget);
+    parent_insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tp, w.cap - 1, status, w.ctr, w.budget);
+    // first children: flags + per-block scan (one of the two runs)
+    brick_first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, w.first,
+                                                         w.excl, w.bsum);
+    first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, tp, w.cap - 1, w.excl, w.bsum, w.ctr, w.budget);
+    block_scan_kernel<<<1, kScanBlock, 0, st>>>(w.bsum, nblk, np_dev);
+    pool_fill_kernel<<<kStrideGrid, 256, 0, st>>>(pool_rows, np_dev, ni);
+    brick_assign_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, w.first,
+                                                             w.excl, w.bsum, np_dev, par, up_rows, pool_rows,
+                                                             inv_count, status);
+    assign_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tp, w.cap - 1, w.excl, w.bsum, par, up_rows, w.ctr, w.budget);
+    slot_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tf, w.cap - 1, up_rows, np_dev, pool_rows, inv_count, status,
+                                             w.ctr, w.budget);
     return cudaGetLastError();
 }
 
