@@ -365,69 +365,72 @@ __global__ void brick_fill_kernel(const int4* __restrict__ coords, int n, const 
     }
 }
 
-// Neighbour map over the brick records.  Per group of 32 consecutive voxels:
-//   1. 8 x 32 threads look up, per voxel, the bricks its taps can reach:
-//      offset bits (ox, oy, oz); on an axis with the bit set the neighbour
-//      brick is the one below when the voxel sits on the brick's low face
-//      (cell coordinate 0), above on the high face (3), none otherwise;
-//   2. 27 x 32 threads: tap t of voxel v reads the record entry of its
-//      neighbour cell in the brick looked up in step 1;
-//   3. the [32][27] results leave as one contiguous run.
-__global__ void __launch_bounds__(27 * kMapVox) brick_neighbor_kernel(const int4* __restrict__ coords, int n,
-                                                                      const Slot* __restrict__ t, uint64_t mask,
-                                                                      const int* __restrict__ rec,
-                                                                      const int* __restrict__ ctr, int budget,
-                                                                      int* __restrict__ nbr) {
+// Neighbour map over the brick records, one thread per voxel (256 voxels
+// per block, several blocks per SM, so thousands of independent lookups are
+// in flight): the thread looks up the bricks its taps can reach (offset bits
+// (ox, oy, oz): on an axis with the bit set the neighbour brick is the one
+// below when the voxel sits on its brick's low face (cell coordinate 0),
+// above on the high face (3), none otherwise) into shared memory, then
+// reads one record entry per tap; the block's [256][27] rows are staged in
+// shared memory (row stride 27 words: conflict-free) and leave as one
+// contiguous run.
+constexpr int kNbrThreads = 256;
+
+__global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4* __restrict__ coords, int n,
+                                                                     const Slot* __restrict__ t, uint64_t mask,
+                                                                     const int* __restrict__ rec,
+                                                                     const int* __restrict__ ctr, int budget,
+                                                                     int* __restrict__ nbr) {
     if (*ctr > budget) return;
-    __shared__ int4 sc[kMapVox];
-    __shared__ int sb[kMapVox * 8];
-    __shared__ int sn[kMapVox * 27];
+    __shared__ int sn[kNbrThreads * 27];
+    __shared__ int sb[8 * kNbrThreads];
     const int tid = threadIdx.x;
-    const int v = tid % kMapVox;
-    const int tap = tid / kMapVox;
-    const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kMapVox; base < n;
-         base += static_cast<int64_t>(gridDim.x) * kMapVox) {
-        if (tid < kMapVox && base + tid < n) sc[tid] = __ldg(coords + base + tid);
-        __syncthreads();
-        if (tid < 8 * kMapVox) {
-            const int o = tid / kMapVox;  // offset bits
-            int id = -1;
-            if (base + v < n) {
-                const int4 c = sc[v];
-                if (coord_ok(c)) {
-                    const int lx = c.x & 3, ly = c.y & 3, lz = c.z & 3;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kNbrThreads; base < n;
+         base += static_cast<int64_t>(gridDim.x) * kNbrThreads) {
+        const int64_t i = base + tid;
+        int* row = sn + tid * 27;
+        if (i < n) {
+            const int4 c = __ldg(coords + i);
+            if (!coord_ok(c)) {
+#pragma unroll
+                for (int tap = 0; tap < 27; ++tap) row[tap] = n;
+            } else {
+                const int lx = c.x & 3, ly = c.y & 3, lz = c.z & 3;
+                const int bx = c.x >> 2, by = c.y >> 2, bz = c.z >> 2;
+                constexpr int kBrickMax = kAxisMax >> 2;
+#pragma unroll
+                for (int o = 0; o < 8; ++o) {
                     const int ox = (o & 1) ? (lx == 0 ? -1 : (lx == 3 ? 1 : 2)) : 0;
                     const int oy = (o & 2) ? (ly == 0 ? -1 : (ly == 3 ? 1 : 2)) : 0;
                     const int oz = (o & 4) ? (lz == 0 ? -1 : (lz == 3 ? 1 : 2)) : 0;
-                    const int bx = (c.x >> 2) + ox, by = (c.y >> 2) + oy, bz = (c.z >> 2) + oz;
-                    if (ox != 2 && oy != 2 && oz != 2 && bx >= 0 && by >= 0 && bz >= 0 && bx <= (kAxisMax >> 2) &&
-                        by <= (kAxisMax >> 2) && bz <= (kAxisMax >> 2))
-                        id = table_find(t, mask, brick_key(bx, by, bz, c.w));
+                    const int qx = bx + ox, qy = by + oy, qz = bz + oz;
+                    int id = -1;
+                    if (ox != 2 && oy != 2 && oz != 2 && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kBrickMax &&
+                        qy <= kBrickMax && qz <= kBrickMax)
+                        id = table_find(t, mask, brick_key(qx, qy, qz, c.w));
+                    sb[o * kNbrThreads + tid] = id;
+                }
+#pragma unroll
+                for (int tap = 0; tap < 27; ++tap) {
+                    const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+                    const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
+                    int found = n;
+                    if (qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
+                        const int o = ((qx >> 2) != bx) | (((qy >> 2) != by) << 1) | (((qz >> 2) != bz) << 2);
+                        const int id = sb[o * kNbrThreads + tid];
+                        if (id >= 0) {
+                            const int j = __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz));
+                            if (j != kNoVoxel) found = j;
+                        }
+                    }
+                    row[tap] = found;
                 }
             }
-            sb[v * 8 + o] = id;
         }
         __syncthreads();
-        if (base + v < n) {
-            const int4 c = sc[v];
-            const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
-            int found = n;
-            if (coord_ok(c) && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
-                const int o = ((qx >> 2) != (c.x >> 2)) | (((qy >> 2) != (c.y >> 2)) << 1) |
-                              (((qz >> 2) != (c.z >> 2)) << 2);
-                const int id = sb[v * 8 + o];
-                if (id >= 0) {
-                    const int j = __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz));
-                    if (j != kNoVoxel) found = j;
-                }
-            }
-            sn[v * 27 + tap] = found;
-        }
-        __syncthreads();
-        const int64_t count = (n - base < kMapVox ? n - base : kMapVox) * 27;
+        const int64_t count = (n - base < kNbrThreads ? n - base : kNbrThreads) * 27;
         int* out = nbr + base * 27;
-        for (int k = tid; k < count; k += blockDim.x) out[k] = sn[k];
+        for (int64_t k = tid; k < count; k += kNbrThreads) out[k] = sn[k];
         __syncthreads();
     }
 }
@@ -591,8 +594,8 @@ cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, vo
     const int ni = static_cast<int>(n);
     cudaError_t e = launch_brick_build(c4, ni, w, status, st);
     if (e != cudaSuccess) return e;
-    brick_neighbor_kernel<<<stride_grid(n, kMapVox), 27 * kMapVox, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr,
-                                                                            w.budget, nbr);
+    brick_neighbor_kernel<<<stride_grid(n, kNbrThreads), kNbrThreads, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr,
+                                                                               w.budget, nbr);
     // too many bricks: the per-voxel hash (these return at once otherwise)
     table_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.t, w.cap, w.ctr, w.budget);
     insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, w.t, w.cap - 1, status, w.ctr, w.budget);
