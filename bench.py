@@ -69,11 +69,13 @@ WORKLOADS = {
     "unet_c64": dict(kind="unet", coords="unet_coords", grid=256),
     "refine_640x480": dict(kind="refine", width=640, height=480, grid=None),
 }
-# DRAM bytes per voxel of one sparse-conv launch, by residual-block kind:
-# dram__bytes_read.sum + dram__bytes_write.sum from ncu captures of a block's
-# two convs (profiles/conv_traffic_*.md), averaged; scaled by the voxels a
-# launch processes.
-CONV_DRAM_BYTES_PER_VOXEL = {"gn": 860.0, "ln": 646.0}
+# DRAM bytes per voxel of one sparse-conv launch, by workload and residual-
+# block kind: dram__bytes_read.sum + dram__bytes_write.sum from ncu captures
+# of a block's two convs on that workload (profiles/conv_traffic_*.md),
+# averaged; scaled by the voxels a launch processes.  shell_4m's gathers miss
+# L2 more than res4_c128's (its tap-ordered tiles spread over a 450 MB
+# operand), so each workload uses its own capture.
+CONV_DRAM_BYTES_PER_VOXEL = {("shell_4m", "ln"): 1296.0, ("res4_c128", "gn"): 860.0, ("res4_c128", "ln"): 646.0}
 # Compulsory bytes per voxel of one Q8_0 conv launch at C = 128 (each input
 # row read once): activation codes + block scales (128 + 16), the plan's
 # tile row and neighbour list (4 + 108), the output (fused Q8_0 codes + scales
@@ -418,6 +420,8 @@ def run_ours(args):
     ex = SparseCudaExecutor(local)
     dev = torch.device("cuda", local)
     coords = getattr(synth, w["coords"])() if "coords" in w else np.zeros((w["width"] * w["height"], 4), np.int32)
+    if args.voxels and "coords" in w:
+        coords = np.ascontiguousarray(coords[:args.voxels])   # a z-slab: (b, z, y, x) order
     n = coords.shape[0]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
@@ -761,8 +765,10 @@ def build_stack(args, w, ex, dev, coords, rank, world):
             achieved, peak, unit = (flops / t / 1e12 if launches else None), i8, "TOP/s"
         return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                 "frac": (achieved / peak) if achieved else None,
-                "traffic": CONV_DRAM_BYTES_PER_VOXEL[args.block] * nl,
-                "traffic_unit": "DRAM bytes per conv launch (ncu capture, per voxel, scaled by the launch's voxels)",
+                "traffic": (CONV_DRAM_BYTES_PER_VOXEL[(args.workload, args.block)] * nl
+                            if (args.workload, args.block) in CONV_DRAM_BYTES_PER_VOXEL else None),
+                "traffic_unit": "DRAM bytes per conv launch (ncu capture on this workload, per voxel, "
+                                "scaled by the launch's voxels)",
                 "kernel": "conv_tc (Q8_0 x Q8_0, kind::i8, C=128)",
                 "peak_source": f"{peak_src} HBM copy bandwidth; int8 peak measured in this run (cuBLAS int8 GEMM)",
                 "algorithmic_bytes_per_launch": alg, "flops_per_launch": flops,
@@ -1054,6 +1060,8 @@ def main():
     ap.add_argument("--conv", default="ordered", choices=["ordered", "direct"])
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU halo exchange: fused peer stores (default) or NCCL send/recv per block")
+    ap.add_argument("--voxels", type=int, default=0,
+                    help="run on the first N voxels of the workload (a z-slab), for small profiling captures")
     ap.add_argument("--block", default=None, choices=["ln", "gn"],
                     help="residual block (default: the one the workload is quoted on)")
     args = ap.parse_args()

@@ -174,15 +174,16 @@ def _rank_main_peer(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
-def test_two_gpu_peer_halo_matches_single_gpu_stack(tmp_path, ex):
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_halo_matches_single_gpu_stack(tmp_path, ex, world):
     """The fused-exchange path (msc_slab_*): halo rows written by each
-    block's second conv into the neighbour's buffer over NVLink.  The owned
-    rows of both ranks equal the single-GPU stack bit for bit."""
+    block's second conv into the neighbours' buffers over NVLink.  The owned
+    rows of every rank equal the single-GPU stack bit for bit.  With four
+    ranks the two inner ones exchange with both neighbours."""
     import multiprocessing as mp
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     port = _free_port()
     outs = [str(tmp_path / f"peer{r}.npy") for r in range(world)]
