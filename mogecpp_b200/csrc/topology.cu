@@ -322,16 +322,18 @@ __device__ __forceinline__ unsigned long long brick_key(int bx, int by, int bz, 
 __device__ __forceinline__ int brick_cell(int x, int y, int z) { return (x & 3) | ((y & 3) << 2) | ((z & 3) << 4); }
 
 // ctr[0] = bricks numbered so far (forced above the budget when the table
-// runs out, which selects the per-voxel hash)
+// runs out, which selects the per-voxel hash).  Neighbouring voxels of the
+// (b, z, y, x) order share bricks, so the lanes of a warp that hold the same
+// brick key elect one lane to insert it: fewer atomics on the same slot.
 __global__ void brick_insert_kernel(const int4* __restrict__ coords, int n, Slot* __restrict__ t, uint64_t mask,
                                     int* __restrict__ ctr, int budget, uint32_t* status) {
     for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
         const int4 c = __ldg(coords + u);
-        if (!coord_ok(c)) {
-            set_status(status, MSC_DEV_BAD_COORD);
-            continue;
-        }
-        const unsigned long long key = brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w);
+        const bool ok = coord_ok(c);
+        if (!ok) set_status(status, MSC_DEV_BAD_COORD);
+        const unsigned long long key = ok ? brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w) : kEmpty;
+        const unsigned peers = __match_any_sync(__activemask(), key);
+        if (!ok || static_cast<int>(threadIdx.x & 31) != __ffs(peers) - 1) continue;
         uint64_t h = mix64(key) & mask;
         bool done = false;
         for (uint64_t probe = 0; probe <= mask && !done; ++probe) {
@@ -356,24 +358,31 @@ __global__ void brick_fill_kernel(const int4* __restrict__ coords, int n, const 
     if (*ctr > budget) return;
     for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
         const int4 c = __ldg(coords + u);
-        if (!coord_ok(c)) continue;
-        const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
-        if (id < 0) continue;  // cannot happen: every voxel's brick was inserted
+        const bool ok = coord_ok(c);
+        const unsigned long long key = ok ? brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w) : kEmpty;
+        // one table lookup per brick key among the warp's lanes
+        const unsigned peers = __match_any_sync(__activemask(), key);
+        const int leader = __ffs(peers) - 1;
+        int id = -1;
+        if (ok && static_cast<int>(threadIdx.x & 31) == leader) id = table_find(t, mask, key);
+        id = __shfl_sync(peers, id, leader);
+        if (!ok || id < 0) continue;  // id < 0 cannot happen: every voxel's brick was inserted
         const int old = atomicMin(&rec[static_cast<int64_t>(id) * kBrickVox + brick_cell(c.x, c.y, c.z)],
                                   static_cast<int>(u));
         if (old != kNoVoxel) set_status(status, MSC_DEV_DUP_COORD);
     }
 }
 
-// Neighbour map over the brick records, one thread per voxel (256 voxels
-// per block, several blocks per SM, so thousands of independent lookups are
-// in flight): the thread looks up the bricks its taps can reach (offset bits
-// (ox, oy, oz): on an axis with the bit set the neighbour brick is the one
-// below when the voxel sits on its brick's low face (cell coordinate 0),
-// above on the high face (3), none otherwise) into shared memory, then
-// reads one record entry per tap; the block's [256][27] rows are staged in
-// shared memory (row stride 27 words: conflict-free) and leave as one
-// contiguous run.
+// Neighbour map over the brick records, one thread per voxel and one block
+// per 256 voxels (no grid-stride loop: shared memory holds 6 blocks per SM,
+// and a fixed grid-stride grid left a second, partial wave of blocks): the
+// thread looks up the bricks its taps can reach (offset bits (ox, oy, oz):
+// on an axis with the bit set the neighbour brick is the one below when the
+// voxel sits on its brick's low face (cell coordinate 0), above on the high
+// face (3), none otherwise) into shared memory, then issues its 27 record
+// reads before using any of them (27 independent loads in flight per
+// thread); the block's [256][27] rows are staged in shared memory (row
+// stride 27 words: conflict-free) and leave as one contiguous run.
 constexpr int kNbrThreads = 256;
 
 __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4* __restrict__ coords, int n,
@@ -385,54 +394,51 @@ __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4*
     __shared__ int sn[kNbrThreads * 27];
     __shared__ int sb[8 * kNbrThreads];
     const int tid = threadIdx.x;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kNbrThreads; base < n;
-         base += static_cast<int64_t>(gridDim.x) * kNbrThreads) {
-        const int64_t i = base + tid;
-        int* row = sn + tid * 27;
-        if (i < n) {
-            const int4 c = __ldg(coords + i);
-            if (!coord_ok(c)) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kNbrThreads;
+    const int64_t i = base + tid;
+    int* row = sn + tid * 27;
+    if (i < n) {
+        const int4 c = __ldg(coords + i);
+        if (!coord_ok(c)) {
 #pragma unroll
-                for (int tap = 0; tap < 27; ++tap) row[tap] = n;
-            } else {
-                const int lx = c.x & 3, ly = c.y & 3, lz = c.z & 3;
-                const int bx = c.x >> 2, by = c.y >> 2, bz = c.z >> 2;
-                constexpr int kBrickMax = kAxisMax >> 2;
+            for (int tap = 0; tap < 27; ++tap) row[tap] = n;
+        } else {
+            const int lx = c.x & 3, ly = c.y & 3, lz = c.z & 3;
+            const int bx = c.x >> 2, by = c.y >> 2, bz = c.z >> 2;
+            constexpr int kBrickMax = kAxisMax >> 2;
 #pragma unroll
-                for (int o = 0; o < 8; ++o) {
-                    const int ox = (o & 1) ? (lx == 0 ? -1 : (lx == 3 ? 1 : 2)) : 0;
-                    const int oy = (o & 2) ? (ly == 0 ? -1 : (ly == 3 ? 1 : 2)) : 0;
-                    const int oz = (o & 4) ? (lz == 0 ? -1 : (lz == 3 ? 1 : 2)) : 0;
-                    const int qx = bx + ox, qy = by + oy, qz = bz + oz;
-                    int id = -1;
-                    if (ox != 2 && oy != 2 && oz != 2 && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kBrickMax &&
-                        qy <= kBrickMax && qz <= kBrickMax)
-                        id = table_find(t, mask, brick_key(qx, qy, qz, c.w));
-                    sb[o * kNbrThreads + tid] = id;
-                }
-#pragma unroll
-                for (int tap = 0; tap < 27; ++tap) {
-                    const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-                    const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
-                    int found = n;
-                    if (qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
-                        const int o = ((qx >> 2) != bx) | (((qy >> 2) != by) << 1) | (((qz >> 2) != bz) << 2);
-                        const int id = sb[o * kNbrThreads + tid];
-                        if (id >= 0) {
-                            const int j = __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz));
-                            if (j != kNoVoxel) found = j;
-                        }
-                    }
-                    row[tap] = found;
-                }
+            for (int o = 0; o < 8; ++o) {
+                const int ox = (o & 1) ? (lx == 0 ? -1 : (lx == 3 ? 1 : 2)) : 0;
+                const int oy = (o & 2) ? (ly == 0 ? -1 : (ly == 3 ? 1 : 2)) : 0;
+                const int oz = (o & 4) ? (lz == 0 ? -1 : (lz == 3 ? 1 : 2)) : 0;
+                const int qx = bx + ox, qy = by + oy, qz = bz + oz;
+                int id = -1;
+                if (ox != 2 && oy != 2 && oz != 2 && qx >= 0 && qy >= 0 && qz >= 0 && qx <= kBrickMax &&
+                    qy <= kBrickMax && qz <= kBrickMax)
+                    id = table_find(t, mask, brick_key(qx, qy, qz, c.w));
+                sb[o * kNbrThreads + tid] = id;
             }
+            int v[27];
+#pragma unroll
+            for (int tap = 0; tap < 27; ++tap) {
+                const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+                const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
+                int id = -1;
+                if (qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
+                    const int o = ((qx >> 2) != bx) | (((qy >> 2) != by) << 1) | (((qz >> 2) != bz) << 2);
+                    id = sb[o * kNbrThreads + tid];
+                }
+                v[tap] = id >= 0 ? __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz))
+                                 : kNoVoxel;
+            }
+#pragma unroll
+            for (int tap = 0; tap < 27; ++tap) row[tap] = v[tap] != kNoVoxel ? v[tap] : n;
         }
-        __syncthreads();
-        const int64_t count = (n - base < kNbrThreads ? n - base : kNbrThreads) * 27;
-        int* out = nbr + base * 27;
-        for (int64_t k = tid; k < count; k += kNbrThreads) out[k] = sn[k];
-        __syncthreads();
     }
+    __syncthreads();
+    const int64_t count = (n - base < kNbrThreads ? n - base : kNbrThreads) * 27;
+    int* out = nbr + base * 27;
+    for (int64_t k = tid; k < count; k += kNbrThreads) out[k] = sn[k];
 }
 
 // The 8 record entries of voxel c's stride-2 cell (the 2 x 2 x 2 block of
@@ -594,8 +600,8 @@ cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, vo
     const int ni = static_cast<int>(n);
     cudaError_t e = launch_brick_build(c4, ni, w, status, st);
     if (e != cudaSuccess) return e;
-    brick_neighbor_kernel<<<stride_grid(n, kNbrThreads), kNbrThreads, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr,
-                                                                               w.budget, nbr);
+    brick_neighbor_kernel<<<static_cast<unsigned>((n + kNbrThreads - 1) / kNbrThreads), kNbrThreads, 0, st>>>(
+        c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, nbr);
     // too many bricks: the per-voxel hash (these return at once otherwise)
     table_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.t, w.cap, w.ctr, w.budget);
     insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, w.t, w.cap - 1, status, w.ctr, w.budget);
