@@ -84,6 +84,12 @@ CONV_ALG_BYTES_PER_VOXEL = {"ln": ((144 + 112 + 144) + (144 + 112 + 256 + 256)) 
                             "gn": ((144 + 112 + 512) + (144 + 112 + 256 + 256)) / 2.0}
 Q8_WEIGHT_BYTES = 27 * 128 * 128 + 27 * 4 * 128 * 4   # int8 codes + fp32 block scales per conv
 PLAN_SORT_KERNELS = 6  # cub radix sort of 27-bit keys: histogram, scan, 4 digit passes
+# kernels per topology call: the voxel table (table clear, brick insert,
+# record clear, record fill), the neighbour map (brick kernel + the three
+# per-voxel fallback kernels, which return at once unless the bricks
+# overflow), the stride-2 maps (brick first-child scan, block scan, pool
+# fill, brick assign + six fallback kernels)
+TOPO_KERNELS = {"make_level": 8, "downsample": 14, "make_level_downsample": 18}
 
 
 def load_peaks():
@@ -630,7 +636,7 @@ def build_refine(args, w, ex, dev):
                 "flops_note": "dense-equivalent 2*C*C*27*N per conv (the tap-skipping kernel does less)"}
 
     def launches(prof):
-        per = {"make_level": 3, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "downsample": 8}
+        per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1}
         # + per pass: z quantisation (3), level-0 map, input rows, input_proj,
         # encoder rows, fuse_proj.0, SiLU, out_proj, log z update, key compare
         return sum(per.get(k, 1) * v[0] for k, v in prof.items()) + 12 * args.steps
@@ -781,10 +787,10 @@ def build_stack(args, w, ex, dev, coords, rank, world):
         return 2.0 * c * c * state["e_pairs"] / (ms / max(launches, 1) * 1e-3) / 1e12 if launches else None
 
     def launches(prof):
-        # kernels per profiled family call: make_level = clear + insert +
-        # neighbour; plan_build = header + mask keys + the radix sort's kernels
-        # + tile lists; gn_stats/finalize/act_prepare/conv_tc = 1
-        per = {"make_level": 3, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "halo": 0,
+        # kernels per profiled family call: topology as TOPO_KERNELS;
+        # plan_build = header + mask keys + the radix sort's kernels + tile
+        # lists; gn_stats/finalize/act_prepare/conv_tc = 1
+        per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "halo": 0,
                "halo_wait": 2 if peer else 1}  # wait + signal kernels per block
         return sum(per.get(k, 1) * v[0] for k, v in prof.items())
 
@@ -902,8 +908,7 @@ def build_other(args, w, ex, dev, coords):
 
     if w["kind"] == "topo":
         def step(coords_t=coords_d):
-            state["nbr"] = ex.make_level(coords_t)
-            state["tr"] = ex.downsample(coords_t, sync=False)
+            state["nbr"], state["tr"] = ex.make_level_downsample(coords_t, sync=False)
 
         out_dev = lambda bi: state["nbr"]
         h_out_shape, h_out_dtype = (n, 27), torch.int32
@@ -912,33 +917,29 @@ def build_other(args, w, ex, dev, coords):
         units = n
 
         def roofline(prof):
-            # compulsory bytes per call: make_level reads the coords (16 B
-            # rows), clears and fills the table (16-byte slots, capacity cap),
-            # reads the coords again to probe and writes the map (108 B per
-            # voxel); downsample reads the coords and writes the parents
-            # (16 B), pool_rows (8 x 4 B per parent), inv_count and up_rows
-            cap = 64
-            while cap < 2 * n:
-                cap <<= 1
+            # compulsory bytes of one level's topology: read the coords once
+            # (16 B rows), write the neighbour map (108 B per voxel), the
+            # parents (16 B), pool_rows (8 x 4 B per parent), inv_count (4 B
+            # per parent) and up_rows (4 B per voxel); tables and records are
+            # scratch that an L2-resident design need not send to HBM
             np_ = int(state["tr"].np_dev.item())
-            alg = {"make_level": 16 * n + 16 * cap + 16 * n + 108 * n,
-                   "downsample": 16 * n + 16 * np_ + 4 * (8 * np_ + n + np_)}
-            per = {k: prof[k][1] / prof[k][0] * 1e-3 for k in alg if prof.get(k, (0, 0.0))[0]}
-            if not per:
+            fam = "make_level_downsample"
+            alg = 16 * n + 108 * n + 16 * np_ + 4 * (8 * np_ + np_) + 4 * n
+            launches, ms = prof.get(fam, (0, 0.0))
+            if not launches:
                 return {"bound": "hbm", "achieved": None, "peak": peak_hbm, "unit": "GB/s", "frac": None,
                         "traffic": None}
-            fam = max(per, key=per.get)
-            ach = alg[fam] / per[fam] / 1e9
+            t = ms / launches * 1e-3
+            ach = alg / t / 1e9
             return {"bound": "hbm", "achieved": ach, "peak": peak_hbm, "unit": "GB/s", "frac": ach / peak_hbm,
-                    "traffic": None, "kernel": f"{fam} family (dominant)", "peak_source": peak_src,
-                    "algorithmic_bytes_per_launch": alg, "parents": np_,
-                    "ms_per_launch": {k: v * 1e3 for k, v in per.items()},
-                    "gbs_per_family": {k: alg[k] / v / 1e9 for k, v in per.items()},
-                    "topology_gbs": sum(alg.values()) / sum(per.values()) / 1e9}
+                    "traffic": None, "kernel": f"{fam} (brick table, neighbour map, stride-2 maps)",
+                    "peak_source": peak_src, "algorithmic_bytes_per_launch": alg, "parents": np_,
+                    "ms_per_launch": t * 1e3}
 
         dtype = "int32 coords, 64-bit packed keys"
-        cfg = {"step": "make_level (hash + 27-tap map) + downsample (stride-2 maps)", "parents": None}
-        launches_per = {"make_level": 3, "downsample": 8}
+        cfg = {"step": "make_level + downsample in one call (voxel table, 27-tap map, stride-2 maps)",
+               "parents": None}
+        launches_per = dict(TOPO_KERNELS)
     elif w["kind"] == "conv":
         pw = ex.prepare_weight(torch.from_numpy(extra["w"]).to(dev), "f32", 64, 64, 27)
         x_d = torch.from_numpy(extra["x"]).to(dev)
@@ -961,7 +962,7 @@ def build_other(args, w, ex, dev, coords):
 
         dtype = "fp32 (exact hi/lo fp16 split on tcgen05 kind::f16, fp32 accumulation)"
         cfg = {"step": "make_level + tap-order plan + 1 sparse conv", "channels": 64}
-        launches_per = {"make_level": 3, "plan_build": 2 + PLAN_SORT_KERNELS + 1}
+        launches_per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1}
     else:  # unet
         p = extra["p"]
         P = lambda k, ci, co, t: ex.prepare_weight(torch.from_numpy(p[k]).to(dev), "f32", ci, co, t)
@@ -971,8 +972,7 @@ def build_other(args, w, ex, dev, coords):
         n_coarse = tr0.np
 
         def step(coords_t=coords_d, x_t=x_d):
-            nbr = ex.make_level(coords_t)
-            tr = ex.downsample(coords_t)
+            nbr, tr = ex.make_level_downsample(coords_t)
             nbr_c = ex.make_level(tr.parent.contiguous())
             state["nbr"] = nbr
             h0 = ex.sparse_conv(x_t, nbr, pw0, None, out_dtype=torch.bfloat16)
@@ -993,7 +993,7 @@ def build_other(args, w, ex, dev, coords):
         dtype = "bf16 activations, fp32 weights (exact hi/lo fp16 split on tcgen05 kind::f16)"
         cfg = {"step": "make_level x2 + downsample + conv 64 + pool/linear 64->128 + conv 128 + linear/up + skip",
                "samples": 2, "coarse_voxels": int(n_coarse)}
-        launches_per = {"make_level": 3, "downsample": 8}
+        launches_per = dict(TOPO_KERNELS)
 
     def e2e_buffers():
         h_out = [torch.empty(h_out_shape, dtype=h_out_dtype).pin_memory() for _ in range(2)]

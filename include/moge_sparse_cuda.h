@@ -127,6 +127,16 @@ int msc_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* par
                    int32_t* pool_rows, float* inv_count, int32_t* up_rows, int64_t* np_host, void* ws,
                    size_t ws_bytes, void* stream);
 
+/* msc_make_level and msc_downsample of the same voxels in one call (the
+ * neighbour map and the stride-2 maps of one pyramid level): the voxel
+ * table is built once instead of twice.  Same arguments and results as the
+ * two calls; the workspace is msc_topology_workspace_bytes(n).
+ * Replaces: make_level + downsample of one level (src/sparse.cpp:238-272,
+ * 312-357) as build_topology_from_key (src/sparse.cpp:408-431) calls them. */
+int msc_make_level_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr, int32_t* parent,
+                              int32_t* np_dev, int32_t* pool_rows, float* inv_count, int32_t* up_rows,
+                              int64_t* np_host, void* ws, size_t ws_bytes, void* stream);
+
 /* Log-depth voxel bins of an image: for every pixel i (factor_coord [n][3]
  * floats: x/z, y/z, log z), q = nearbyint(double(log z * depth_resolution))
  * (float product, round half to even), zbin[i] = q - min(q).  Syncs; fails

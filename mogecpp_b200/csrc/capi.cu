@@ -358,6 +358,28 @@ int msc_make_level(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr
     });
 }
 
+namespace {
+// With np_host: sync, store the parent count and report device failures of
+// the stride-2 numbering (duplicate coordinates) by the return code.
+void read_parent_count(msc_ctx_t ctx, const int32_t* np_dev, int64_t* np_host, cudaStream_t st) {
+    if (!np_host) return;
+    int32_t h = 0;
+    cuda_ok(cudaMemcpyAsync(&h, np_dev, sizeof(h), cudaMemcpyDeviceToHost, st), "np read");
+    uint32_t bits = 0;
+    cuda_ok(cudaMemcpyAsync(&bits, ctx->status, sizeof(bits), cudaMemcpyDeviceToHost, st), "status read");
+    cuda_ok(cudaStreamSynchronize(st), "stream sync");
+    *np_host = h;
+    if (bits & MSC_DEV_DUP_COORD) {
+        cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), st), "status clear");
+        fail(MSC_E_DEVICE, "duplicate voxel coordinates: stride-2 slot numbering needs unique voxels");
+    }
+    if (bits & ~MSC_DEV_DUP_COORD) {
+        cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), st), "status clear");
+        fail(MSC_E_DEVICE, "device failure in downsample (status bits " + std::to_string(bits) + ")");
+    }
+}
+}  // namespace
+
 int msc_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev,
                    int32_t* pool_rows, float* inv_count, int32_t* up_rows, int64_t* np_host, void* ws,
                    size_t ws_bytes, void* stream) {
@@ -378,22 +400,31 @@ int msc_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* par
                                            S(stream)),
                     "downsample launch");
         }
-        if (np_host) {
-            int32_t h = 0;
-            cuda_ok(cudaMemcpyAsync(&h, np_dev, sizeof(h), cudaMemcpyDeviceToHost, S(stream)), "np read");
-            uint32_t bits = 0;
-            cuda_ok(cudaMemcpyAsync(&bits, ctx->status, sizeof(bits), cudaMemcpyDeviceToHost, S(stream)), "status read");
-            cuda_ok(cudaStreamSynchronize(S(stream)), "stream sync");
-            *np_host = h;
-            if (bits & MSC_DEV_DUP_COORD) {
-                cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), S(stream)), "status clear");
-                fail(MSC_E_DEVICE, "duplicate voxel coordinates: stride-2 slot numbering needs unique voxels");
-            }
-            if (bits & ~MSC_DEV_DUP_COORD) {
-                cuda_ok(cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), S(stream)), "status clear");
-                fail(MSC_E_DEVICE, "device failure in downsample (status bits " + std::to_string(bits) + ")");
-            }
+        read_parent_count(ctx, np_dev, np_host, S(stream));
+    });
+}
+
+int msc_make_level_downsample(msc_ctx_t ctx, const int32_t* coords, int64_t n, int32_t* nbr, int32_t* parent,
+                              int32_t* np_dev, int32_t* pool_rows, float* inv_count, int32_t* up_rows,
+                              int64_t* np_host, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        need(np_dev != nullptr, "null np pointer");
+        if (n > 0) {
+            need(coords && nbr && parent && pool_rows && inv_count && up_rows && ws, "null pointer");
+            need_aligned(coords, 16, "coords");
+            need_aligned(parent, 16, "parent");
+            need_aligned(ws, 16, "workspace");
+            need_ws(ws_bytes, msc::topology_workspace_bytes(n));
         }
+        {
+            ProfScope ps(ctx, "make_level_downsample", S(stream));
+            cuda_ok(msc::launch_make_level_downsample(coords, n, nbr, parent, np_dev, pool_rows, inv_count, up_rows,
+                                                      ws, ctx->status, S(stream)),
+                    "make_level_downsample launch");
+        }
+        read_parent_count(ctx, np_dev, np_host, S(stream));
     });
 }
 

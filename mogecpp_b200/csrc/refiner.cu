@@ -7,7 +7,7 @@
 //                                      device, rebuild the pyramid on a miss:
 //                                      level 0 from the pixel grid
 //                                      (make_dense_image_level), coarser
-//                                      levels by msc_downsample + msc_make_level
+//                                      levels by msc_make_level_downsample
 //                                      (build_topology_from_key, :408-431),
 //                                      plus one tap-order conv plan per level
 //   upload_feature + input_proj        refiner input rows and a SIMT linear
@@ -477,35 +477,42 @@ void build_topology(msc_refiner* R, const int32_t* zbin, int w, int h, cudaStrea
     cuda(launch_dense_image_level(zbin, w, h, l0.coords.as<int32_t>(), l0.nbr.as<int32_t>(), st), "dense image level");
     for (int l = 0; l < L; ++l) {
         auto& lv = R->levels[l];
-        if (l > 0) {
-            lv.nbr.ensure(4 * 27 * (lv.n ? lv.n : 1));
-            const size_t wsb = msc_topology_workspace_bytes(lv.n);
-            R->ws.ensure(wsb);
-            ok(msc_make_level(ctx, lv.coords.as<int32_t>(), lv.n, lv.nbr.as<int32_t>(), R->ws.p, R->ws.cap, st),
-               "make_level");
-        }
-        const size_t pb = msc_conv_plan_bytes(lv.n);
-        lv.plan.ensure(pb);
-        R->ws.ensure(msc_conv_plan_workspace_bytes(lv.n));
-        ok(msc_conv_plan_build(ctx, nullptr, lv.n, lv.nbr.as<int32_t>(), MSC_PLAN_TAP_ORDER, lv.plan.p, pb, R->ws.p,
-                               R->ws.cap, st),
-           "conv plan");
-        if (l + 1 < L) {
-            auto& nx = R->levels[l + 1];
-            const int64_t n = lv.n;
-            nx.coords.ensure(16 * (n ? n : 1));
+        const int64_t n = lv.n;
+        const bool map = l > 0;          // level 0's map comes from the pixel grid
+        const bool down = l + 1 < L;     // stride-2 maps into the next level
+        if (map) lv.nbr.ensure(4 * 27 * (n ? n : 1));
+        if (down) {
+            R->levels[l + 1].coords.ensure(16 * (n ? n : 1));
             lv.pool_rows.ensure(4 * 8 * (n ? n : 1));
             lv.inv.ensure(4 * (n ? n : 1));
             lv.up_rows.ensure(4 * (n ? n : 1));
             lv.np_dev.ensure(4);
-            R->ws.ensure(msc_topology_workspace_bytes(n));
-            int64_t np = 0;
-            ok(msc_downsample(ctx, lv.coords.as<int32_t>(), n, nx.coords.as<int32_t>(), lv.np_dev.as<int32_t>(),
-                              lv.pool_rows.as<int32_t>(), lv.inv.as<float>(), lv.up_rows.as<int32_t>(), &np, R->ws.p,
-                              R->ws.cap, st),
-               "downsample");
-            nx.n = np;
         }
+        R->ws.ensure(msc_topology_workspace_bytes(n));
+        int64_t np = 0;
+        if (map && down) {
+            // one voxel table for both maps of the level
+            ok(msc_make_level_downsample(ctx, lv.coords.as<int32_t>(), n, lv.nbr.as<int32_t>(),
+                                         R->levels[l + 1].coords.as<int32_t>(), lv.np_dev.as<int32_t>(),
+                                         lv.pool_rows.as<int32_t>(), lv.inv.as<float>(), lv.up_rows.as<int32_t>(), &np,
+                                         R->ws.p, R->ws.cap, st),
+               "make_level_downsample");
+        } else if (map) {
+            ok(msc_make_level(ctx, lv.coords.as<int32_t>(), n, lv.nbr.as<int32_t>(), R->ws.p, R->ws.cap, st),
+               "make_level");
+        } else if (down) {
+            ok(msc_downsample(ctx, lv.coords.as<int32_t>(), n, R->levels[l + 1].coords.as<int32_t>(),
+                              lv.np_dev.as<int32_t>(), lv.pool_rows.as<int32_t>(), lv.inv.as<float>(),
+                              lv.up_rows.as<int32_t>(), &np, R->ws.p, R->ws.cap, st),
+               "downsample");
+        }
+        if (down) R->levels[l + 1].n = np;
+        const size_t pb = msc_conv_plan_bytes(n);
+        lv.plan.ensure(pb);
+        R->ws.ensure(msc_conv_plan_workspace_bytes(n));
+        ok(msc_conv_plan_build(ctx, nullptr, n, lv.nbr.as<int32_t>(), MSC_PLAN_TAP_ORDER, lv.plan.p, pb, R->ws.p,
+                               R->ws.cap, st),
+           "conv plan");
     }
 }
 

@@ -321,6 +321,18 @@ uint64_t brick_capacity(int64_t n) {
 __device__ __forceinline__ unsigned long long brick_key(int bx, int by, int bz, int b) { return pack_key(bx, by, bz, b); }
 __device__ __forceinline__ int brick_cell(int x, int y, int z) { return (x & 3) | ((y & 3) << 2) | ((z & 3) << 4); }
 
+// Brick-table lookup shared by the lanes of a warp that hold the same key
+// (neighbouring voxels of the (b, z, y, x) order share bricks): the first of
+// them probes, the others take its answer.  Lanes with valid = false get -1.
+__device__ __forceinline__ int warp_brick_find(const Slot* __restrict__ t, uint64_t mask, unsigned long long key,
+                                               bool valid) {
+    const unsigned peers = __match_any_sync(__activemask(), valid ? key : kEmpty);
+    const int leader = __ffs(peers) - 1;
+    int id = -1;
+    if (valid && static_cast<int>(threadIdx.x & 31) == leader) id = table_find(t, mask, key);
+    return __shfl_sync(peers, id, leader);
+}
+
 // ctr[0] = bricks numbered so far (forced above the budget when the table
 // runs out, which selects the per-voxel hash).  Neighbouring voxels of the
 // (b, z, y, x) order share bricks, so the lanes of a warp that hold the same
@@ -337,9 +349,16 @@ __global__ void brick_insert_kernel(const int4* __restrict__ coords, int n, Slot
         uint64_t h = mix64(key) & mask;
         bool done = false;
         for (uint64_t probe = 0; probe <= mask && !done; ++probe) {
-            const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
-            if (prev == kEmpty) t[h].val = atomicAdd(ctr, 1);
-            done = prev == kEmpty || prev == key;
+            // most bricks are already in the table: a plain L2 read finds
+            // them without an atomic (a stale empty read just takes the CAS)
+            const unsigned long long cur = __ldcg(&t[h].key);
+            if (cur == key) {
+                done = true;
+            } else if (cur == kEmpty) {
+                const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
+                if (prev == kEmpty) t[h].val = atomicAdd(ctr, 1);
+                done = prev == kEmpty || prev == key;
+            }
             h = (h + 1) & mask;
         }
         if (!done) atomicMax(ctr, budget + 1);
@@ -359,13 +378,7 @@ __global__ void brick_fill_kernel(const int4* __restrict__ coords, int n, const 
     for (uint64_t u = grid_index(); u < static_cast<uint64_t>(n); u += grid_stride()) {
         const int4 c = __ldg(coords + u);
         const bool ok = coord_ok(c);
-        const unsigned long long key = ok ? brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w) : kEmpty;
-        // one table lookup per brick key among the warp's lanes
-        const unsigned peers = __match_any_sync(__activemask(), key);
-        const int leader = __ffs(peers) - 1;
-        int id = -1;
-        if (ok && static_cast<int>(threadIdx.x & 31) == leader) id = table_find(t, mask, key);
-        id = __shfl_sync(peers, id, leader);
+        const int id = warp_brick_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w), ok);
         if (!ok || id < 0) continue;  // id < 0 cannot happen: every voxel's brick was inserted
         const int old = atomicMin(&rec[static_cast<int64_t>(id) * kBrickVox + brick_cell(c.x, c.y, c.z)],
                                   static_cast<int>(u));
@@ -391,7 +404,7 @@ __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4*
                                                                      const int* __restrict__ ctr, int budget,
                                                                      int* __restrict__ nbr) {
     if (*ctr > budget) return;
-    __shared__ int sn[kNbrThreads * 27];
+    __shared__ __align__(16) int sn[kNbrThreads * 27];
     __shared__ int sb[8 * kNbrThreads];
     const int tid = threadIdx.x;
     const int64_t base = static_cast<int64_t>(blockIdx.x) * kNbrThreads;
@@ -418,17 +431,23 @@ __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4*
                     id = table_find(t, mask, brick_key(qx, qy, qz, c.w));
                 sb[o * kNbrThreads + tid] = id;
             }
+            // per axis and offset d in {-1, 0, 1} (index d + 1): the brick-offset
+            // bit (set when the tap crosses into the neighbouring brick) and the
+            // cell coordinate inside the brick reached.  A tap outside the
+            // coordinate range lands in a brick that was not looked up (id -1).
+            const int ox[3] = {lx == 0 ? 1 : 0, 0, lx == 3 ? 1 : 0};
+            const int oy[3] = {ly == 0 ? 2 : 0, 0, ly == 3 ? 2 : 0};
+            const int oz[3] = {lz == 0 ? 4 : 0, 0, lz == 3 ? 4 : 0};
+            const int cx[3] = {(lx + 3) & 3, lx, (lx + 1) & 3};
+            const int cy[3] = {((ly + 3) & 3) << 2, ly << 2, ((ly + 1) & 3) << 2};
+            const int cz[3] = {((lz + 3) & 3) << 4, lz << 4, ((lz + 1) & 3) << 4};
+            const int* sbt = sb + tid;
             int v[27];
 #pragma unroll
             for (int tap = 0; tap < 27; ++tap) {
-                const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-                const int qx = c.x + dx, qy = c.y + dy, qz = c.z + dz;
-                int id = -1;
-                if (qx >= 0 && qy >= 0 && qz >= 0 && qx <= kAxisMax && qy <= kAxisMax && qz <= kAxisMax) {
-                    const int o = ((qx >> 2) != bx) | (((qy >> 2) != by) << 1) | (((qz >> 2) != bz) << 2);
-                    id = sb[o * kNbrThreads + tid];
-                }
-                v[tap] = id >= 0 ? __ldg(rec + static_cast<int64_t>(id) * kBrickVox + brick_cell(qx, qy, qz))
+                const int ix = tap / 9, iy = (tap / 3) % 3, iz = tap % 3;
+                const int id = sbt[(ox[ix] | oy[iy] | oz[iz]) * kNbrThreads];
+                v[tap] = id >= 0 ? __ldg(rec + static_cast<int64_t>(id) * kBrickVox + (cx[ix] | cy[iy] | cz[iz]))
                                  : kNoVoxel;
             }
 #pragma unroll
@@ -438,7 +457,16 @@ __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4*
     __syncthreads();
     const int64_t count = (n - base < kNbrThreads ? n - base : kNbrThreads) * 27;
     int* out = nbr + base * 27;
-    for (int64_t k = tid; k < count; k += kNbrThreads) out[k] = sn[k];
+    int64_t k0 = 0;
+    if ((reinterpret_cast<uintptr_t>(nbr) & 15) == 0) {
+        // a block's run starts 256 x 108 bytes after the previous one: 16-byte
+        // stores when the map itself is 16-byte aligned
+        const int64_t c4 = count / 4;
+        for (int64_t k = tid; k < c4; k += kNbrThreads)
+            reinterpret_cast<int4*>(out)[k] = reinterpret_cast<const int4*>(sn)[k];
+        k0 = c4 * 4;
+    }
+    for (int64_t k = k0 + tid; k < count; k += kNbrThreads) out[k] = sn[k];
 }
 
 // The 8 record entries of voxel c's stride-2 cell (the 2 x 2 x 2 block of
@@ -507,7 +535,7 @@ __global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, cons
         up_rows[i] = pid;
         if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
         const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
-        const CellInfo ci = cell_info(rec, id, c, i);
+        const CellInfo ci = id >= 0 ? cell_info(rec, id, c, i) : CellInfo{kNoVoxel, 0, 8};
         if (pid < 0 || pid >= np || ci.rank >= 8) {
             set_status(status, MSC_DEV_POOL_OVERFLOW);
             continue;
@@ -592,14 +620,13 @@ size_t topology_workspace_bytes(int64_t n) {
            align_up(static_cast<size_t>(n) * 4, 256);
 }
 
-cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, void* ws, uint32_t* status,
-                              cudaStream_t st) {
-    if (n == 0) return cudaSuccess;
-    const TopoWs w = carve(ws, n);
-    const auto* c4 = reinterpret_cast<const int4*>(coords);
+namespace {
+
+// The neighbour map from a built brick table (or the per-voxel hash when
+// the bricks overflowed).
+cudaError_t launch_map(const int4* c4, int64_t n, int32_t* nbr, const TopoWs& w, uint32_t* status,
+                       cudaStream_t st) {
     const int ni = static_cast<int>(n);
-    cudaError_t e = launch_brick_build(c4, ni, w, status, st);
-    if (e != cudaSuccess) return e;
     brick_neighbor_kernel<<<static_cast<unsigned>((n + kNbrThreads - 1) / kNbrThreads), kNbrThreads, 0, st>>>(
         c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, nbr);
     // too many bricks: the per-voxel hash (these return at once otherwise)
@@ -607,6 +634,18 @@ cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, vo
     insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, w.t, w.cap - 1, status, w.ctr, w.budget);
     neighbor_kernel<<<stride_grid(n, kMapVox), 27 * kMapVox, 0, st>>>(c4, ni, w.t, w.cap - 1, nbr, w.ctr, w.budget);
     return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, void* ws, uint32_t* status,
+                              cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const TopoWs w = carve(ws, n);
+    const auto* c4 = reinterpret_cast<const int4*>(coords);
+    cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
+    if (e != cudaSuccess) return e;
+    return launch_map(c4, n, nbr, w, status, st);
 }
 
 size_t topology_table_bytes(int64_t n) { return table_capacity(n) * sizeof(Slot); }
@@ -625,18 +664,16 @@ cudaError_t launch_make_level_in_table(const int32_t* coords, int64_t n, int32_t
     return cudaGetLastError();
 }
 
-cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
-                              float* inv_count, int32_t* up_rows, void* ws, uint32_t* status, cudaStream_t st) {
-    if (n == 0) return cudaMemsetAsync(np_dev, 0, sizeof(int32_t), st);
-    const TopoWs w = carve(ws, n);
+namespace {
+
+// The stride-2 maps from a built brick table (or the per-voxel hashes).
+cudaError_t launch_stride2(const int4* c4, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
+                           float* inv_count, int32_t* up_rows, const TopoWs& w, uint32_t* status, cudaStream_t st) {
     Slot* tf = w.t;
     Slot* tp = w.t + w.cap;
     const int nblk = static_cast<int>((n + kScanBlock - 1) / kScanBlock);
-    const auto* c4 = reinterpret_cast<const int4*>(coords);
     const int ni = static_cast<int>(n);
     auto* par = reinterpret_cast<int4*>(parent);
-    cudaError_t e = launch_brick_build(c4, ni, w, status, st);
-    if (e != cudaSuccess) return e;
     // per-voxel tables only when the bricks overflowed (gated kernels)
     table_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.t, 2 * w.cap, w.ctr, w.budget);
     insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tf, w.cap - 1, status, w.ctr, w.budget);
@@ -654,6 +691,31 @@ cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent,
     slot_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tf, w.cap - 1, up_rows, np_dev, pool_rows, inv_count, status,
                                              w.ctr, w.budget);
     return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
+                              float* inv_count, int32_t* up_rows, void* ws, uint32_t* status, cudaStream_t st) {
+    if (n == 0) return cudaMemsetAsync(np_dev, 0, sizeof(int32_t), st);
+    const TopoWs w = carve(ws, n);
+    const auto* c4 = reinterpret_cast<const int4*>(coords);
+    cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
+    if (e != cudaSuccess) return e;
+    return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st);
+}
+
+cudaError_t launch_make_level_downsample(const int32_t* coords, int64_t n, int32_t* nbr, int32_t* parent,
+                                         int32_t* np_dev, int32_t* pool_rows, float* inv_count, int32_t* up_rows,
+                                         void* ws, uint32_t* status, cudaStream_t st) {
+    if (n == 0) return cudaMemsetAsync(np_dev, 0, sizeof(int32_t), st);
+    const TopoWs w = carve(ws, n);
+    const auto* c4 = reinterpret_cast<const int4*>(coords);
+    cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
+    if (e != cudaSuccess) return e;
+    e = launch_map(c4, n, nbr, w, status, st);
+    if (e != cudaSuccess) return e;
+    return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st);
 }
 
 }  // namespace msc

@@ -25,4 +25,10 @@ cudaError_t launch_make_level_in_table(const int32_t* coords, int64_t n, int32_t
 cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
                               float* inv_count, int32_t* up_rows, void* ws, uint32_t* status, cudaStream_t st);
 
+// Both of the above for one set of voxels, the brick table built once
+// (the neighbour map and the stride-2 maps of a pyramid level).
+cudaError_t launch_make_level_downsample(const int32_t* coords, int64_t n, int32_t* nbr, int32_t* parent,
+                                         int32_t* np_dev, int32_t* pool_rows, float* inv_count, int32_t* up_rows,
+                                         void* ws, uint32_t* status, cudaStream_t st);
+
 }  // namespace msc

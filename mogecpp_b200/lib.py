@@ -31,6 +31,8 @@ SIGNATURES = {
     "msc_make_level": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "msc_make_level_noalloc": (C.c_int, [_vp, _i64, _vp, _vp, _vp]),
     "msc_downsample": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, C.POINTER(_i64), _vp, _sz, _vp]),
+    "msc_make_level_downsample": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, C.POINTER(_i64), _vp,
+                                            _sz, _vp]),
     "msc_weight_blob_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "msc_weight_prepare": (C.c_int, [_vp, _i32, _vp, _i32, _i32, _i32, _vp, _sz, _vp]),
     "msc_op_workspace_bytes": (_sz, [_i64, _i32]),

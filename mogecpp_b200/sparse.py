@@ -155,6 +155,28 @@ class SparseCudaExecutor:
         m = np_host.value
         return Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n, np_dev)
 
+    def make_level_downsample(self, coords: torch.Tensor, sync: bool = True):
+        """make_level and downsample of the same voxels in one call (one
+        voxel table): returns (nbr, Transition), as the two calls would."""
+        n = coords.shape[0]
+        dev = coords.device
+        nbr = torch.empty((n, 27), dtype=torch.int32, device=dev)
+        parent = torch.empty((max(n, 1), 4), dtype=torch.int32, device=dev)
+        np_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        pool = torch.empty(8 * max(n, 1), dtype=torch.int32, device=dev)
+        inv = torch.empty(max(n, 1), dtype=torch.float32, device=dev)
+        up = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        wsb = self.lib.msc_topology_workspace_bytes(n)
+        ws = self.workspace(wsb)
+        np_host = C.c_int64(0)
+        L.check(self.lib.msc_make_level_downsample(self.ctx, _p(coords), n, _p(nbr), _p(parent), _p(np_dev), _p(pool),
+                                                   _p(inv), _p(up), C.byref(np_host) if sync else None, _p(ws), wsb,
+                                                   _stream()))
+        if not sync:
+            return nbr, Transition(parent, pool, inv, up[:n], -1, n, np_dev)
+        m = np_host.value
+        return nbr, Transition(parent[:m], pool[:8 * m].view(8, m), inv[:m], up[:n], m, n, np_dev)
+
     def conv_plan(self, coords: torch.Tensor, nbr: torch.Tensor, kind: str = "tap_order") -> torch.Tensor:
         """Conv plan of a level (``msc_conv_plan_build``) for sparse_conv /
         res_block on the same level: the voxels in tiles of rows with similar

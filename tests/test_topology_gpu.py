@@ -140,3 +140,30 @@ def test_sparse_input_takes_the_per_voxel_hash(ex, oracle, spacing):
     nbr = host(ex.make_level(dev(coords)))
     ex.check()
     np.testing.assert_array_equal(nbr, oracle.make_level(coords))
+
+
+@pytest.mark.parametrize("gen", ["golden", "topo_4m", "sparse"])
+def test_make_level_downsample_equals_the_two_calls(ex, golden_topology, gen):
+    """msc_make_level_downsample (one voxel table for both maps) gives the
+    neighbour map of msc_make_level and the stride-2 maps of
+    msc_downsample, bit for bit: the reference's shuffled golden set, the
+    4M-voxel stress set, and a lattice sparse enough for the per-voxel hash."""
+    if gen == "golden":
+        c = golden_topology["topo_shuffled_coords"]
+    elif gen == "topo_4m":
+        c = synth.topo_4m_coords()
+    else:
+        g = np.arange(0, 22 * 5, 5)
+        x, y, z = np.meshgrid(g, g, g[:12], indexing="ij")
+        c = np.stack([x.ravel(), y.ravel(), z.ravel(), np.zeros(x.size, np.int64)], 1).astype(np.int32)
+    cd = dev(c)
+    nbr_f, tr_f = ex.make_level_downsample(cd)
+    ex.check()
+    nbr = ex.make_level(cd)
+    tr = ex.downsample(cd)
+    ex.check()
+    assert tr_f.np == tr.np
+    assert bool((nbr_f == nbr).all())
+    for a, b in ((tr_f.parent, tr.parent), (tr_f.pool_rows, tr.pool_rows), (tr_f.inv_count, tr.inv_count),
+                 (tr_f.up_rows, tr.up_rows)):
+        assert bool((a == b).all())
