@@ -347,7 +347,7 @@ __global__ void brick_insert_kernel(const int4* __restrict__ coords, int n, Slot
         const unsigned peers = __match_any_sync(__activemask(), key);
         if (!ok || static_cast<int>(threadIdx.x & 31) != __ffs(peers) - 1) continue;
         uint64_t h = mix64(key) & mask;
-        bool done = false;
+        bool done = false, fresh = false;
         for (uint64_t probe = 0; probe <= mask && !done; ++probe) {
             // most bricks are already in the table: a plain L2 read finds
             // them without an atomic (a stale empty read just takes the CAS)
@@ -356,10 +356,21 @@ __global__ void brick_insert_kernel(const int4* __restrict__ coords, int n, Slot
                 done = true;
             } else if (cur == kEmpty) {
                 const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, key);
-                if (prev == kEmpty) t[h].val = atomicAdd(ctr, 1);
-                done = prev == kEmpty || prev == key;
+                fresh = prev == kEmpty;
+                done = fresh || prev == key;
             }
-            h = (h + 1) & mask;
+            if (!done) h = (h + 1) & mask;
+        }
+        // ids for the bricks this warp inserted: one counter add per warp
+        const unsigned active = __activemask();
+        const unsigned won = __ballot_sync(active, fresh);
+        if (won) {
+            const int lead = __ffs(won) - 1;
+            const int lane = static_cast<int>(threadIdx.x & 31);
+            int base = 0;
+            if (lane == lead) base = atomicAdd(ctr, __popc(won));
+            base = __shfl_sync(active, base, lead);
+            if (fresh) t[h].val = base + __popc(won & ((1u << lane) - 1u));
         }
         if (!done) atomicMax(ctr, budget + 1);
     }
@@ -498,6 +509,7 @@ __global__ void __launch_bounds__(kScanBlock) brick_first_scan_kernel(const int4
                                                                       const int* __restrict__ rec,
                                                                       const int* __restrict__ ctr, int budget,
                                                                       int* __restrict__ first_idx,
+                                                                      int* __restrict__ cell_rc,
                                                                       int* __restrict__ excl, int* __restrict__ bsum) {
     if (*ctr > budget) return;
     __shared__ int warp_tot[kScanBlock / 32];
@@ -505,12 +517,17 @@ __global__ void __launch_bounds__(kScanBlock) brick_first_scan_kernel(const int4
     int f = 0;
     if (i < n) {
         const int4 c = __ldg(coords + i);
-        int first = -1;
+        int first = -1, rc = 8;
         if (coord_ok(c)) {
             const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
-            if (id >= 0) first = cell_info(rec, id, c, i).first;
+            if (id >= 0) {
+                const CellInfo ci = cell_info(rec, id, c, i);
+                first = ci.first;
+                rc = ci.rank | (ci.count << 8);
+            }
         }
         first_idx[i] = first;
+        cell_rc[i] = rc;
         f = first == i;
     }
     const int e = block_exclusive_scan(f, warp_tot, bsum + blockIdx.x);
@@ -518,9 +535,9 @@ __global__ void __launch_bounds__(kScanBlock) brick_first_scan_kernel(const int4
 }
 
 // Parent ids, up_rows, parent coordinates, pool_rows slots and inv_count.
-__global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, const Slot* __restrict__ t, uint64_t mask,
-                                    const int* __restrict__ rec, const int* __restrict__ ctr, int budget,
-                                    const int* __restrict__ first_idx, const int* __restrict__ excl,
+__global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, const int* __restrict__ ctr, int budget,
+                                    const int* __restrict__ first_idx, const int* __restrict__ cell_rc,
+                                    const int* __restrict__ excl,
                                     const int* __restrict__ bsum, const int* __restrict__ np_dev,
                                     int4* __restrict__ parent, int* __restrict__ up_rows, int* __restrict__ pool_rows,
                                     float* __restrict__ inv_count, uint32_t* status) {
@@ -534,8 +551,8 @@ __global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, cons
         const int pid = excl[first] + bsum[first / kScanBlock];
         up_rows[i] = pid;
         if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
-        const int id = table_find(t, mask, brick_key(c.x >> 2, c.y >> 2, c.z >> 2, c.w));
-        const CellInfo ci = id >= 0 ? cell_info(rec, id, c, i) : CellInfo{kNoVoxel, 0, 8};
+        const int rc = cell_rc[i];  // the cell's rank and count from the first-child pass
+        const CellInfo ci{first, rc >> 8, rc & 0xff};
         if (pid < 0 || pid >= np || ci.rank >= 8) {
             set_status(status, MSC_DEV_POOL_OVERFLOW);
             continue;
@@ -563,7 +580,8 @@ unsigned stride_grid(int64_t n, int per) {
 // Workspace layout (shared by make_level and downsample):
 //   per-voxel tables: 2 x cap slots (make_level uses the first; downsample
 //   the fine and parent tables) | excl [n + 1] | bsum | brick table (bcap
-//   slots) | brick records [budget][64] | counter | first child [n]
+//   slots) | brick records [budget][64] | counter | first child [n] |
+//   stride-2 cell rank and count [n]
 namespace {
 struct TopoWs {
     Slot* t;
@@ -573,6 +591,7 @@ struct TopoWs {
     int* rec;
     int* ctr;
     int* first;
+    int* cell;  // per voxel: the stride-2 cell's rank of it | count << 8
     uint64_t cap, bcap;
     int budget;
 };
@@ -597,6 +616,8 @@ TopoWs carve(void* ws, int64_t n) {
     w.ctr = reinterpret_cast<int*>(p);
     p += 256;
     w.first = reinterpret_cast<int*>(p);
+    p += align_up(static_cast<size_t>(n) * 4, 256);
+    w.cell = reinterpret_cast<int*>(p);
     return w;
 }
 
@@ -617,7 +638,7 @@ size_t topology_workspace_bytes(int64_t n) {
     return align_up(2 * table_capacity(n) * sizeof(Slot), 256) + align_up(static_cast<size_t>(n + 1) * 4, 256) +
            align_up(static_cast<size_t>(nblk) * 4, 256) + align_up(brick_capacity(n) * sizeof(Slot), 256) +
            align_up(static_cast<size_t>(brick_budget(n)) * kBrickVox * 4, 256) + 256 +
-           align_up(static_cast<size_t>(n) * 4, 256);
+           2 * align_up(static_cast<size_t>(n) * 4, 256);
 }
 
 namespace {
@@ -680,13 +701,12 @@ cudaError_t launch_stride2(const int4* c4, int64_t n, int32_t* parent, int32_t* 
     parent_insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tp, w.cap - 1, status, w.ctr, w.budget);
     // first children: flags + per-block scan (one of the two runs)
     brick_first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, w.first,
-                                                         w.excl, w.bsum);
+                                                         w.cell, w.excl, w.bsum);
     first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, tp, w.cap - 1, w.excl, w.bsum, w.ctr, w.budget);
     block_scan_kernel<<<1, kScanBlock, 0, st>>>(w.bsum, nblk, np_dev);
     pool_fill_kernel<<<kStrideGrid, 256, 0, st>>>(pool_rows, np_dev, ni);
-    brick_assign_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, w.first,
-                                                             w.excl, w.bsum, np_dev, par, up_rows, pool_rows,
-                                                             inv_count, status);
+    brick_assign_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, ni, w.ctr, w.budget, w.first, w.cell, w.excl, w.bsum,
+                                                             np_dev, par, up_rows, pool_rows, inv_count, status);
     assign_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tp, w.cap - 1, w.excl, w.bsum, par, up_rows, w.ctr, w.budget);
     slot_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tf, w.cap - 1, up_rows, np_dev, pool_rows, inv_count, status,
                                              w.ctr, w.budget);
