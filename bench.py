@@ -67,6 +67,11 @@ WORKLOADS = {
     "topo_4m": dict(kind="topo", coords="topo_4m_coords", grid=1024),
     "conv_c64": dict(kind="conv", coords="conv_c64_coords", grid=128, c=64),
     "unet_c64": dict(kind="unet", coords="unet_coords", grid=256),
+    # the same U-level with the octant-weighted stride-2 conv and its
+    # transpose in place of pool + linear and linear + nearest up (an
+    # extension: the reference has neither, so its arm is unavailable and the
+    # CPU baseline is the oracle on a z-slab sample)
+    "unet_octant_c64": dict(kind="unet", coords="unet_coords", grid=256, octant=True),
     "refine_640x480": dict(kind="refine", width=640, height=480, grid=None),
 }
 # DRAM bytes per voxel of one sparse-conv launch, by workload and residual-
@@ -143,7 +148,8 @@ def unet_params():
     lin = lambda seed, co, ci: (np.random.default_rng(seed).standard_normal((co, ci)) / np.sqrt(ci)).astype(np.float32)
     return dict(w0=synth.conv_weight(3000, 64, 64), wl=lin(3001, 128, 64), w1=synth.conv_weight(3002, 128, 128),
                 wu=lin(3003, 64, 128), b0=np.zeros(64, np.float32), bl=np.zeros(128, np.float32),
-                b1=np.zeros(128, np.float32), bu=np.zeros(64, np.float32))
+                b1=np.zeros(128, np.float32), bu=np.zeros(64, np.float32),
+                wd8=lin(3004, 128, 8 * 64), wu8=lin(3005, 64, 8 * 128))   # octant weights [cout][8*cin]
 
 
 class ClockSampler:
@@ -247,6 +253,30 @@ def stack_sample(coords, x0, blocks, block_kind, R, kind, target_s):
     return ns, sec
 
 
+def cpu_octant_baseline(coords, extra, ns=12000):
+    """The octant U-level on the oracle (single-threaded C), on the first ns
+    voxels of the set (a z-slab of the first sample): the reference has no
+    such operator, so this CPU restatement is the baseline."""
+    from oracle.oracle import Oracle, W_F32
+    q = Oracle()
+    c = np.ascontiguousarray(coords[:ns])
+    x = extra["x"][:ns]
+    p = extra["p"]
+    t0 = time.perf_counter()
+    nbr = q.make_level(c)
+    parent, pool, inv, up = q.downsample(c)
+    down, upm = q.octant_maps(c, pool, up)
+    pc = np.ascontiguousarray(parent)
+    nbr_c = q.make_level(pc)
+    h0 = q.sparse_conv(x, nbr, p["w0"], W_F32)
+    h1 = q.conv_rect(h0, down, pc.shape[0], 8, p["wd8"], W_F32)
+    h2 = q.sparse_conv(h1, nbr_c, p["w1"], W_F32)
+    q.conv_rect(h2, upm, c.shape[0], 8, p["wu8"], W_F32)
+    sec = time.perf_counter() - t0
+    return {"value": (c.shape[0] + pc.shape[0]) / sec, "unit": "voxels/s", "cores": 1, "kind": "port",
+            "sample": f"first {c.shape[0]} voxels of the set (a z-slab), the octant U-level step on the oracle"}
+
+
 def cpu_other_step(R, w, coords, extra):
     """One CPU step of the topology, single-conv or U-level workloads on the
     whole set.  Returns seconds."""
@@ -288,6 +318,11 @@ def run_reference(args):
         return
     from mogecpp_b200 import synth
     w = WORKLOADS[args.workload]
+    if w.get("octant"):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no octant-weighted stride-2 conv or "
+                          "transposed conv (its stride-2 operators are pool + linear and linear + nearest up, "
+                          "timed by --workload unet_c64)"}), flush=True)
+        return
     coords = getattr(synth, w["coords"])() if "coords" in w else np.zeros((0, 4), np.int32)
     threads = os.cpu_count() or 1
     R, kind, cores = open_reference(threads)
@@ -963,6 +998,38 @@ def build_other(args, w, ex, dev, coords):
         dtype = "fp32 (exact hi/lo fp16 split on tcgen05 kind::f16, fp32 accumulation)"
         cfg = {"step": "make_level + tap-order plan + 1 sparse conv", "channels": 64}
         launches_per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1}
+    elif w.get("octant"):
+        p = extra["p"]
+        P = lambda k, ci, co, t: ex.prepare_weight(torch.from_numpy(p[k]).to(dev), "f32", ci, co, t)
+        pw0, pwd, pw1, pwu = P("w0", 64, 64, 27), P("wd8", 64, 128, 8), P("w1", 128, 128, 27), P("wu8", 128, 64, 8)
+        x_d = torch.from_numpy(extra["x"]).to(dev).to(torch.bfloat16)
+        n_coarse = ex.downsample(coords_d).np
+
+        def step(coords_t=coords_d, x_t=x_d):
+            nbr, tr = ex.make_level_downsample(coords_t)
+            nbr_c = ex.make_level(tr.parent.contiguous())
+            down, up = ex.octant_maps(coords_t, tr)
+            state["nbr"] = nbr
+            h0 = ex.sparse_conv(x_t, nbr, pw0, None, out_dtype=torch.bfloat16)
+            h1 = ex.octant_conv(h0, down, pwd, None, out_dtype=torch.bfloat16, plan=ex.conv_plan_rect(down, n))
+            h2 = ex.sparse_conv(h1, nbr_c, pw1, None, out_dtype=torch.bfloat16)
+            state["y"] = ex.octant_conv(h2, up, pwu, None, out_dtype=torch.bfloat16,
+                                        plan=ex.conv_plan_rect(up, tr.np), skip=h0)
+
+        out_dev = lambda bi: state["y"]
+        h_out_shape, h_out_dtype = (n, 64), torch.bfloat16
+        h_in = (torch.from_numpy(coords).pin_memory(), x_d.cpu().pin_memory())
+        bufs = [(coords_d, x_d), (torch.empty_like(coords_d), torch.empty_like(x_d))]
+        units = n + n_coarse   # the two submanifold convs; the octant convs are counted as stride-2 operators
+
+        def roofline(prof):
+            return conv_roofline(prof, "conv_tc", 64, 64, state, n, 4 + 4 + 112, 0, "bf16 (hi/lo fp16, kind::f16)",
+                                 peak_tf, peak_hbm, peak_src, 3, bytes_x=4, bytes_y=2)
+
+        dtype = "bf16 activations, fp32 weights (exact hi/lo fp16 split on tcgen05 kind::f16)"
+        cfg = {"step": "make_level x2 + downsample + octant maps + conv 64 + octant strided conv 64->128 + conv 128 "
+                       "+ octant transposed conv 128->64 + skip", "samples": 2, "coarse_voxels": int(n_coarse)}
+        launches_per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "octant_maps": 2}
     else:  # unet
         p = extra["p"]
         P = lambda k, ci, co, t: ex.prepare_weight(torch.from_numpy(p[k]).to(dev), "f32", ci, co, t)
@@ -1003,6 +1070,8 @@ def build_other(args, w, ex, dev, coords):
         return sum(launches_per.get(k, 1) * v[0] for k, v in prof.items())
 
     def cpu_baseline():
+        if w.get("octant"):
+            return {"cpu_baseline": cpu_octant_baseline(coords, extra)}
         threads = os.cpu_count() or 1
         R, kind, cores = open_reference(threads)
         cpu_other_step(R, w, coords, extra)  # warm-up

@@ -338,6 +338,40 @@ int msc_nearest_up(msc_ctx_t ctx, const void* x, int x_dtype, int64_t np, int c,
                    int64_t nfine, const void* blob, const float* bias, const void* skip, int skip_dtype, void* y,
                    int y_dtype, void* ws, size_t ws_bytes, void* stream);
 
+/* ------------------------------------------------- octant stride-2 conv
+ * An extension with no counterpart in the reference, whose stride-2
+ * operators are pool_down (mean over the children + linear,
+ * src/sparse.cpp:646-668) and nearest_up (linear + parent gather, :670-674):
+ * the octant-weighted stride-2 conv (each parent sums W_o x[child at octant
+ * o] over its 2 x 2 x 2 cell) and its transpose (each child takes W_o
+ * x[parent], o its own octant).  The octant of fine voxel (x, y, z) is
+ * (x & 1) * 4 + (y & 1) * 2 + (z & 1); weights are packed [cout][8 * cin]
+ * (cin fastest), prepared with ntaps = 8.
+ *
+ * Octant maps of a transition from msc_downsample (pool_rows [8][np],
+ * up_rows [nfine]; np on the host): down_nbr [np][27] (column o = the child
+ * at octant o, else nfine; columns 8-26 nfine) and up_nbr [nfine][27]
+ * (column oct(c) = c's parent, every other column np). */
+int msc_octant_maps(msc_ctx_t ctx, const int32_t* coords, int64_t nfine, const int32_t* pool_rows,
+                    const int32_t* up_rows, int64_t np, int32_t* down_nbr, int32_t* up_nbr, void* stream);
+
+/* Tap-order conv plan for a map whose neighbour lists index another level's
+ * rows: n_out output rows, entries in [0, n_in) present.  Sizes as
+ * msc_conv_plan_bytes(n_out) / msc_conv_plan_workspace_bytes(n_out). */
+int msc_conv_plan_build_rect(msc_ctx_t ctx, int64_t n_out, int64_t n_in, const int32_t* nbr, void* plan,
+                             size_t plan_bytes, void* ws, size_t ws_bytes, void* stream);
+
+/* y [n_out][cout] = sum_{o < 8} W_o x[nbr[i][o]] + bias (+ skip [n_out][cout],
+ * may be NULL) over x [n_in][cin]: the strided conv with nbr = down_nbr
+ * (n_in = nfine, n_out = np), the transposed conv with nbr = up_nbr (n_in =
+ * np, n_out = nfine; the skip is the decoder's additive skip).  plan: from
+ * msc_conv_plan_build_rect over the same map, or NULL (strongly advised for
+ * the transpose, whose rows each have one tap).  Workspace:
+ * msc_op_workspace_bytes(n_in, cin). */
+int msc_octant_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n_in, int cin, const int32_t* nbr,
+                    int64_t n_out, const void* plan, const void* blob, const float* bias, const void* skip,
+                    int skip_dtype, void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream);
+
 /* ------------------------------------------------------------ multi-GPU
  * A z-slab shard of a level for one GPU of a node (one process per GPU).
  * No counterpart in the reference (its refiner is single-device,

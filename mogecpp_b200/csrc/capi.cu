@@ -31,8 +31,9 @@ struct msc_context {
     std::mutex mu;
     std::unordered_map<const void*, Blob> blobs;
     struct Plan {
-        int64_t n;
+        int64_t n;     // output rows
         int kind;
+        int64_t n_in;  // input rows its neighbour lists index
     };
     std::unordered_map<const void*, Plan> plans;  // conv plans built by this context
     // kernel profiling (msc_profile_*): one event pair per launch
@@ -170,16 +171,18 @@ struct PlanUse {
 
 void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, const int32_t* nbr,
               const msc_context::Blob& b, const void* blob, const float* bias, int silu_out, const void* residual,
-              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}, void* q_out = nullptr) {
+              int res_dtype, void* y, int y_dtype, cudaStream_t st, PlanUse pu = {}, void* q_out = nullptr,
+              int64_t n_in = -1, const char* family = nullptr) {
+    if (n_in < 0) n_in = n;  // input rows (the prepared planes) = output rows unless given
     msc::ConvArgs a{};
     a.planes = planes;
     a.q8 = mode == msc::ACT_Q8 || mode == msc::ACT_Q8I;
     a.i8 = mode == msc::ACT_Q8I;
     a.a_scale = a.q8 ? reinterpret_cast<const float*>(static_cast<const char*>(planes) +
-                                                      msc::act_scale_offset(mode, n, cin))
+                                                      msc::act_scale_offset(mode, n_in, cin))
                      : nullptr;
     a.na = msc::act_planes(mode);
-    a.n_in = n;
+    a.n_in = n_in;
     a.n = n;
     a.row_begin = 0;
     a.perm = nullptr;
@@ -209,14 +212,15 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
     a.tile_rows = pu.tiles.rows;
     a.tile_nbr = nbr ? pu.tiles.nbr : nullptr;
     a.tile_mask = pu.tiles.mask;
-    ProfScope ps(ctx, nbr ? "conv_tc" : "linear_tc", st);
+    ProfScope ps(ctx, family ? family : (nbr ? "conv_tc" : "linear_tc"), st);
     cuda_ok(msc::launch_conv(a, st), "conv launch");
 }
 
 // The plan, when given, must come from msc_conv_plan_build on this context
 // for n voxels; it reorders the neighbour-map conv's tiles for every weight
 // type.
-PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n) {
+PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n, int64_t n_in = -1) {
+    if (n_in < 0) n_in = n;
     PlanUse pu;
     if (!plan) return pu;
     msc_context::Plan pl{};
@@ -228,6 +232,8 @@ PlanUse use_plan(msc_ctx_t ctx, const void* plan, int64_t n) {
     }
     if (pl.n != n)
         fail(MSC_E_INVALID, "conv plan covers " + std::to_string(pl.n) + " voxels, not " + std::to_string(n));
+    if (pl.n_in != n_in)
+        fail(MSC_E_INVALID, "conv plan indexes " + std::to_string(pl.n_in) + " input rows, not " + std::to_string(n_in));
     pu.tiles = msc::plan_tiles(static_cast<uint8_t*>(const_cast<void*>(plan)), n);
     pu.order = pu.tiles.order;
     return pu;
@@ -439,7 +445,8 @@ int msc_weight_prepare(msc_ctx_t ctx, int wtype, const void* w, int cin, int cou
     return guard([&] {
         need_ctx(ctx);
         need(wtype == MSC_W_F32 || wtype == MSC_W_F16 || wtype == MSC_W_Q8_0, "unknown weight type");
-        need(ntaps == 27 || ntaps == 1, "ntaps must be 27 (sparse conv) or 1 (linear)");
+        need(ntaps == 27 || ntaps == 8 || ntaps == 1,
+             "ntaps must be 27 (sparse conv), 8 (octant-weighted stride-2 conv) or 1 (linear)");
         need(w && blob, "null pointer");
         need(cin > 0 && cout > 0, "bad channel counts");
         if (cin % 64 != 0) fail(MSC_E_UNSUPPORTED, "cin must be a multiple of 64");
@@ -489,7 +496,30 @@ int msc_conv_plan_build(msc_ctx_t ctx, const int32_t* coords, int64_t n, const i
             cuda_ok(msc::launch_plan_build(nbr, n, n, plan, ws, S(stream)), "plan build launch");
         }
         std::lock_guard<std::mutex> lk(ctx->mu);
-        ctx->plans[plan] = msc_context::Plan{n, kind};
+        ctx->plans[plan] = msc_context::Plan{n, kind, n};
+    });
+}
+
+int msc_conv_plan_build_rect(msc_ctx_t ctx, int64_t n_out, int64_t n_in, const int32_t* nbr, void* plan,
+                             size_t plan_bytes, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(n_out >= 0 && n_out < (int64_t(1) << 31) / 27, "voxel count out of range");
+        need(n_in >= 0 && n_in < (int64_t(1) << 31), "input row count out of range");
+        need(plan != nullptr, "null plan pointer");
+        need_aligned(plan, 256, "plan");
+        need_ws(plan_bytes, msc::plan_bytes(n_out));
+        if (n_out > 0) {
+            need(nbr && ws, "null pointer");
+            need_aligned(ws, 256, "workspace");
+            need_ws(ws_bytes, msc::plan_workspace_bytes(n_out));
+        }
+        {
+            ProfScope ps(ctx, "plan_build", S(stream));
+            cuda_ok(msc::launch_plan_build(nbr, n_out, n_in, plan, ws, S(stream)), "plan build launch");
+        }
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        ctx->plans[plan] = msc_context::Plan{n_out, MSC_PLAN_TAP_ORDER, n_in};
     });
 }
 
@@ -514,6 +544,52 @@ int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n
         cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
                 "activation prepare");
         run_conv(ctx, ws, mode, n, cin, nbr, b, blob, bias, 0, nullptr, 0, y, y_dtype, S(stream), pl);
+    });
+}
+
+int msc_octant_maps(msc_ctx_t ctx, const int32_t* coords, int64_t nfine, const int32_t* pool_rows,
+                    const int32_t* up_rows, int64_t np, int32_t* down_nbr, int32_t* up_nbr, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need(nfine >= 0 && nfine < (int64_t(1) << 31) / 27, "voxel count out of range");
+        need(np >= 0 && np <= nfine, "parent count out of range");
+        if (nfine == 0) return;
+        need(coords && pool_rows && up_rows && down_nbr && up_nbr, "null pointer");
+        need_aligned(coords, 16, "coords");
+        ProfScope ps(ctx, "octant_maps", S(stream));
+        cuda_ok(msc::launch_octant_maps(coords, nfine, pool_rows, up_rows, np, down_nbr, up_nbr, S(stream)),
+                "octant maps launch");
+    });
+}
+
+int msc_octant_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n_in, int cin, const int32_t* nbr,
+                    int64_t n_out, const void* plan, const void* blob, const float* bias, const void* skip,
+                    int skip_dtype, void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need_dtype(y_dtype, "y");
+        const auto b = blob_info(ctx, blob);
+        check_conv_shape(b, cin, 8);
+        need(n_in >= 0 && n_in < (int64_t(1) << 31), "input row count out of range");
+        need(n_out >= 0 && n_out < (int64_t(1) << 31) / 27, "output row count out of range");
+        if (n_out == 0) return;
+        const PlanUse pl = use_plan(ctx, plan, n_out, n_in);
+        need(nbr && y && ws && (x || n_in == 0), "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(y, 16, "y");
+        need_aligned(ws, 256, "workspace");
+        if (skip) {
+            need_dtype(skip_dtype, "skip");
+            need_aligned(skip, 16, "skip");
+        }
+        const int mode = act_mode(b.wtype, x_dtype, b.cin);
+        need_ws(ws_bytes, msc::act_bytes(mode, n_in, cin));
+        if (n_in > 0)
+            cuda_ok(act_prepare(ctx, x, x_dtype, n_in, cin, 0, nullptr, nullptr, 0.f, 0, mode, ws, S(stream)),
+                    "activation prepare");
+        run_conv(ctx, ws, mode, n_out, cin, nbr, b, blob, bias, 0, skip, skip ? skip_dtype : 0, y, y_dtype,
+                 S(stream), pl, nullptr, n_in, "octant_conv");
     });
 }
 

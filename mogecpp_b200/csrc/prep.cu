@@ -200,9 +200,22 @@ __device__ __forceinline__ float row_sum8(float s) {
 
 // Normalisation, SiLU and the operand output of one row; all 32 lanes call
 // it (the shuffles need them), `valid` gates the stores.
+// The affine weights of the normalisation, per row-group lane j: its EPL
+// channels at j * (EPL + 4) floats in shared memory (the 4-float pad puts
+// the 8 lanes' 16-byte reads in distinct banks).
+template <int C>
+struct Affine {
+    static constexpr int EPL = C / 8;
+    static constexpr int STRIDE = EPL + 4;
+    const float* g;  // this lane's gamma (nullptr: none)
+    const float* b;  // this lane's beta (nullptr: none)
+    __device__ __forceinline__ float gamma(int k) const { return g[k]; }
+    __device__ __forceinline__ float beta(int k) const { return b[k]; }
+};
+
 template <int C>
 __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, bool valid, int j, int64_t n, int ln,
-                                             const float* gamma, const float* beta, float eps, int silu, int mode,
+                                             const Affine<C>& aff, float eps, int silu, int mode,
                                              __half* planes, const float2* gn, const int4* coords, int nsamples) {
     constexpr int EPL = C / 8;
     constexpr int CPG = C / 32;  // channels per GroupNorm group
@@ -218,8 +231,8 @@ __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, boo
 #pragma unroll
             for (int k = gq * CPG; k < (gq + 1) * CPG; ++k) {
                 float t = __fmul_rn(v[k] - ms.x, ms.y);
-                if (gamma) t = __fmul_rn(t, __ldg(gamma + j * EPL + k));
-                if (beta) t = __fadd_rn(t, __ldg(beta + j * EPL + k));
+                if (aff.g) t = __fmul_rn(t, aff.gamma(k));
+                if (aff.b) t = __fadd_rn(t, aff.beta(k));
                 v[k] = t;
             }
         }
@@ -238,8 +251,8 @@ __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, boo
 #pragma unroll
         for (int k = 0; k < EPL; ++k) {
             float t = __fmul_rn(v[k] - mean, scale);
-            if (gamma) t = __fmul_rn(t, __ldg(gamma + j * EPL + k));
-            if (beta) t = __fadd_rn(t, __ldg(beta + j * EPL + k));
+            if (aff.g) t = __fmul_rn(t, aff.gamma(k));
+            if (aff.b) t = __fadd_rn(t, aff.beta(k));
             v[k] = t;
         }
     }
@@ -302,11 +315,24 @@ template <int C>
 __global__ void __launch_bounds__(256, C <= 128 ? 4 : 1) act_prepare_kernel(const void* x, int x_dtype, int64_t n, int ln, const float* gamma,
                                    const float* beta, float eps, int silu, int mode, __half* planes,
                                    const float2* gn, const int4* coords, int nsamples) {
+    // gamma / beta once per block into shared memory (a per-element global
+    // load per row cost 32 L1 requests per lane and row)
+    using A = Affine<C>;
+    __shared__ __align__(16) float s_aff[2][8 * A::STRIDE];
+    if (gamma || beta) {  // uniform over the block
+        for (int e = threadIdx.x; e < C; e += blockDim.x) {
+            const int jj = e / A::EPL, k = e % A::EPL;
+            s_aff[0][jj * A::STRIDE + k] = gamma ? __ldg(gamma + e) : 1.0f;
+            s_aff[1][jj * A::STRIDE + k] = beta ? __ldg(beta + e) : 0.0f;
+        }
+        __syncthreads();
+    }
     const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int j = lane & (kLanesPerRow - 1);
     const int64_t r0 = warp * (4 * kPrepIters) + (lane >> 3);
     if (warp * (4 * kPrepIters) >= n) return;
+    const A aff{gamma ? s_aff[0] + j * A::STRIDE : nullptr, beta ? s_aff[1] + j * A::STRIDE : nullptr};
     float v[kPrepIters][C / 8];
 #pragma unroll
     for (int it = 0; it < kPrepIters; ++it) {
@@ -321,7 +347,7 @@ __global__ void __launch_bounds__(256, C <= 128 ? 4 : 1) act_prepare_kernel(cons
 #pragma unroll
     for (int it = 0; it < kPrepIters; ++it) {
         const int64_t row = r0 + 4 * it;
-        prepare_row8<C>(v[it], row, row < n, j, n, ln, gamma, beta, eps, silu, mode, planes, gn, coords, nsamples);
+        prepare_row8<C>(v[it], row, row < n, j, n, ln, aff, eps, silu, mode, planes, gn, coords, nsamples);
     }
 }
 

@@ -562,6 +562,62 @@ __global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, cons
     }
 }
 
+// Octant maps of a stride-2 transition, for the octant-weighted stride-2
+// conv and its transpose (an extension: the reference's stride-2 operators
+// are pool + linear and linear + nearest up).  The octant of fine voxel
+// (x, y, z) in its parent's 2 x 2 x 2 cell is (x & 1) * 4 + (y & 1) * 2 +
+// (z & 1).  One thread per output row; a block's [256][27] rows are staged
+// in shared memory and leave as one contiguous run.
+//   down [np][27]: column o = the child at octant o (from pool_rows), or nfine
+//   up [nfine][27]: column oct(c) = up_rows[c], every other column np
+__device__ __forceinline__ int octant(int4 c) { return (c.x & 1) * 4 + (c.y & 1) * 2 + (c.z & 1); }
+
+__device__ __forceinline__ void store_rows27(int* __restrict__ out, const int* __restrict__ sn, int64_t rows) {
+    const int64_t count = rows * 27;
+    int64_t k0 = 0;
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        const int64_t c4 = count / 4;
+        for (int64_t k = threadIdx.x; k < c4; k += blockDim.x)
+            reinterpret_cast<int4*>(out)[k] = reinterpret_cast<const int4*>(sn)[k];
+        k0 = c4 * 4;
+    }
+    for (int64_t k = k0 + threadIdx.x; k < count; k += blockDim.x) out[k] = sn[k];
+}
+
+__global__ void __launch_bounds__(256) octant_down_kernel(const int4* __restrict__ coords, int nfine,
+                                                          const int* __restrict__ pool_rows, int np,
+                                                          int* __restrict__ down) {
+    __shared__ __align__(16) int sn[256 * 27];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * 256;
+    const int64_t p = base + threadIdx.x;
+    int* row = sn + threadIdx.x * 27;
+#pragma unroll
+    for (int t = 0; t < 27; ++t) row[t] = nfine;
+    if (p < np) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const int c = __ldg(pool_rows + static_cast<int64_t>(s) * np + p);
+            if (c >= 0 && c < nfine) row[octant(__ldg(coords + c))] = c;
+        }
+    }
+    __syncthreads();
+    store_rows27(down + base * 27, sn, np - base < 256 ? np - base : 256);
+}
+
+__global__ void __launch_bounds__(256) octant_up_kernel(const int4* __restrict__ coords, int nfine,
+                                                        const int* __restrict__ up_rows, int np,
+                                                        int* __restrict__ up) {
+    __shared__ __align__(16) int sn[256 * 27];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * 256;
+    const int64_t c = base + threadIdx.x;
+    int* row = sn + threadIdx.x * 27;
+#pragma unroll
+    for (int t = 0; t < 27; ++t) row[t] = np;
+    if (c < nfine) row[octant(__ldg(coords + c))] = __ldg(up_rows + c);
+    __syncthreads();
+    store_rows27(up + base * 27, sn, nfine - base < 256 ? nfine - base : 256);
+}
+
 uint64_t table_capacity(int64_t n) {
     uint64_t cap = 64;
     while (cap < static_cast<uint64_t>(2 * n)) cap <<= 1;
@@ -723,6 +779,18 @@ cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent,
     cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
     if (e != cudaSuccess) return e;
     return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st);
+}
+
+cudaError_t launch_octant_maps(const int32_t* coords, int64_t nfine, const int32_t* pool_rows,
+                               const int32_t* up_rows, int64_t np, int32_t* down, int32_t* up, cudaStream_t st) {
+    const auto* c4 = reinterpret_cast<const int4*>(coords);
+    if (np > 0)
+        octant_down_kernel<<<static_cast<unsigned>((np + 255) / 256), 256, 0, st>>>(
+            c4, static_cast<int>(nfine), pool_rows, static_cast<int>(np), down);
+    if (nfine > 0)
+        octant_up_kernel<<<static_cast<unsigned>((nfine + 255) / 256), 256, 0, st>>>(
+            c4, static_cast<int>(nfine), up_rows, static_cast<int>(np), up);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_make_level_downsample(const int32_t* coords, int64_t n, int32_t* nbr, int32_t* parent,

@@ -31,4 +31,10 @@ cudaError_t launch_make_level_downsample(const int32_t* coords, int64_t n, int32
                                          int32_t* np_dev, int32_t* pool_rows, float* inv_count, int32_t* up_rows,
                                          void* ws, uint32_t* status, cudaStream_t st);
 
+// Octant maps of a stride-2 transition (pool_rows [8][np], up_rows
+// [nfine]): down [np][27] (column o = the child at octant o, else nfine) and
+// up [nfine][27] (column oct(c) = c's parent, else np).
+cudaError_t launch_octant_maps(const int32_t* coords, int64_t nfine, const int32_t* pool_rows,
+                               const int32_t* up_rows, int64_t np, int32_t* down, int32_t* up, cudaStream_t st);
+
 }  // namespace msc

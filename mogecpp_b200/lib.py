@@ -40,6 +40,10 @@ SIGNATURES = {
     "msc_conv_plan_bytes": (_sz, [_i64]),
     "msc_conv_plan_workspace_bytes": (_sz, [_i64]),
     "msc_conv_plan_build": (C.c_int, [_vp, _vp, _i64, _vp, _i32, _vp, _sz, _vp, _sz, _vp]),
+    "msc_conv_plan_build_rect": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _sz, _vp, _sz, _vp]),
+    "msc_octant_maps": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "msc_octant_conv": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp,
+                                  _sz, _vp]),
     "msc_sparse_conv_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz,
                                           _vp]),
     "msc_res_block_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -229,6 +229,44 @@ class SparseCudaExecutor:
                                                  _stream()))
         return y
 
+    def octant_maps(self, coords: torch.Tensor, tr: "Transition"):
+        """(down_nbr [np][27], up_nbr [nfine][27]) of a synced stride-2
+        transition: the maps of the octant-weighted strided conv and of its
+        transpose (an extension; the reference's stride-2 operators are pool
+        + linear and linear + nearest up)."""
+        nfine, np_ = coords.shape[0], tr.np
+        down = torch.empty((max(np_, 1), 27), dtype=torch.int32, device=coords.device)
+        up = torch.empty((max(nfine, 1), 27), dtype=torch.int32, device=coords.device)
+        L.check(self.lib.msc_octant_maps(self.ctx, _p(coords), nfine, _p(tr.pool_rows), _p(tr.up_rows), np_,
+                                         _p(down), _p(up), _stream()))
+        return down[:np_], up[:nfine]
+
+    def conv_plan_rect(self, nbr: torch.Tensor, n_in: int) -> torch.Tensor:
+        """Tap-order plan of a map whose entries index n_in rows of another
+        level (msc_conv_plan_build_rect)."""
+        n = nbr.shape[0]
+        pb = self.lib.msc_conv_plan_bytes(n)
+        plan = torch.empty(pb, dtype=torch.uint8, device=nbr.device)
+        wsb = self.lib.msc_conv_plan_workspace_bytes(n)
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_conv_plan_build_rect(self.ctx, n, n_in, _p(nbr), _p(plan), pb, _p(ws), wsb,
+                                                  _stream()))
+        return plan
+
+    def octant_conv(self, x, nbr, w: PreparedWeight, bias=None, out_dtype=torch.float32, plan=None, skip=None):
+        """y [nbr rows][cout] = sum_o W_o x[nbr[i][o]] + bias (+ skip) (w
+        prepared with ntaps = 8): the strided conv over down_nbr, the
+        transpose over up_nbr."""
+        n_in, cin = x.shape
+        n_out = nbr.shape[0]
+        y = torch.empty((n_out, w.cout), dtype=out_dtype, device=x.device)
+        wsb = self.lib.msc_op_workspace_bytes(max(n_in, 1), max(cin, w.cout))
+        ws = self.workspace(wsb)
+        L.check(self.lib.msc_octant_conv(self.ctx, _p(x), _DT[x.dtype], n_in, cin, _p(nbr), n_out, _p(plan),
+                                         _p(w.blob), _p(bias), _p(skip), _DT[skip.dtype] if skip is not None else 0,
+                                         _p(y), _DT[out_dtype], _p(ws), wsb, _stream()))
+        return y
+
     def linear(self, x, w: PreparedWeight, bias=None, out_dtype=torch.float32):
         n, cin = x.shape
         y = torch.empty((n, w.cout), dtype=out_dtype, device=x.device)

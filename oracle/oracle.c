@@ -347,6 +347,63 @@ void orc_sparse_conv(const float *x, int64_t n, int cin, const int32_t *nbr, int
     free(aq);
 }
 
+/* Octant-weighted stride-2 conv and its transpose: an extension with no
+ * counterpart in the reference, whose stride-2 operators are pool_down
+ * (src/sparse.cpp:646-668) and nearest_up (:670-674).  A conv over a map
+ * whose inputs are another level's rows: n_in input rows, n_out output rows,
+ * nbr [n_out][27] of which the first ntaps columns are used (sentinel: any
+ * value outside [0, n_in)); W packed [cout][ntaps * cin] as the 27-tap
+ * conv's.  The gathered row is multiplied as orc_sparse_conv's (ggml
+ * mul_mat semantics for wtype). */
+void orc_conv_rect(const float *x, int64_t n_in, int cin, const int32_t *nbr, int64_t n_out, int ntaps, int wtype,
+                   const void *w, int cout, const float *bias, float *y) {
+    const int k = ntaps * cin;
+    float *g = (float *)malloc(sizeof(float) * (size_t)k);
+    float *af = (float *)malloc(sizeof(float) * (size_t)k);
+    orc_block_q8_0 *aq = (orc_block_q8_0 *)malloc(sizeof(orc_block_q8_0) * (size_t)(k / 32 + 1));
+    const orc_wview v = orc_view(wtype, w, k);
+    for (int64_t i = 0; i < n_out; ++i) {
+        for (int t = 0; t < ntaps; ++t) {
+            const int32_t j = nbr[i * 27 + t];
+            if (j >= 0 && j < n_in)
+                memcpy(g + t * cin, x + (int64_t)j * cin, sizeof(float) * (size_t)cin);
+            else
+                memset(g + t * cin, 0, sizeof(float) * (size_t)cin);
+        }
+        orc_prep(wtype, g, k, af, aq);
+        for (int o = 0; o < cout; ++o) {
+            float r = (float)orc_dot_row(&v, o, af, aq);
+            if (bias) r += bias[o];
+            y[i * cout + o] = r;
+        }
+    }
+    free(g);
+    free(af);
+    free(aq);
+}
+
+/* Octant maps of a stride-2 transition (orc_downsample's pool_rows [8][np]
+ * and up_rows [nfine]).  The octant of fine voxel (x, y, z) inside its
+ * parent's 2 x 2 x 2 cell is (x & 1) * 4 + (y & 1) * 2 + (z & 1).
+ *   down [np][27]: column o = the child at octant o, or nfine; columns 8-26 nfine
+ *   up [nfine][27]: column oct(c) = c's parent, every other column np */
+void orc_octant_maps(const int32_t *coords, int64_t nfine, const int32_t *pool_rows, const int32_t *up_rows,
+                     int64_t np, int32_t *down, int32_t *up) {
+    for (int64_t i = 0; i < np * 27; ++i) down[i] = (int32_t)nfine;
+    for (int64_t i = 0; i < nfine * 27; ++i) up[i] = (int32_t)np;
+    for (int64_t p = 0; p < np; ++p)
+        for (int s = 0; s < 8; ++s) {
+            const int32_t c = pool_rows[(int64_t)s * np + p];
+            if (c < 0 || c >= nfine) continue;
+            const int32_t *q = coords + (int64_t)c * 4;
+            down[p * 27 + (q[0] & 1) * 4 + (q[1] & 1) * 2 + (q[2] & 1)] = c;
+        }
+    for (int64_t c = 0; c < nfine; ++c) {
+        const int32_t *q = coords + c * 4;
+        up[c * 27 + (q[0] & 1) * 4 + (q[1] & 1) * 2 + (q[2] & 1)] = up_rows[c];
+    }
+}
+
 /* src/sparse.cpp:515-518 linear: mul_mat(W [cout][cin], x) + bias. */
 void orc_linear(const float *x, int64_t n, int cin, int wtype, const void *w, int cout, const float *bias, float *y) {
     float *af = (float *)malloc(sizeof(float) * (size_t)cin);

@@ -52,6 +52,14 @@ int orc_downsample(const int32_t *coords, int32_t n, int32_t *parent, int32_t *n
  *   quantised per 32-block, w = orc_block_q8_0 rows. */
 void orc_sparse_conv(const float *x, int64_t n, int cin, const int32_t *nbr, int wtype, const void *w, int cout,
                      const float *bias, float *y);
+/* Conv from n_in input rows to n_out output rows over nbr [n_out][27] (first
+ * ntaps columns), W [cout][ntaps*cin]: the octant-weighted stride-2 conv and
+ * its transpose (no counterpart in the reference). */
+void orc_conv_rect(const float *x, int64_t n_in, int cin, const int32_t *nbr, int64_t n_out, int ntaps, int wtype,
+                   const void *w, int cout, const float *bias, float *y);
+/* Octant maps of a stride-2 transition: down [np][27], up [nfine][27]. */
+void orc_octant_maps(const int32_t *coords, int64_t nfine, const int32_t *pool_rows, const int32_t *up_rows,
+                     int64_t np, int32_t *down, int32_t *up);
 /* y[n][cout] = W x + bias with W [cout][cin] (ggml linear). */
 void orc_linear(const float *x, int64_t n, int cin, int wtype, const void *w, int cout, const float *bias, float *y);
 void orc_layer_norm(const float *x, int64_t n, int c, const float *gamma, const float *beta, float eps, float *y);

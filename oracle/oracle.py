@@ -46,6 +46,9 @@ class Oracle:
         L.orc_downsample.argtypes = [_i32p, C.c_int32, _i32p, C.POINTER(C.c_int32), _i32p, _f32p, _i32p]
         L.orc_sparse_conv.argtypes = [_f32p, _i64, C.c_int, _i32p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, _f32p]
         L.orc_linear.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, _f32p]
+        L.orc_conv_rect.argtypes = [_f32p, _i64, C.c_int, _i32p, _i64, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                    C.c_void_p, _f32p]
+        L.orc_octant_maps.argtypes = [_i32p, _i64, _i32p, _i32p, _i64, _i32p, _i32p]
         L.orc_layer_norm.argtypes = [_f32p, _i64, C.c_int, C.c_void_p, C.c_void_p, C.c_float, _f32p]
         L.orc_silu.argtypes = [_f32p, _i64]
         L.orc_res_block.argtypes = [_f32p, _i64, C.c_int, _i32p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -135,6 +138,28 @@ class Oracle:
         self.lib.orc_sparse_conv(x, n, cin, _c(nbr, np.int32), wtype, payload.ctypes.data_as(C.c_void_p), cout,
                                  _opt(bias), y)
         return y
+
+    def conv_rect(self, x, nbr, n_out, ntaps, w, wtype, bias=None):
+        """Conv from x's rows to n_out rows over nbr [n_out][27] (first ntaps
+        columns): the octant-weighted stride-2 conv and its transpose."""
+        x = _c(x, np.float32)
+        n_in, cin = x.shape
+        payload = self.weight_payload(w, wtype, self)
+        cout = w.shape[0]
+        y = np.empty((n_out, cout), dtype=np.float32)
+        self.lib.orc_conv_rect(x, n_in, cin, _c(nbr, np.int32), n_out, ntaps, wtype,
+                               payload.ctypes.data_as(C.c_void_p), cout, _opt(bias), y)
+        return y
+
+    def octant_maps(self, coords, pool_rows, up_rows):
+        """(down [np][27], up [nfine][27]) of a stride-2 transition."""
+        coords = _c(coords, np.int32)
+        pool_rows = _c(pool_rows, np.int32)
+        nfine, np_ = coords.shape[0], pool_rows.size // 8
+        down = np.empty(np_ * 27, dtype=np.int32)
+        up = np.empty(nfine * 27, dtype=np.int32)
+        self.lib.orc_octant_maps(coords.ravel(), nfine, pool_rows.ravel(), _c(up_rows, np.int32), np_, down, up)
+        return down.reshape(np_, 27), up.reshape(nfine, 27)
 
     def linear(self, x, w, wtype, bias=None):
         x = _c(x, np.float32)
