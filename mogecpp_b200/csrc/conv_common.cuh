@@ -1,6 +1,5 @@
-// Device helpers shared by the tensor-core conv kernels (conv_tc.cu,
-// conv_cached.cu): bounded waits, tap-order rotation, packed f32x2
-// arithmetic and row stores.
+// Device helpers of the tensor-core conv kernel (conv_tc.cu): bounded waits,
+// tap-order rotation and row loads / stores.
 #pragma once
 
 #include "common.cuh"
@@ -57,30 +56,6 @@ __device__ __forceinline__ uint32_t rot_mask(uint32_t m, int r) {
 __device__ __forceinline__ int rot_tap(int bit, int r) {
     const int t = bit + r;
     return t >= 27 ? t - 27 : t;
-}
-
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
 }
 
 __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t idx) {

@@ -209,9 +209,28 @@ struct Affine {
     static constexpr int STRIDE = EPL + 4;
     const float* g;  // this lane's gamma (nullptr: none)
     const float* b;  // this lane's beta (nullptr: none)
-    __device__ __forceinline__ float gamma(int k) const { return g[k]; }
-    __device__ __forceinline__ float beta(int k) const { return b[k]; }
+    // channels (2k, 2k + 1) as an f32x2 pair
+    __device__ __forceinline__ uint64_t gamma2(int k) const { return reinterpret_cast<const uint64_t*>(g)[k]; }
+    __device__ __forceinline__ uint64_t beta2(int k) const { return reinterpret_cast<const uint64_t*>(b)[k]; }
 };
+
+// SiLU of two lanes, v / (1 + 2^(-v log2 e)), with the PTX approximations
+// ex2.approx.ftz and rcp.approx.ftz (relative error ~1e-6 over the range
+// that matters; v -> -inf gives -0, v -> +inf gives v) and packed multiplies.
+__device__ __forceinline__ uint64_t silu2(uint64_t v2) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    float a0, a1;
+    unpack2(mul2(v2, pack2(-kLog2e, -kLog2e)), a0, a1);
+    float e0, e1;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
+    float d0, d1;
+    unpack2(add2(pack2(e0, e1), pack2(1.0f, 1.0f)), d0, d1);
+    float r0, r1;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+    return mul2(v2, pack2(r0, r1));
+}
 
 template <int C>
 __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, bool valid, int j, int64_t n, int ln,
@@ -220,46 +239,63 @@ __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, boo
     constexpr int EPL = C / 8;
     constexpr int CPG = C / 32;  // channels per GroupNorm group
     const int64_t base = row * C + j * EPL;
+    // the row part as f32x2 pairs (channels 2k, 2k + 1)
+    uint64_t p[EPL / 2];
+#pragma unroll
+    for (int k = 0; k < EPL / 2; ++k) p[k] = pack2(v[2 * k], v[2 * k + 1]);
     if (gn) {
         // GroupNorm, 32 groups: ggml order ((x - mean) * scale, then * gamma,
-        // then + beta); a lane holds EPL / CPG = 4 groups
+        // then + beta); a lane holds EPL / CPG groups of CPG channels
         int b = valid ? __ldg(coords + row).w : 0;  // out-of-range samples are reported by the statistics pass
         b = b < 0 ? 0 : (b >= nsamples ? nsamples - 1 : b);
+        constexpr int PPG = CPG >= 2 ? CPG / 2 : 1;  // pairs per group load
 #pragma unroll
-        for (int gq = 0; gq < EPL / CPG; ++gq) {
-            const float2 ms = gn[b * 32 + (j * EPL) / CPG + gq];
+        for (int k0 = 0; k0 < EPL / 2; k0 += PPG) {
+            // the pair's (or pairs') group statistics; with one channel per
+            // group the two lanes of a pair have their own
+            const float2 m0 = gn[b * 32 + (j * EPL + 2 * k0) / CPG];
+            const float2 m1 = CPG >= 2 ? m0 : gn[b * 32 + (j * EPL + 2 * k0 + 1) / CPG];
+            const uint64_t nm2 = pack2(-m0.x, -m1.x), sc2 = pack2(m0.y, m1.y);
 #pragma unroll
-            for (int k = gq * CPG; k < (gq + 1) * CPG; ++k) {
-                float t = __fmul_rn(v[k] - ms.x, ms.y);
-                if (aff.g) t = __fmul_rn(t, aff.gamma(k));
-                if (aff.b) t = __fadd_rn(t, aff.beta(k));
-                v[k] = t;
+            for (int k = k0; k < k0 + PPG; ++k) {
+                uint64_t t = mul2(add2(p[k], nm2), sc2);
+                if (aff.g) t = mul2(t, aff.gamma2(k));
+                if (aff.b) t = add2(t, aff.beta2(k));
+                p[k] = t;
             }
         }
     } else if (ln) {
-        float s = 0.0f;
+        uint64_t s2 = p[0];
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) s += v[k];
-        const float mean = row_sum8(s) / C;
-        float q = 0.0f;
+        for (int k = 1; k < EPL / 2; ++k) s2 = add2(s2, p[k]);
+        float s0, s1;
+        unpack2(s2, s0, s1);
+        const float mean = row_sum8(s0 + s1) / C;
+        const uint64_t nm2 = pack2(-mean, -mean);
+        uint64_t q2 = 0ull;  // (+0, +0)
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) {
-            const float d = v[k] - mean;
-            q = fmaf(d, d, q);
+        for (int k = 0; k < EPL / 2; ++k) {
+            p[k] = add2(p[k], nm2);  // x - mean
+            q2 = fma2(p[k], p[k], q2);
         }
-        const float scale = 1.0f / sqrtf(row_sum8(q) / C + eps);
+        float q0, q1;
+        unpack2(q2, q0, q1);
+        const float scale = 1.0f / sqrtf(row_sum8(q0 + q1) / C + eps);
+        const uint64_t sc2 = pack2(scale, scale);
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) {
-            float t = __fmul_rn(v[k] - mean, scale);
-            if (aff.g) t = __fmul_rn(t, aff.gamma(k));
-            if (aff.b) t = __fadd_rn(t, aff.beta(k));
-            v[k] = t;
+        for (int k = 0; k < EPL / 2; ++k) {
+            uint64_t t = mul2(p[k], sc2);
+            if (aff.g) t = mul2(t, aff.gamma2(k));
+            if (aff.b) t = add2(t, aff.beta2(k));
+            p[k] = t;
         }
     }
     if (silu) {
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) v[k] = silu_fast(v[k]);
+        for (int k = 0; k < EPL / 2; ++k) p[k] = silu2(p[k]);
     }
+#pragma unroll
+    for (int k = 0; k < EPL / 2; ++k) unpack2(p[k], v[2 * k], v[2 * k + 1]);
     const int64_t plane = n * C;
     if (mode == ACT_FP16) {
         __half h[EPL];
