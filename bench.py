@@ -537,8 +537,11 @@ def run_ours(args):
                        "l2": "flushed between steps (256 MiB write)"},
             "e2e": {"value": W["units"] / (e2e_t * 1e-3), "unit": "voxels/s",
                     "h2d_bytes_per_step": W["h2d_bytes"], "d2h_bytes_per_step": W["d2h_bytes"], "ms_per_step": e2e_t,
-                    "copies": "pinned host buffers; step i+1's input copy and step i's result copy overlap "
-                              "step i's compute (two copy streams, double-buffered device inputs)"},
+                    "copies": ("one msc_level_stack_host call per step (C ABI, pinned host buffers in and out; "
+                               "the library copies on two copy streams ordered against the compute stream by "
+                               "events, two workspaces in flight)") if W.get("e2e_host_step") else
+                              ("pinned host buffers; step i+1's input copy and step i's result copy overlap "
+                               "step i's compute (two copy streams, double-buffered device inputs)")},
             "roofline": W["roofline"](prof),
             "kernel_ms_per_step": {k: v[1] / args.steps for k, v in prof.items()},
             "gpu_launches": int(W["launches"](prof)),
@@ -562,6 +565,8 @@ def e2e_run(W, args, flush, barrier):
     h_ins = h_in if W.get("alternate_inputs") else [h_in]
     comp = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    if W.get("e2e_host_step"):
+        return e2e_run_host(W, args, flush, barrier, h_ins[0], h_out, comp, s_in, s_out)
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_comp = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
@@ -597,6 +602,31 @@ def e2e_run(W, args, flush, barrier):
                 ev_out[bi].record(s_out)
                 if i == k - 1:
                     t1.record(s_out)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / k
+
+    once(args.warmup)
+    return once(args.steps)
+
+
+def e2e_run_host(W, args, flush, barrier, h_in, h_out, comp, s_in, s_out):
+    """End to end through a host-buffer C-ABI call per step (the library
+    copies the inputs in and the result out on the copy streams, ordered
+    against the compute stream by events); two workspaces in flight, so
+    step i+1's input copy and step i's result copy overlap compute."""
+    import torch
+    h_coords, h_x = h_in
+
+    def once(k):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        barrier()
+        t0.record(s_in)
+        for i in range(k):
+            with torch.cuda.stream(comp):
+                flush.fill_(i & 0xff)  # L2 flush between steps
+            W["e2e_host_step"](i, h_coords, h_x, h_out[i % 2], comp, s_in, s_out)
+        t1.record(s_out)
         torch.cuda.synchronize()
         return t0.elapsed_time(t1) / k
 
@@ -873,9 +903,21 @@ def build_stack(args, w, ex, dev, coords, rank, world):
     def cpu_baseline():
         return stack_cpu_baseline(args, w, ex, dev, coords, blocks, blocks_np, convs)
 
+    host_step = None
+    if world == 1 and args.block == "ln" and plan_kind:
+        # one GPU, LayerNorm blocks: the end-to-end run goes through the C ABI
+        # with host buffers (msc_level_stack_host: copies in, make_level,
+        # plan, blocks, copy out), two workspaces in flight
+        wsb = ex.level_stack_host_workspace(nl, c)
+        host_ws = [torch.empty(wsb, dtype=torch.uint8, device=dev) for _ in range(2)]
+
+        def host_step(i, h_coords, h_x, h_y, comp, s_in, s_out):
+            ex.level_stack_host(h_coords, h_x, blocks, h_y, ws=host_ws[i % 2], stream=comp, copy_in=s_in,
+                                copy_out=s_out)
+
     return dict(step=step, reset=reset, after_warmup=after_warmup, e2e_buffers=e2e_buffers, roofline=roofline,
                 tflops=tflops, launches=launches, parity=parity, cpu_baseline=cpu_baseline,
-                halo_events=halo_events, units=n * convs,
+                halo_events=halo_events, units=n * convs, e2e_host_step=host_step,
                 h2d_bytes=int(lcoords.nbytes + lx0.nbytes), d2h_bytes=int(part.n_owned * c * lx0.itemsize),
                 dtype="q8_0 (int8 codes exact on tcgen05, per-32-block fp32 scaling as ggml)",
                 config={"channels": c, "blocks": len(blocks_np), "convs_per_step": convs,

@@ -282,6 +282,27 @@ int msc_res_stack(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const i
                   const float* const* b1, const void* const* blob2, const float* const* b2, void* ws, size_t ws_bytes,
                   void* stream);
 
+/* A level's LayerNorm residual stack from host tensors to host tensors:
+ * copies coords [n][4] and x [n][c] (x_dtype) in, builds the neighbour map
+ * and the tap-order plan, runs the nblocks blocks of msc_res_stack and
+ * copies the result to y_host [n][c] (may be x_host).  Everything is
+ * ordered on `stream` and the call returns without waiting; with
+ * copy_in_stream / copy_out_stream (may be NULL) the copies run there,
+ * ordered against the compute by events, so that consecutive calls on two
+ * workspaces overlap one call's copies with another's compute.  The next
+ * call on the same workspace waits for this call's result copy.  Host
+ * buffers must stay valid until the result copy has completed
+ * (page-locked buffers let the copies run asynchronously).
+ * Workspace: msc_level_stack_host_workspace_bytes(n, c) device bytes.
+ * Replaces: a level's upload, make_level, res_block loop and readback
+ * (src/sparse.cpp:935-952, 238-272, 1118-1121, 1293-1295). */
+size_t msc_level_stack_host_workspace_bytes(int64_t n, int c);
+int msc_level_stack_host(msc_ctx_t ctx, const int32_t* coords_host, const void* x_host, int x_dtype, int64_t n,
+                         int c, int nblocks, const float* const* norm_w, const float* const* norm_b,
+                         const void* const* blob1, const float* const* b1, const void* const* blob2,
+                         const float* const* b2, void* y_host, void* ws, size_t ws_bytes, void* stream,
+                         void* copy_in_stream, void* copy_out_stream);
+
 /* --------------------------------------------------- GroupNorm res block
  * The GroupNorm variant of the residual block, in place:
  *   x = x + conv2(SiLU(GroupNorm_32(conv1(x) + b1))) + b2

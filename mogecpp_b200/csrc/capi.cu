@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -44,6 +45,14 @@ struct msc_context {
     bool prof = false;
     std::vector<Rec> recs;
     std::vector<cudaEvent_t> pool;
+    // msc_level_stack_host, per workspace: events after the input copies,
+    // after the blocks and after the result copy of the last call on it
+    // (the next call on that workspace waits for the last before
+    // overwriting the device copies)
+    struct WsEvents {
+        cudaEvent_t in_done, blocks_done, out_done;
+    };
+    std::unordered_map<const void*, WsEvents> ws_events;
 };
 
 namespace {
@@ -321,6 +330,11 @@ int msc_destroy(msc_ctx_t ctx) {
             cudaEventDestroy(r.b);
         }
         for (auto e : ctx->pool) cudaEventDestroy(e);
+        for (auto& kv : ctx->ws_events) {
+            cudaEventDestroy(kv.second.in_done);
+            cudaEventDestroy(kv.second.blocks_done);
+            cudaEventDestroy(kv.second.out_done);
+        }
         delete ctx;
     });
 }
@@ -685,6 +699,100 @@ int msc_res_stack(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const i
                                                  blob1[i], opt(b1, i), blob2[i], opt(b2, i), ws, ws_bytes, stream);
             if (rc != MSC_OK) fail(rc, "block " + std::to_string(i) + ": " + g_err);
         }
+    });
+}
+
+namespace {
+// Section offsets of the msc_level_stack_host workspace: device coords,
+// features, neighbour map, plan, then scratch shared by the topology, the
+// plan build and the blocks.
+struct StackHostWs {
+    size_t coords, x, nbr, plan, scratch, scratch_bytes, total;
+};
+StackHostWs stack_host_ws(int64_t n, int c, int es) {
+    StackHostWs w{};
+    w.coords = 0;
+    w.x = w.coords + align256(static_cast<size_t>(n) * 16);
+    w.nbr = w.x + align256(static_cast<size_t>(n) * c * es);
+    w.plan = w.nbr + align256(static_cast<size_t>(n) * 27 * 4);
+    w.scratch = w.plan + align256(msc::plan_bytes(n));
+    w.scratch_bytes = std::max({msc::topology_workspace_bytes(n), msc::plan_workspace_bytes(n),
+                                msc_op_workspace_bytes(n, c)});
+    w.total = w.scratch + align256(w.scratch_bytes);
+    return w;
+}
+}  // namespace
+
+size_t msc_level_stack_host_workspace_bytes(int64_t n, int c) {
+    if (n < 0 || c <= 0) return 0;
+    return stack_host_ws(n, c, 4).total;  // sized for fp32 features (fp16 / bf16 fit)
+}
+
+int msc_level_stack_host(msc_ctx_t ctx, const int32_t* coords_host, const void* x_host, int x_dtype, int64_t n,
+                         int c, int nblocks, const float* const* norm_w, const float* const* norm_b,
+                         const void* const* blob1, const float* const* b1, const void* const* blob2,
+                         const float* const* b2, void* y_host, void* ws, size_t ws_bytes, void* stream,
+                         void* copy_in_stream, void* copy_out_stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        need(c > 0 && c % 32 == 0, "channels must be a positive multiple of 32");
+        need(nblocks >= 0, "negative block count");
+        if (n == 0) return;
+        need(coords_host && x_host && y_host && ws, "null pointer");
+        need_aligned(ws, 256, "workspace");
+        const int es = x_dtype == MSC_F32 ? 4 : 2;
+        const StackHostWs L = stack_host_ws(n, c, es);
+        need_ws(ws_bytes, msc_level_stack_host_workspace_bytes(n, c));
+        char* base = static_cast<char*>(ws);
+        auto* coords = reinterpret_cast<int32_t*>(base + L.coords);
+        void* x = base + L.x;
+        auto* nbr = reinterpret_cast<int32_t*>(base + L.nbr);
+        void* plan = base + L.plan;
+        void* scratch = base + L.scratch;
+        const size_t xbytes = static_cast<size_t>(n) * c * es;
+        cudaStream_t st = S(stream);
+        cudaStream_t in = copy_in_stream ? S(copy_in_stream) : st;
+        cudaStream_t out = copy_out_stream ? S(copy_out_stream) : st;
+        msc_context::WsEvents ev{};
+        bool fresh = false;
+        {
+            std::lock_guard<std::mutex> lk(ctx->mu);
+            auto it = ctx->ws_events.find(ws);
+            if (it == ctx->ws_events.end()) {
+                msc_context::WsEvents e{};
+                cuda_ok(cudaEventCreateWithFlags(&e.in_done, cudaEventDisableTiming), "event create");
+                cuda_ok(cudaEventCreateWithFlags(&e.blocks_done, cudaEventDisableTiming), "event create");
+                cuda_ok(cudaEventCreateWithFlags(&e.out_done, cudaEventDisableTiming), "event create");
+                it = ctx->ws_events.emplace(ws, e).first;
+                fresh = true;
+            }
+            ev = it->second;
+        }
+        // inputs: after the previous call on this workspace has copied its result out
+        if (!fresh) cuda_ok(cudaStreamWaitEvent(in, ev.out_done, 0), "wait previous result copy");
+        cuda_ok(cudaMemcpyAsync(coords, coords_host, static_cast<size_t>(n) * 16, cudaMemcpyHostToDevice, in),
+                "coords copy");
+        cuda_ok(cudaMemcpyAsync(x, x_host, xbytes, cudaMemcpyHostToDevice, in), "features copy");
+        if (in != st) {
+            cuda_ok(cudaEventRecord(ev.in_done, in), "event record");
+            cuda_ok(cudaStreamWaitEvent(st, ev.in_done, 0), "wait inputs");
+        }
+        int rc = msc_make_level(ctx, coords, n, nbr, scratch, L.scratch_bytes, st);
+        if (rc != MSC_OK) fail(rc, "make_level: " + g_err);
+        rc = msc_conv_plan_build(ctx, coords, n, nbr, MSC_PLAN_TAP_ORDER, plan, msc::plan_bytes(n), scratch,
+                                 L.scratch_bytes, st);
+        if (rc != MSC_OK) fail(rc, "plan: " + g_err);
+        rc = msc_res_stack(ctx, x, x_dtype, n, c, nbr, plan, nblocks, norm_w, norm_b, blob1, b1, blob2, b2, scratch,
+                           L.scratch_bytes, st);
+        if (rc != MSC_OK) fail(rc, g_err);
+        if (out != st) {
+            cuda_ok(cudaEventRecord(ev.blocks_done, st), "event record");
+            cuda_ok(cudaStreamWaitEvent(out, ev.blocks_done, 0), "wait blocks");
+        }
+        cuda_ok(cudaMemcpyAsync(y_host, x, xbytes, cudaMemcpyDeviceToHost, out), "result copy");
+        cuda_ok(cudaEventRecord(ev.out_done, out), "event record");
     });
 }
 

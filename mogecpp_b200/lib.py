@@ -48,6 +48,9 @@ SIGNATURES = {
                                           _vp]),
     "msc_res_block_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _sz, _vp]),
+    "msc_level_stack_host_workspace_bytes": (_sz, [_i64, _i32]),
+    "msc_level_stack_host": (C.c_int, [_vp, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                       _sz, _vp, _vp, _vp]),
     "msc_res_stack": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                 _vp]),
     "msc_gn_stats_doubles": (_i64, [_i32]),

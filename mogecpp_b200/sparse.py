@@ -305,6 +305,38 @@ class SparseCudaExecutor:
                                        _p(ws), wsb, _stream()))
         return x
 
+    def level_stack_host(self, coords_host, x_host, blocks: list, y_host, ws=None, stream=None, copy_in=None,
+                         copy_out=None):
+        """A level's LayerNorm residual stack from host tensors to host
+        tensors (``msc_level_stack_host``): coords [n, 4] int32 and x [n, c]
+        in, the result into y_host (may be x_host).  Asynchronous on
+        ``stream`` (default: the current stream), copies on copy_in /
+        copy_out when given; ws is a device uint8 workspace of
+        ``level_stack_host_workspace(n, c)`` bytes (one per call in flight).
+        Returns ws."""
+        n, c = x_host.shape
+        k = len(blocks)
+        wsb = self.lib.msc_level_stack_host_workspace_bytes(n, c)
+        if ws is None:
+            ws = torch.empty(wsb, dtype=torch.uint8, device=torch.device("cuda", self.device))
+
+        def arr(key, attr=None):
+            vals = [b.get(key) for b in blocks]
+            if all(v is None for v in vals):
+                return None
+            ptrs = [None if v is None else (getattr(v, attr) if attr else v).data_ptr() for v in vals]
+            return (C.c_void_p * k)(*ptrs)
+        st = stream.cuda_stream if stream is not None else _stream()
+        L.check(self.lib.msc_level_stack_host(self.ctx, _p(coords_host), _p(x_host), _DT[x_host.dtype], n, c, k,
+                                              arr("norm_w"), arr("norm_b"), arr("w1", "blob"), arr("b1"),
+                                              arr("w2", "blob"), arr("b2"), _p(y_host), _p(ws), ws.numel(), st,
+                                              copy_in.cuda_stream if copy_in is not None else None,
+                                              copy_out.cuda_stream if copy_out is not None else None))
+        return ws
+
+    def level_stack_host_workspace(self, n: int, c: int) -> int:
+        return self.lib.msc_level_stack_host_workspace_bytes(n, c)
+
     def res_block_gn(self, x, nbr, coords, nsamples: int, blk: dict, eps: float = 1e-5, plan=None,
                      n_stat: int | None = None, allreduce=None):
         """In place on x: x + conv2(SiLU(GroupNorm_32(conv1(x) + b1))) + b2.

@@ -174,3 +174,36 @@ def test_res_stack_other_formats_run_block_by_block(ex, oracle):
         ex.res_block(b, dev(nbr), blk)
     ex.check()
     np.testing.assert_array_equal(host(a), host(b))
+
+
+@pytest.mark.parametrize("pinned,streams", [(True, True), (True, False), (False, False)])
+def test_level_stack_host_equals_the_device_calls(ex, oracle, pinned, streams):
+    """msc_level_stack_host (host coords and features in, host result out:
+    copies, make_level, plan and blocks inside one C-ABI call) gives the bits
+    of make_level + conv_plan + res_stack on device tensors; three calls in
+    a row on two workspaces (the pipelined use) each give the same result."""
+    coords = synth.small_coords(180, extent=26, grid=32)
+    n = coords.shape[0]
+    x0 = synth.features(181, n, 128, np.float16)
+    raws = [raw_block(190 + 10 * b, 128) for b in range(2)]
+    blks = [make_block(ex, oracle, r, "q8_0", 128) for r in raws]
+    cd = dev(coords)
+    nbrd = ex.make_level(cd)
+    ref = dev(x0)
+    ex.res_stack(ref, nbrd, blks, plan=ex.conv_plan(cd, nbrd))
+    ex.check()
+    h_c = torch.from_numpy(coords)
+    h_x = torch.from_numpy(x0)
+    outs = [torch.empty((n, 128), dtype=torch.float16) for _ in range(3)]
+    if pinned:
+        h_c, h_x = h_c.pin_memory(), h_x.pin_memory()
+        outs = [o.pin_memory() for o in outs]
+    wsb = ex.level_stack_host_workspace(n, 128)
+    ws = [torch.empty(wsb, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    s_in, s_out = (torch.cuda.Stream(), torch.cuda.Stream()) if streams else (None, None)
+    for i in range(3):
+        ex.level_stack_host(h_c, h_x, blks, outs[i], ws=ws[i % 2], copy_in=s_in, copy_out=s_out)
+    torch.cuda.synchronize()
+    ex.check()
+    for o in outs:
+        np.testing.assert_array_equal(o.numpy(), host(ref))
