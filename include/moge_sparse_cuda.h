@@ -265,6 +265,29 @@ int msc_sparse_conv_planned(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n
                             const void* plan, const void* blob, const float* bias, void* y, int y_dtype, void* ws,
                             size_t ws_bytes, void* stream);
 
+/* Prologue and epilogue of a fused sparse conv:
+ *   y = [SiLU](W * gather([SiLU]([LayerNorm](x))) + bias) [+ residual]
+ * The prologue runs in the operand preparation of x, the epilogue in the
+ * conv's tile epilogue (no extra passes over memory). */
+typedef struct {
+    int layer_norm;           /* 1: LayerNorm over each input row (ggml norm, eps), then the affine */
+    const float* norm_w;      /* [cin] gamma (may be NULL) */
+    const float* norm_b;      /* [cin] beta (may be NULL) */
+    float eps;
+    int silu_in;              /* 1: SiLU on the (normalised) input */
+    int silu_out;             /* 1: SiLU on conv + bias */
+    const void* residual;     /* [n][cout], added last (may be NULL) */
+    int residual_dtype;
+} msc_conv_fusion;
+
+/* msc_sparse_conv_planned with a fused prologue / epilogue (fusion may be
+ * NULL: none).  Workspace: msc_op_workspace_bytes(n, max(cin, cout)).
+ * Replaces: the layer_norm -> silu -> sparse_conv -> silu / + skip chains of
+ * res_block (src/sparse.cpp:629-642), one conv at a time. */
+int msc_sparse_conv_fused(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                          const void* plan, const msc_conv_fusion* fusion, const void* blob, const float* bias,
+                          void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream);
+
 /* msc_res_block with an optional plan, same rules as msc_sparse_conv_planned. */
 int msc_res_block_planned(msc_ctx_t ctx, void* x, int x_dtype, int64_t n, int c, const int32_t* nbr,
                           const void* plan, const float* norm_w, const float* norm_b, const void* blob1,

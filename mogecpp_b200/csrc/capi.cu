@@ -607,6 +607,38 @@ int msc_octant_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n_in, int
     });
 }
 
+int msc_sparse_conv_fused(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
+                          const void* plan, const msc_conv_fusion* fusion, const void* blob, const float* bias,
+                          void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream) {
+    return guard([&] {
+        need_ctx(ctx);
+        need_dtype(x_dtype, "x");
+        need_dtype(y_dtype, "y");
+        const auto b = blob_info(ctx, blob);
+        check_conv_shape(b, cin, 27);
+        need(n >= 0 && n < (int64_t(1) << 31) / 27, "voxel count out of range");
+        if (n == 0) return;
+        const msc_conv_fusion f = fusion ? *fusion : msc_conv_fusion{};
+        need(!f.layer_norm || f.eps > 0.0f, "LayerNorm eps must be positive");
+        if (f.residual) {
+            need_dtype(f.residual_dtype, "residual");
+            need_aligned(f.residual, 16, "residual");
+        }
+        const PlanUse pl = use_plan(ctx, plan, n);
+        need(x && nbr && y && ws, "null pointer");
+        need_aligned(x, 16, "x");
+        need_aligned(y, 16, "y");
+        need_aligned(ws, 256, "workspace");
+        const int mode = act_mode(b.wtype, x_dtype, b.cin);
+        need_ws(ws_bytes, msc::act_bytes(mode, n, cin));
+        cuda_ok(act_prepare(ctx, x, x_dtype, n, cin, f.layer_norm ? 1 : 0, f.layer_norm ? f.norm_w : nullptr,
+                            f.layer_norm ? f.norm_b : nullptr, f.eps, f.silu_in ? 1 : 0, mode, ws, S(stream)),
+                "activation prepare");
+        run_conv(ctx, ws, mode, n, cin, nbr, b, blob, bias, f.silu_out ? 1 : 0, f.residual,
+                 f.residual ? f.residual_dtype : 0, y, y_dtype, S(stream), pl);
+    });
+}
+
 int msc_sparse_conv(msc_ctx_t ctx, const void* x, int x_dtype, int64_t n, int cin, const int32_t* nbr,
                     const void* blob, const float* bias, void* y, int y_dtype, void* ws, size_t ws_bytes,
                     void* stream) {

@@ -46,6 +46,8 @@ SIGNATURES = {
                                   _sz, _vp]),
     "msc_sparse_conv_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz,
                                           _vp]),
+    "msc_sparse_conv_fused": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz,
+                                        _vp]),
     "msc_res_block_planned": (C.c_int, [_vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _sz, _vp]),
     "msc_level_stack_host_workspace_bytes": (_sz, [_i64, _i32]),
@@ -100,6 +102,12 @@ class SparseConfig(C.Structure):
                 ("encoder_blocks", C.c_int * MAX_LEVELS), ("decoder_blocks", C.c_int * MAX_LEVELS),
                 ("downsample_factors", C.c_int * MAX_LEVELS), ("bottleneck_blocks", C.c_int),
                 ("encoder_downsample", C.c_int), ("depth_resolution", C.c_float)]
+
+
+class ConvFusion(C.Structure):
+    """msc_conv_fusion: prologue (LayerNorm, SiLU) and epilogue (SiLU, residual) of a fused conv."""
+    _fields_ = [("layer_norm", C.c_int), ("norm_w", C.c_void_p), ("norm_b", C.c_void_p), ("eps", C.c_float),
+                ("silu_in", C.c_int), ("silu_out", C.c_int), ("residual", C.c_void_p), ("residual_dtype", C.c_int)]
 
 
 class SlabDesc(C.Structure):

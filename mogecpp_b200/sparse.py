@@ -229,6 +229,21 @@ class SparseCudaExecutor:
                                                  _stream()))
         return y
 
+    def sparse_conv_fused(self, x, nbr, w: PreparedWeight, bias=None, out_dtype=torch.float32, plan=None,
+                          norm_w=None, norm_b=None, layer_norm=False, eps=1e-6, silu_in=False, silu_out=False,
+                          residual=None):
+        """y = [SiLU](W * gather([SiLU]([LayerNorm](x))) + bias) [+ residual]
+        in one conv (msc_sparse_conv_fused)."""
+        n, cin = x.shape
+        y = torch.empty((n, w.cout), dtype=out_dtype, device=x.device)
+        wsb = self.lib.msc_op_workspace_bytes(n, max(cin, w.cout))
+        ws = self.workspace(wsb)
+        f = L.ConvFusion(1 if layer_norm else 0, _p(norm_w), _p(norm_b), eps, 1 if silu_in else 0,
+                         1 if silu_out else 0, _p(residual), _DT[residual.dtype] if residual is not None else 0)
+        L.check(self.lib.msc_sparse_conv_fused(self.ctx, _p(x), _DT[x.dtype], n, cin, _p(nbr), _p(plan), C.byref(f),
+                                               _p(w.blob), _p(bias), _p(y), _DT[out_dtype], _p(ws), wsb, _stream()))
+        return y
+
     def octant_maps(self, coords: torch.Tensor, tr: "Transition"):
         """(down_nbr [np][27], up_nbr [nfine][27]) of a synced stride-2
         transition: the maps of the octant-weighted strided conv and of its

@@ -126,3 +126,40 @@ def test_workspace_too_small_rejected(ex, oracle):
                                 C.c_void_p(pw.blob.data_ptr()), None, C.c_void_p(y.data_ptr()), 0,
                                 C.c_void_p(ws.data_ptr()), 1024, None)
     assert rc == -5 and "workspace" in ex.lib.msc_last_error().decode()
+
+
+@pytest.mark.parametrize("tag,xdt", [("q8_0", torch.float16), ("f32", torch.float32)])
+@pytest.mark.parametrize("flags", [(True, True, True, True), (False, True, False, False), (True, False, True, False),
+                                   (False, False, False, True)])
+def test_fused_conv_matches_oracle_composition(ex, oracle, tag, xdt, flags):
+    """msc_sparse_conv_fused: [SiLU](W * gather([SiLU]([LayerNorm](x))) + b)
+    [+ residual] against the oracle's layer_norm, silu and sparse_conv run
+    one after the other."""
+    ln, silu_in, silu_out, res = flags
+    coords = synth.small_coords(200, extent=22, grid=32)
+    n = coords.shape[0]
+    nbr = oracle.make_level(coords)
+    rng = np.random.default_rng(201)
+    x = synth.features(202, n, 128)
+    gamma = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(128)).astype(np.float32)
+    w = synth.conv_weight(203, 128, 128)
+    b = (0.05 * rng.standard_normal(128)).astype(np.float32)
+    r = synth.features(204, n, 128)
+    xd = dev(x).to(xdt)
+    xin = xd.float().cpu().numpy()
+    pw = ex.prepare_weight(weight_tensor(oracle, w, tag), tag, 128, 128, 27)
+    rd = dev(r).to(xdt) if res else None
+    y = ex.sparse_conv_fused(xd, dev(nbr), pw, dev(b), plan=ex.conv_plan(dev(coords), dev(nbr)),
+                             norm_w=dev(gamma), norm_b=dev(beta), layer_norm=ln, silu_in=silu_in,
+                             silu_out=silu_out, residual=rd)
+    ex.check()
+    h = oracle.layer_norm(xin, gamma, beta, 1e-6) if ln else xin
+    if silu_in:
+        h = oracle.silu(h)
+    ref = oracle.sparse_conv(h, nbr, w, WT[tag], b)
+    if silu_out:
+        ref = oracle.silu(ref)
+    if res:
+        ref = ref + rd.float().cpu().numpy()
+    tol_ok(host(y), ref, fp32=(tag == "f32" and xdt == torch.float32))
