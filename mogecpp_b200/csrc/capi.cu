@@ -221,6 +221,7 @@ void run_conv(msc_ctx_t ctx, const void* planes, int mode, int64_t n, int cin, c
     a.tile_rows = pu.tiles.rows;
     a.tile_nbr = nbr ? pu.tiles.nbr : nullptr;
     a.tile_mask = pu.tiles.mask;
+    a.tile_sched = nbr ? pu.tiles.sched : nullptr;
     ProfScope ps(ctx, family ? family : (nbr ? "conv_tc" : "linear_tc"), st);
     cuda_ok(msc::launch_conv(a, st), "conv launch");
 }

@@ -72,6 +72,7 @@ struct ConvArgs {
     const int32_t* tile_rows;
     const int32_t* tile_nbr;
     const uint32_t* tile_mask;
+    const int32_t* tile_sched;  // plan: tiles by descending cost, dealt to the CTAs in a snake (NULL: round-robin)
     int cin;
     const int32_t* nbr;      // [rows][27] indexed by output row; null => linear (row i reads row i)
     const void* blob;        // prepared weights

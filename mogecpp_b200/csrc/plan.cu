@@ -64,16 +64,21 @@ __global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, int n_in, T
 
 // One block per 128-row tile, 16 warps of 8 rows, lane t = tap t: each
 // row's voxel, its neighbour list with -1 for missing taps (8 rows of loads
-// in flight per warp), and the tile's tap mask (ballots OR-ed in shared
-// memory, one plain store per tile).
+// in flight per warp), the tile's tap mask (ballots OR-ed in shared memory,
+// one plain store per tile) and its drain cost: the taps of each 32-row
+// quarter summed over the quarters (a conv drain warp reads the tile's
+// accumulators for the taps its quarter uses), the key of the schedule.
 constexpr int kTileListWarps = 16;
 __global__ void __launch_bounds__(32 * kTileListWarps)
-    tile_lists_kernel(const int* __restrict__ order, const int* __restrict__ nbr, int n, int n_in, PlanTiles T) {
+    tile_lists_kernel(const int* __restrict__ order, const int* __restrict__ nbr, int n, int n_in, PlanTiles T,
+                      uint32_t* __restrict__ cost, int* __restrict__ tile_id) {
     constexpr int RPW = kPlanTileRows / kTileListWarps;
-    __shared__ uint32_t smask;
+    constexpr int kQuarterWarps = 32 / RPW;  // warps per 32-row quarter
+    __shared__ uint32_t smask, qmask[kPlanTileRows / 32];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) smask = 0u;
+    if (threadIdx.x < kPlanTileRows / 32) qmask[threadIdx.x] = 0u;
     __syncthreads();
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kPlanTileRows + warp * RPW;
     int v[RPW], j[RPW];
@@ -91,10 +96,20 @@ __global__ void __launch_bounds__(32 * kTileListWarps)
     if (lane == 0) {
 #pragma unroll
         for (int u = 0; u < RPW; ++u) T.rows[r0 + u] = v[u];
-        if (m) atomicOr(&smask, m);
+        if (m) {
+            atomicOr(&smask, m);
+            atomicOr(&qmask[warp / kQuarterWarps], m);
+        }
     }
     __syncthreads();
-    if (threadIdx.x == 0) T.mask[blockIdx.x] = smask;
+    if (threadIdx.x == 0) {
+        T.mask[blockIdx.x] = smask;
+        uint32_t c = 0;
+#pragma unroll
+        for (int q = 0; q < kPlanTileRows / 32; ++q) c += __popc(qmask[q]);
+        cost[blockIdx.x] = c;
+        tile_id[blockIdx.x] = blockIdx.x;
+    }
 }
 
 __global__ void plan_header_kernel(PlanHeader* h, int64_t n) {
@@ -105,20 +120,26 @@ __global__ void plan_header_kernel(PlanHeader* h, int64_t n) {
 
 size_t align256(size_t v) { return plan_align(v); }
 
+int64_t tiles_of(int64_t n) { return (n + kPlanTileRows - 1) / kPlanTileRows; }
+
+// Scratch of the two sorts: the voxels by tap key (27 bits) and the tiles by
+// descending cost (7 bits).
 size_t sort_temp_bytes(int64_t n) {
-    size_t b32 = 0;
-    cub::DeviceRadixSort::SortPairs(nullptr, b32, static_cast<const uint32_t*>(nullptr),
+    size_t b_vox = 0, b_tile = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, b_vox, static_cast<const uint32_t*>(nullptr),
                                     static_cast<uint32_t*>(nullptr), static_cast<const int*>(nullptr),
                                     static_cast<int*>(nullptr), static_cast<int>(n), 0, 27);
-    return b32;
+    cub::DeviceRadixSort::SortPairsDescending(nullptr, b_tile, static_cast<const uint32_t*>(nullptr),
+                                              static_cast<uint32_t*>(nullptr), static_cast<const int*>(nullptr),
+                                              static_cast<int*>(nullptr), static_cast<int>(tiles_of(n)), 0, 7);
+    return b_vox > b_tile ? b_vox : b_tile;
 }
-
-int64_t tiles_of(int64_t n) { return (n + kPlanTileRows - 1) / kPlanTileRows; }
 
 }  // namespace
 
 // Plan layout: PlanHeader | order [n] | tile rows [n_pad] | tile neighbour
-// lists [n_pad][27] | tile masks [n_pad / 128], each section 256-byte aligned.
+// lists [n_pad][27] | tile masks [n_pad / 128] | tile schedule [n_pad / 128],
+// each section 256-byte aligned.
 PlanTiles plan_tiles(uint8_t* plan, int64_t n) {
     const int64_t np = tiles_of(n) * kPlanTileRows;
     uint8_t* p = plan + align256(sizeof(PlanHeader));
@@ -130,13 +151,15 @@ PlanTiles plan_tiles(uint8_t* plan, int64_t n) {
     t.nbr = reinterpret_cast<int*>(p);
     p += align256(static_cast<size_t>(np) * 27 * 4);
     t.mask = reinterpret_cast<uint32_t*>(p);
+    p += align256(static_cast<size_t>(tiles_of(n)) * 4);
+    t.sched = reinterpret_cast<int*>(p);
     return t;
 }
 
 size_t plan_bytes(int64_t n) {
     const int64_t np = tiles_of(n) * kPlanTileRows;
     return align256(sizeof(PlanHeader)) + align256(static_cast<size_t>(n) * 4) + align256(static_cast<size_t>(np) * 4) +
-           align256(static_cast<size_t>(np) * 27 * 4) + align256(static_cast<size_t>(tiles_of(n)) * 4);
+           align256(static_cast<size_t>(np) * 27 * 4) + 2 * align256(static_cast<size_t>(tiles_of(n)) * 4);
 }
 
 size_t plan_workspace_bytes(int64_t n) {
@@ -162,7 +185,15 @@ cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, int64_t n_in, void*
     mask_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(nbr, ni, nin, tb, k_in, vals_in);
     cudaError_t e = cub::DeviceRadixSort::SortPairs(w, temp_bytes, k_in, k_out, vals_in, T.order, ni, 0, 27, st);
     if (e != cudaSuccess) return e;
-    tile_lists_kernel<<<static_cast<unsigned>(tiles_of(n)), 32 * kTileListWarps, 0, st>>>(T.order, nbr, ni, nin, T);
+    // the key and value buffers of the voxel sort are free again: tile costs
+    // and ids, then the tiles sorted by descending cost (stable: equal costs
+    // keep the tap order)
+    const int nt = static_cast<int>(tiles_of(n));
+    tile_lists_kernel<<<static_cast<unsigned>(nt), 32 * kTileListWarps, 0, st>>>(T.order, nbr, ni, nin, T, k_in,
+                                                                                  vals_in);
+    size_t tile_temp = temp_bytes;
+    e = cub::DeviceRadixSort::SortPairsDescending(w, tile_temp, k_in, k_out, vals_in, T.sched, nt, 0, 7, st);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -350,7 +350,7 @@ int msc_slab_res_block(msc_slab_t s, const float* norm_w, const float* norm_b, c
                 a.n_in = n;
                 a.n = rows;
                 const PlanTiles T = plan_tiles(static_cast<uint8_t*>(const_cast<void*>(plan)), rows);
-                a.perm = T.order, a.tile_rows = T.rows, a.tile_nbr = T.nbr, a.tile_mask = T.mask;
+                a.perm = T.order, a.tile_rows = T.rows, a.tile_nbr = T.nbr, a.tile_mask = T.mask, a.tile_sched = T.sched;
                 a.cin = c, a.nbr = s->nbr, a.blob = blob, a.wplanes = 1, a.cout = c, a.ntaps = 27;
                 a.bias = bias;
                 a.status = status;

@@ -47,7 +47,9 @@ def test_size_queries_are_host_only():
     assert lib.msc_op_workspace_bytes(1000, 128) >= 1000 * 128 * 8
     # conv plan: header + order + tile rows + tile neighbour lists + tile masks
     npad = 8 * 128
-    assert lib.msc_conv_plan_bytes(1000) == r256(16) + r256(4000) + r256(4 * npad) + r256(4 * 27 * npad) + r256(4 * 8)
+    # header | order | tile rows | tile neighbour lists | tile masks | tile schedule
+    assert lib.msc_conv_plan_bytes(1000) == (r256(16) + r256(4000) + r256(4 * npad) + r256(4 * 27 * npad) +
+                                             2 * r256(4 * 8))
     assert lib.msc_conv_plan_bytes(-1) == 0
     assert lib.msc_conv_plan_workspace_bytes(1000) >= 1000 * 12
     # GroupNorm statistics: 32 sums, 1 count, 32 squared deviations per sample

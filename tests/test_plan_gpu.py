@@ -28,7 +28,8 @@ def _align(v):
 def parse_plan(buf, n):
     """Sections of a plan buffer (layout of mogecpp_b200/csrc/plan.h):
     header {magic, reserved, n}, order [n], tile rows [n_pad], tile
-    neighbour lists [n_pad][27], tile masks [n_pad / 128]."""
+    neighbour lists [n_pad][27], tile masks [n_pad / 128], tile schedule
+    [n_pad / 128]."""
     b = buf.cpu().numpy()
     magic = int(b[:4].view(np.uint32)[0])
     hn = int(b[8:16].view(np.int64)[0])
@@ -42,7 +43,9 @@ def parse_plan(buf, n):
     tnbr = b[off:off + 4 * 27 * npad].view(np.int32).reshape(npad, 27)
     off += _align(4 * 27 * npad)
     mask = b[off:off + 4 * ntiles].view(np.uint32)
-    return dict(magic=magic, n=hn, order=order, rows=rows, nbr=tnbr, mask=mask)
+    off += _align(4 * ntiles)
+    sched = b[off:off + 4 * ntiles].view(np.int32)
+    return dict(magic=magic, n=hn, order=order, rows=rows, nbr=tnbr, mask=mask, sched=sched)
 
 
 def dense_offset_cube(side=20, offset=(5, 3, 6)):
@@ -114,6 +117,17 @@ def test_tap_order_tile_lists(ex, oracle):
     p = parse_plan(plan, coords.shape[0])
     assert p["magic"] == 0x4E4C5053 and p["n"] == coords.shape[0]
     check_tiles(p, nbr)
+
+
+def test_tile_schedule_sorts_tiles_by_drain_cost(ex, oracle):
+    """The schedule lists every tile once, by descending drain cost (the taps
+    of each 32-row quarter, summed), ties in tile order."""
+    coords = synth.small_coords(33, extent=34, grid=48)
+    nbr, plan = _level(ex, oracle, coords)
+    p = parse_plan(plan, coords.shape[0])
+    ntiles = p["mask"].shape[0]
+    q = (p["nbr"] >= 0).reshape(ntiles, 4, 32, 27).any(2).sum((1, 2))
+    np.testing.assert_array_equal(p["sched"], np.argsort(-q, kind="stable"))
 
 
 @pytest.mark.parametrize("tag", ["f32", "f16", "q8_0"])
