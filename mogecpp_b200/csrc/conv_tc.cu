@@ -148,7 +148,7 @@ __device__ __forceinline__ int64_t tile_row(const ConvArgs& a, int64_t idx) {
 }
 
 // The k-th tile of this CTA, or -1 past the end.  With a plan's schedule
-// (tiles by descending drain cost) the tiles are dealt out in a snake,
+// (tiles by descending cost) the tiles are dealt out in a snake,
 // CTAs 0..G-1 then G-1..0 and so on, which evens out the CTAs' loads
 // (round-robin over tiles in tap order left the busiest CTA 5 % above the
 // mean at 3.1M voxels and 18 % at 400k); without one, round-robin.

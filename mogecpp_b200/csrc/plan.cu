@@ -65,9 +65,12 @@ __global__ void mask_keys_kernel(const int* __restrict__ nbr, int n, int n_in, T
 // One block per 128-row tile, 16 warps of 8 rows, lane t = tap t: each
 // row's voxel, its neighbour list with -1 for missing taps (8 rows of loads
 // in flight per warp), the tile's tap mask (ballots OR-ed in shared memory,
-// one plain store per tile) and its drain cost: the taps of each 32-row
-// quarter summed over the quarters (a conv drain warp reads the tile's
-// accumulators for the taps its quarter uses), the key of the schedule.
+// one plain store per tile) and its cost, the key of the schedule:
+// 4 x the tile's taps (each tap holds an accumulator slot of the whole CTA)
+// + the taps of each 32-row quarter summed (a drain warp reads the slot
+// only for the taps its quarter uses).  Balancing on this sum keeps the
+// busiest CTA within a few per cent of the mean whether the slot or the
+// quarters dominate.
 constexpr int kTileListWarps = 16;
 __global__ void __launch_bounds__(32 * kTileListWarps)
     tile_lists_kernel(const int* __restrict__ order, const int* __restrict__ nbr, int n, int n_in, PlanTiles T,
@@ -104,10 +107,10 @@ __global__ void __launch_bounds__(32 * kTileListWarps)
     __syncthreads();
     if (threadIdx.x == 0) {
         T.mask[blockIdx.x] = smask;
-        uint32_t c = 0;
+        uint32_t c = 4u * __popc(smask);
 #pragma unroll
         for (int q = 0; q < kPlanTileRows / 32; ++q) c += __popc(qmask[q]);
-        cost[blockIdx.x] = c;
+        cost[blockIdx.x] = c;  // <= 216: 8 bits
         tile_id[blockIdx.x] = blockIdx.x;
     }
 }
@@ -123,7 +126,7 @@ size_t align256(size_t v) { return plan_align(v); }
 int64_t tiles_of(int64_t n) { return (n + kPlanTileRows - 1) / kPlanTileRows; }
 
 // Scratch of the two sorts: the voxels by tap key (27 bits) and the tiles by
-// descending cost (7 bits).
+// descending cost (8 bits).
 size_t sort_temp_bytes(int64_t n) {
     size_t b_vox = 0, b_tile = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, b_vox, static_cast<const uint32_t*>(nullptr),
@@ -131,7 +134,7 @@ size_t sort_temp_bytes(int64_t n) {
                                     static_cast<int*>(nullptr), static_cast<int>(n), 0, 27);
     cub::DeviceRadixSort::SortPairsDescending(nullptr, b_tile, static_cast<const uint32_t*>(nullptr),
                                               static_cast<uint32_t*>(nullptr), static_cast<const int*>(nullptr),
-                                              static_cast<int*>(nullptr), static_cast<int>(tiles_of(n)), 0, 7);
+                                              static_cast<int*>(nullptr), static_cast<int>(tiles_of(n)), 0, 8);
     return b_vox > b_tile ? b_vox : b_tile;
 }
 
@@ -192,7 +195,7 @@ cudaError_t launch_plan_build(const int32_t* nbr, int64_t n, int64_t n_in, void*
     tile_lists_kernel<<<static_cast<unsigned>(nt), 32 * kTileListWarps, 0, st>>>(T.order, nbr, ni, nin, T, k_in,
                                                                                   vals_in);
     size_t tile_temp = temp_bytes;
-    e = cub::DeviceRadixSort::SortPairsDescending(w, tile_temp, k_in, k_out, vals_in, T.sched, nt, 0, 7, st);
+    e = cub::DeviceRadixSort::SortPairsDescending(w, tile_temp, k_in, k_out, vals_in, T.sched, nt, 0, 8, st);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

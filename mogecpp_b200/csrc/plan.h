@@ -29,7 +29,7 @@ struct PlanTiles {
     int* rows;        // [n_pad] voxel per tile row, -1 past n
     int* nbr;         // [n_pad][27] neighbour lists, -1 = missing
     uint32_t* mask;   // [n_pad / 128] tap mask of each tile
-    int* sched;       // [n_pad / 128] tiles by descending drain cost (the conv deals them out in a snake)
+    int* sched;       // [n_pad / 128] tiles by descending cost (the conv deals them out in a snake)
 };
 PlanTiles plan_tiles(uint8_t* plan, int64_t n);
 

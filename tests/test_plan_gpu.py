@@ -119,15 +119,16 @@ def test_tap_order_tile_lists(ex, oracle):
     check_tiles(p, nbr)
 
 
-def test_tile_schedule_sorts_tiles_by_drain_cost(ex, oracle):
-    """The schedule lists every tile once, by descending drain cost (the taps
-    of each 32-row quarter, summed), ties in tile order."""
+def test_tile_schedule_sorts_tiles_by_cost(ex, oracle):
+    """The schedule lists every tile once, by descending cost (4 x the tile's
+    taps + the taps of each 32-row quarter, summed), ties in tile order."""
     coords = synth.small_coords(33, extent=34, grid=48)
     nbr, plan = _level(ex, oracle, coords)
     p = parse_plan(plan, coords.shape[0])
     ntiles = p["mask"].shape[0]
-    q = (p["nbr"] >= 0).reshape(ntiles, 4, 32, 27).any(2).sum((1, 2))
-    np.testing.assert_array_equal(p["sched"], np.argsort(-q, kind="stable"))
+    v = (p["nbr"] >= 0).reshape(ntiles, 4, 32, 27)
+    cost = 4 * v.any((1, 2)).sum(1) + v.any(2).sum((1, 2))
+    np.testing.assert_array_equal(p["sched"], np.argsort(-cost, kind="stable"))
 
 
 @pytest.mark.parametrize("tag", ["f32", "f16", "q8_0"])
