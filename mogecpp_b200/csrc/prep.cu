@@ -214,24 +214,6 @@ struct Affine {
     __device__ __forceinline__ uint64_t beta2(int k) const { return reinterpret_cast<const uint64_t*>(b)[k]; }
 };
 
-// SiLU of two lanes, v / (1 + 2^(-v log2 e)), with the PTX approximations
-// ex2.approx.ftz and rcp.approx.ftz (relative error ~1e-6 over the range
-// that matters; v -> -inf gives -0, v -> +inf gives v) and packed multiplies.
-__device__ __forceinline__ uint64_t silu2(uint64_t v2) {
-    constexpr float kLog2e = 1.4426950408889634f;
-    float a0, a1;
-    unpack2(mul2(v2, pack2(-kLog2e, -kLog2e)), a0, a1);
-    float e0, e1;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
-    float d0, d1;
-    unpack2(add2(pack2(e0, e1), pack2(1.0f, 1.0f)), d0, d1);
-    float r0, r1;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
-    return mul2(v2, pack2(r0, r1));
-}
-
 template <int C>
 __device__ __forceinline__ void prepare_row8(float (&v)[C / 8], int64_t row, bool valid, int j, int64_t n, int ln,
                                              const Affine<C>& aff, float eps, int silu, int mode,
