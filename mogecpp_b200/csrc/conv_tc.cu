@@ -49,9 +49,10 @@
 //               own in flight, so the fence does not wait on them).
 // Pipelines (mbarriers): smem stages gathered/full/empty, TMEM accumulator slots
 // acc_full/acc_empty (NACC rotating slots), per-tile tile_ready/tile_free
-// (double-buffered neighbour lists).  Taps are visited in a per-tile rotated
-// order.  Every wait is bounded; a wait that runs out sets MSC_DEV_TIMEOUT
-// and the CTA unwinds.
+// (double-buffered neighbour lists).  Taps are visited in ascending order in
+// every tile (tiling-independent results); with a plan, each CTA takes its
+// tiles from the plan's cost-sorted schedule in a snake order.  Every wait
+// is bounded; a wait that runs out sets MSC_DEV_TIMEOUT and the CTA unwinds.
 #include "common.cuh"
 #include "conv.h"
 #include "conv_common.cuh"
