@@ -2,8 +2,8 @@
 
 Multi-GPU runs of the residual stack (one process per GPU) split the voxels,
 ordered by the packed ``(b, z, y, x)`` key, into contiguous z-slabs whose
-boundaries sit at voxel-count quantiles (a thin surface leaves most uniform
-z-slabs empty).  Submanifold convs and the per-voxel LayerNorm only reach
+boundaries balance each rank's work, owned + local rows (a thin surface
+leaves most uniform z-slabs empty).  Submanifold convs and the per-voxel LayerNorm only reach
 one z-plane across a slab boundary, so each rank holds, besides its own
 voxels, the voxels of the two z-planes on either side that belong to its
 neighbours:
@@ -65,9 +65,12 @@ def _planes(coords: np.ndarray):
 
 
 def partition(coords: np.ndarray, nranks: int, halo: int = HALO_PLANES) -> list[SlabPart]:
-    """Splits rows sorted by (b, z, y, x) into nranks z-slabs at voxel-count
-    quantiles, on plane boundaries.  Every slab must span more than `halo`
-    z-planes of one sample, so that a halo belongs to the adjacent rank only."""
+    """Splits rows sorted by (b, z, y, x) into nranks z-slabs on plane
+    boundaries, placed so that every rank's work (owned + local rows) is
+    about equal (a thin surface leaves most uniform z-slabs empty, and a cut
+    through large planes gives both sides large halos).  Every slab must span
+    more than `halo` z-planes of one sample, so that a halo belongs to the
+    adjacent rank only."""
     n = coords.shape[0]
     if nranks < 1:
         raise ValueError("nranks must be >= 1")
@@ -79,14 +82,16 @@ def partition(coords: np.ndarray, nranks: int, halo: int = HALO_PLANES) -> list[
     nplanes = len(starts)
     if nranks > 1 and nplanes < nranks * (halo + 1):
         raise ValueError(f"{nplanes} z-planes cannot give {nranks} slabs of more than {halo} planes")
-    # plane cut points: first plane whose start row reaches the quantile
-    cuts = [0]
-    for r in range(1, nranks):
-        target = n * r / nranks
-        p = int(np.searchsorted(starts, target, side="left"))
-        p = max(p, cuts[-1] + halo + 1)
-        cuts.append(p)
-    cuts.append(nplanes)
+    cuts = _balanced_cuts(starts, pbz, n, nranks, halo)
+    if cuts is None:
+        # plane cut points: first plane whose start row reaches the quantile
+        cuts = [0]
+        for r in range(1, nranks):
+            target = n * r / nranks
+            p = int(np.searchsorted(starts, target, side="left"))
+            p = max(p, cuts[-1] + halo + 1)
+            cuts.append(p)
+        cuts.append(nplanes)
     for r in range(nranks):
         if cuts[r + 1] - cuts[r] <= halo:
             raise ValueError("slab too thin for the halo; use fewer ranks")
@@ -128,6 +133,70 @@ def partition(coords: np.ndarray, nranks: int, halo: int = HALO_PLANES) -> list[
             assert len(hl) == 0 or (hl[-1] == parts[r].hi - 1 and hl[0] >= parts[r].lo)
             parts[r].send_hi = len(hl)
     return parts
+
+
+def _cut_halos(starts: np.ndarray, pbz: np.ndarray, n: int, halo: int):
+    """Halo rows a cut before plane c gives each side: below[c] = rows the
+    upper rank copies from the planes under c, above[c] = rows the lower rank
+    copies from plane c upwards (same sample, within `halo` z)."""
+    nplanes = len(starts)
+    sizes = np.diff(np.r_[starts, n]).astype(np.int64)
+    b = pbz >> 20
+    z = pbz & ((1 << 20) - 1)
+    below = np.zeros(nplanes + 1, dtype=np.int64)
+    above = np.zeros(nplanes + 1, dtype=np.int64)
+    for c in range(1, nplanes):
+        below[c] = sum(int(sizes[q]) for q in range(max(0, c - halo), c) if b[q] == b[c] and z[c] - z[q] <= halo)
+        above[c] = sum(int(sizes[q]) for q in range(c, min(nplanes, c + halo))
+                       if b[q] == b[c - 1] and z[q] - z[c - 1] <= halo)
+    return below, above
+
+
+def _balanced_cuts(starts: np.ndarray, pbz: np.ndarray, n: int, nranks: int, halo: int):
+    """Plane cuts that even out the ranks' residual-block work, taken as
+    owned + local rows (conv2 runs over the owned rows, conv1 and the operand
+    preparation over owned and halo rows): the smallest bound C for which a
+    greedy sweep (each rank takes planes while its work stays within C) gives
+    every rank more than `halo` planes.  None when no cut is needed or found."""
+    nplanes = len(starts)
+    if nranks == 1:
+        return [0, nplanes]
+    below, above = _cut_halos(starts, pbz, n, halo)
+    row_at = np.r_[starts, n].astype(np.int64)
+
+    def work(s, e):
+        rows = int(row_at[e] - row_at[s])
+        return 2 * rows + (int(below[s]) if s > 0 else 0) + (int(above[e]) if e < nplanes else 0)
+
+    def sweep(bound):
+        cuts, s = [0], 0
+        for r in range(nranks - 1):
+            last = nplanes - (nranks - 1 - r) * (halo + 1)   # leave room for the ranks above
+            best = -1
+            for e in range(s + halo + 1, last + 1):
+                if 2 * int(row_at[e] - row_at[s]) > bound:
+                    break
+                if work(s, e) <= bound:
+                    best = e
+            if best < 0:
+                return None
+            cuts.append(best)
+            s = best
+        if nplanes - s <= halo or work(s, nplanes) > bound:
+            return None
+        cuts.append(nplanes)
+        return cuts
+
+    lo, hi = 2 * n // nranks, 4 * n
+    if sweep(hi) is None:
+        return None
+    while lo < hi:
+        mid = (lo + hi) // 2
+        if sweep(mid) is None:
+            lo = mid + 1
+        else:
+            hi = mid
+    return sweep(hi)
 
 
 def _sort_keys(coords: np.ndarray) -> np.ndarray:
