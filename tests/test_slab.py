@@ -116,10 +116,13 @@ def _free_port():
     return port
 
 
-def test_two_gloo_ranks_match_the_single_process_stack(tmp_path, oracle):
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_match_the_single_process_stack(tmp_path, oracle, world):
+    """The owned rows of 2 or 4 gloo ranks (4: two inner ranks with halos on
+    both sides, cuts from the balanced partition) equal the single-process
+    oracle stack bit for bit."""
     import multiprocessing as mp
     from oracle.oracle import W_Q8_0
-    world = 2
     port = _free_port()
     ctx = mp.get_context("spawn")
     outs = [str(tmp_path / f"rank{r}.npy") for r in range(world)]
