@@ -80,7 +80,7 @@ WORKLOADS = {
 # averaged; scaled by the voxels a launch processes.  shell_4m's gathers miss
 # L2 more than res4_c128's (its tap-ordered tiles spread over a 450 MB
 # operand), so each workload uses its own capture.
-CONV_DRAM_BYTES_PER_VOXEL = {("shell_4m", "ln"): 1296.0, ("res4_c128", "gn"): 860.0, ("res4_c128", "ln"): 646.0}
+CONV_DRAM_BYTES_PER_VOXEL = {("shell_4m", "ln"): 1302.0, ("res4_c128", "gn"): 860.0, ("res4_c128", "ln"): 646.0}
 # Compulsory bytes per voxel of one Q8_0 conv launch at C = 128 (each input
 # row read once): activation codes + block scales (128 + 16), the plan's
 # tile row and neighbour list (4 + 108), the output (fused Q8_0 codes + scales
