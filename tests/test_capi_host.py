@@ -78,3 +78,60 @@ def test_null_context_is_rejected():
     rc = lib.msc_make_level(None, None, 0, None, None, 0, None)
     assert rc == -1
     assert "context" in lib.msc_last_error().decode()
+
+
+def _c_program(syms):
+    """A C99 program that references every declared entry point (so the link
+    resolves each one against the library) and calls the host-only ones."""
+    table = ",\n    ".join(f"(msc_fn)&{s}" for s in syms)
+    return f"""#include <stdio.h>
+#include <string.h>
+#include "moge_sparse_cuda.h"
+
+typedef void (*msc_fn)(void);
+static const msc_fn kEntryPoints[] = {{
+    {table}
+}};
+
+int main(void) {{
+    size_t k, present = 0;
+    int rc;
+    for (k = 0; k < sizeof(kEntryPoints) / sizeof(kEntryPoints[0]); ++k) present += kEntryPoints[k] != NULL;
+    rc = msc_make_level(NULL, NULL, 0, NULL, NULL, 0, NULL);
+    printf("entry_points %lu\\n", (unsigned long)present);
+    printf("abi %d\\n", msc_abi_version());
+    printf("topology_ws_1000 %lu\\n", (unsigned long)msc_topology_workspace_bytes(1000));
+    printf("null_ctx_rc %d\\n", rc);
+    printf("null_ctx_error_has_context %d\\n", strstr(msc_last_error(), "context") != NULL);
+    return 0;
+}}
+"""
+
+
+@pytest.mark.parametrize("compiler,std", [("gcc", "-std=c99"), ("g++", "-std=c++11")])
+def test_header_compiles_links_and_runs_from_plain_c(tmp_path, compiler, std):
+    """What a cgo / JNI / N-API binding sees: the header alone, compiled as
+    strict C99 (and as C++ through its extern "C" guard), linked against the
+    shared library, run on a host without a GPU."""
+    import shutil
+    import subprocess
+    from mogecpp_b200 import lib as L
+    if shutil.which(compiler) is None:
+        pytest.skip(f"{compiler} is not installed")
+    if not os.path.exists(L.LIB_PATH):
+        pytest.skip("library not built")
+    syms = declared_symbols()
+    src = tmp_path / ("abi.c" if compiler == "gcc" else "abi.cpp")
+    src.write_text(_c_program(syms))
+    exe = tmp_path / "abi"
+    libdir = os.path.dirname(L.LIB_PATH)
+    cmd = [compiler, std, "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+           str(src), "-o", str(exe), "-L", libdir, "-l:" + os.path.basename(L.LIB_PATH), "-Wl,-rpath," + libdir]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True, timeout=60).stdout
+    got = dict(line.split() for line in out.splitlines())
+    assert int(got["entry_points"]) == len(syms)
+    assert int(got["abi"]) == 1
+    assert int(got["topology_ws_1000"]) == L.load().msc_topology_workspace_bytes(1000)
+    assert int(got["null_ctx_rc"]) == -1
+    assert got["null_ctx_error_has_context"] == "1"
