@@ -40,7 +40,12 @@ constexpr int kAxisMax = (1 << 19) - 1;
 constexpr int kNoVoxel = 0x7fffffff;
 constexpr int kBrickVox = 64;
 constexpr int kMapVox = 32;       // voxels per neighbour-map block (27 x 32 threads)
-constexpr int kScanBlock = 1024;
+constexpr int kScanBlock = 1024;  // threads of the single-block scan of the block sums
+// Voxels per block of the first-child flag scan (excl[] holds exclusive
+// prefixes within such a block, bsum[] the blocks' totals).  Equal to the
+// neighbour-map block, so make_level_downsample's neighbour kernel scans the
+// flags of the voxels it maps.
+constexpr int kFirstBlock = 256;
 constexpr unsigned kStrideGrid = 148 * 8;
 
 struct __align__(16) Slot {
@@ -193,8 +198,11 @@ __global__ void parent_insert_kernel(const int4* __restrict__ coords, int n, Slo
 
 // Block-level exclusive scan of flags f (one per thread): returns the
 // exclusive prefix within the block; the block total goes to *total.
+// Exclusive scan of f over the block (blockDim.x a multiple of 32, at most
+// 1024; warp_tot holds blockDim.x / 32 ints); the block total goes to *total.
 __device__ __forceinline__ int block_exclusive_scan(int f, int* warp_tot, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = static_cast<int>(blockDim.x >> 5);
     int inc = f;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -204,14 +212,14 @@ __device__ __forceinline__ int block_exclusive_scan(int f, int* warp_tot, int* t
     if (lane == 31) warp_tot[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        const int w = warp_tot[lane];
+        const int w = lane < nwarps ? warp_tot[lane] : 0;
         int wi = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int v = __shfl_up_sync(0xffffffffu, wi, o);
             if (lane >= o) wi += v;
         }
-        warp_tot[lane] = wi - w;
+        if (lane < nwarps) warp_tot[lane] = wi - w;
         if (lane == 31) *total = wi;
     }
     __syncthreads();
@@ -220,13 +228,13 @@ __device__ __forceinline__ int block_exclusive_scan(int f, int* warp_tot, int* t
 
 // first[i] = (i is the first child of its parent); per-block exclusive scan
 // into excl[], block totals into bsum[].
-__global__ void __launch_bounds__(kScanBlock) first_scan_kernel(const int4* __restrict__ coords, int n,
-                                                                const Slot* __restrict__ tp, uint64_t pmask,
-                                                                int* __restrict__ excl, int* __restrict__ bsum,
-                                                                const int* gate, int budget) {
+__global__ void __launch_bounds__(kFirstBlock) first_scan_kernel(const int4* __restrict__ coords, int n,
+                                                                 const Slot* __restrict__ tp, uint64_t pmask,
+                                                                 int* __restrict__ excl, int* __restrict__ bsum,
+                                                                 const int* gate, int budget) {
     if (gated_off(gate, budget)) return;
-    __shared__ int warp_tot[kScanBlock / 32];
-    const int i = blockIdx.x * kScanBlock + threadIdx.x;
+    __shared__ int warp_tot[kFirstBlock / 32];
+    const int i = blockIdx.x * kFirstBlock + threadIdx.x;
     int f = 0;
     if (i < n) {
         const int4 c = __ldg(coords + i);
@@ -236,24 +244,29 @@ __global__ void __launch_bounds__(kScanBlock) first_scan_kernel(const int4* __re
     if (i < n) excl[i] = e;
 }
 
-// Single block: exclusive scan of the block totals; np -> *np_out.
+// Single block: exclusive scan of the block totals in place; np -> *np_out.
+// Thread t takes the run of `per` consecutive totals starting at t * per:
+// its loads are independent (one memory round trip for the whole array),
+// then one block scan of the run sums.
 __global__ void __launch_bounds__(kScanBlock) block_scan_kernel(int* __restrict__ bsum, int nblocks,
                                                                 int* __restrict__ np_out) {
     __shared__ int warp_tot[kScanBlock / 32];
-    __shared__ int carry, total;
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
-    for (int base = 0; base < nblocks; base += kScanBlock) {
-        const int i = base + threadIdx.x;
-        const int f = i < nblocks ? bsum[i] : 0;
-        const int e = block_exclusive_scan(f, warp_tot, &total);
-        const int c0 = carry;
-        if (i < nblocks) bsum[i] = c0 + e;
-        __syncthreads();
-        if (threadIdx.x == 0) carry = c0 + total;
-        __syncthreads();
+    __shared__ int total;
+    const int per = (nblocks + kScanBlock - 1) / kScanBlock;
+    const int64_t b0 = static_cast<int64_t>(threadIdx.x) * per;
+    int s = 0;
+#pragma unroll 4
+    for (int k = 0; k < per; ++k)
+        if (b0 + k < nblocks) s += bsum[b0 + k];
+    int run = block_exclusive_scan(s, warp_tot, &total);
+    for (int k = 0; k < per; ++k) {
+        if (b0 + k < nblocks) {
+            const int v = bsum[b0 + k];
+            bsum[b0 + k] = run;
+            run += v;
+        }
     }
-    if (threadIdx.x == 0) *np_out = carry;
+    if (threadIdx.x == 0) *np_out = total;
 }
 
 // Parent ids, up_rows, parent coordinates.
@@ -267,7 +280,7 @@ __global__ void assign_kernel(const int4* __restrict__ coords, int n, const Slot
         if (!coord_ok(c)) continue;
         const int first = table_find(tp, pmask, pack_key(c.x >> 1, c.y >> 1, c.z >> 1, c.w));
         if (first < 0 || first >= n) continue;
-        const int pid = excl[first] + bsum[first / kScanBlock];
+        const int pid = excl[first] + bsum[first / kFirstBlock];
         up_rows[i] = pid;
         if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
     }
@@ -407,20 +420,35 @@ __global__ void brick_fill_kernel(const int4* __restrict__ coords, int n, const 
 // reads before using any of them (27 independent loads in flight per
 // thread); the block's [256][27] rows are staged in shared memory (row
 // stride 27 words: conflict-free) and leave as one contiguous run.
+//
+// kFirst (make_level_downsample): the voxel's stride-2 cell (the 2 x 2 x 2
+// cells with the same parent) lies inside its brick and its 8 cells are
+// taps of the row just built, so the kernel also does the first-child pass
+// of the stride-2 maps: first child (smallest index), the voxel's rank among
+// its siblings and their count, and the block scan of the first-child flags
+// (one block = kFirstBlock voxels), as brick_first_scan_kernel does from the
+// records.
 constexpr int kNbrThreads = 256;
+static_assert(kNbrThreads == kFirstBlock, "the neighbour block is the first-child scan block");
 
+template <bool kFirst>
 __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4* __restrict__ coords, int n,
                                                                      const Slot* __restrict__ t, uint64_t mask,
                                                                      const int* __restrict__ rec,
                                                                      const int* __restrict__ ctr, int budget,
-                                                                     int* __restrict__ nbr) {
+                                                                     int* __restrict__ nbr,
+                                                                     int* __restrict__ first_idx,
+                                                                     int* __restrict__ cell_rc,
+                                                                     int* __restrict__ excl, int* __restrict__ bsum) {
     if (*ctr > budget) return;
     __shared__ __align__(16) int sn[kNbrThreads * 27];
     __shared__ int sb[8 * kNbrThreads];
+    __shared__ int warp_tot[kNbrThreads / 32];
     const int tid = threadIdx.x;
     const int64_t base = static_cast<int64_t>(blockIdx.x) * kNbrThreads;
     const int64_t i = base + tid;
     int* row = sn + tid * 27;
+    int first = -1, rc = 8;  // brick_first_scan_kernel's values for a voxel without a cell
     if (i < n) {
         const int4 c = __ldg(coords + i);
         if (!coord_ok(c)) {
@@ -463,7 +491,33 @@ __global__ void __launch_bounds__(kNbrThreads) brick_neighbor_kernel(const int4*
             }
 #pragma unroll
             for (int tap = 0; tap < 27; ++tap) row[tap] = v[tap] != kNoVoxel ? v[tap] : n;
+            if (kFirst && sbt[0] >= 0) {
+                // the cell's cells: offset 0 and s per axis, s = +1 on an even
+                // coordinate and -1 on an odd one (tap digit s + 1), all in the
+                // own brick; a missing cell reads n
+                const int sx = (lx & 1) ? 0 : 2, sy = (ly & 1) ? 0 : 2, sz = (lz & 1) ? 0 : 2;
+                int fst = kNoVoxel, cnt = 0, rnk = 0;
+#pragma unroll
+                for (int o = 0; o < 8; ++o) {
+                    const int j = row[((o & 4) ? sx : 1) * 9 + ((o & 2) ? sy : 1) * 3 + ((o & 1) ? sz : 1)];
+                    if (j < n) {
+                        ++cnt;
+                        rnk += j < i;
+                        fst = min(fst, j);
+                    }
+                }
+                first = fst;
+                rc = rnk | (cnt << 8);
+            }
         }
+    }
+    if constexpr (kFirst) {
+        if (i < n) {
+            first_idx[i] = first;
+            cell_rc[i] = rc;
+        }
+        const int e = block_exclusive_scan(i < n && first == i ? 1 : 0, warp_tot, bsum + blockIdx.x);
+        if (i < n) excl[i] = e;
     }
     __syncthreads();
     const int64_t count = (n - base < kNbrThreads ? n - base : kNbrThreads) * 27;
@@ -504,16 +558,16 @@ __device__ __forceinline__ CellInfo cell_info(const int* __restrict__ rec, int i
 
 // first_idx[i] = the first child of i's parent; per-block exclusive scan of
 // the flags (i == first) into excl[], block totals into bsum[].
-__global__ void __launch_bounds__(kScanBlock) brick_first_scan_kernel(const int4* __restrict__ coords, int n,
-                                                                      const Slot* __restrict__ t, uint64_t mask,
-                                                                      const int* __restrict__ rec,
-                                                                      const int* __restrict__ ctr, int budget,
-                                                                      int* __restrict__ first_idx,
-                                                                      int* __restrict__ cell_rc,
-                                                                      int* __restrict__ excl, int* __restrict__ bsum) {
+__global__ void __launch_bounds__(kFirstBlock) brick_first_scan_kernel(const int4* __restrict__ coords, int n,
+                                                                       const Slot* __restrict__ t, uint64_t mask,
+                                                                       const int* __restrict__ rec,
+                                                                       const int* __restrict__ ctr, int budget,
+                                                                       int* __restrict__ first_idx,
+                                                                       int* __restrict__ cell_rc,
+                                                                       int* __restrict__ excl, int* __restrict__ bsum) {
     if (*ctr > budget) return;
-    __shared__ int warp_tot[kScanBlock / 32];
-    const int i = blockIdx.x * kScanBlock + threadIdx.x;
+    __shared__ int warp_tot[kFirstBlock / 32];
+    const int i = blockIdx.x * kFirstBlock + threadIdx.x;
     int f = 0;
     if (i < n) {
         const int4 c = __ldg(coords + i);
@@ -548,7 +602,7 @@ __global__ void brick_assign_kernel(const int4* __restrict__ coords, int n, cons
         const int first = first_idx[i];
         if (first < 0 || first >= n) continue;
         const int4 c = __ldg(coords + i);
-        const int pid = excl[first] + bsum[first / kScanBlock];
+        const int pid = excl[first] + bsum[first / kFirstBlock];
         up_rows[i] = pid;
         if (first == i) parent[pid] = make_int4(c.x >> 1, c.y >> 1, c.z >> 1, c.w);
         const int rc = cell_rc[i];  // the cell's rank and count from the first-child pass
@@ -657,7 +711,7 @@ TopoWs carve(void* ws, int64_t n) {
     w.cap = table_capacity(n);
     w.bcap = brick_capacity(n);
     w.budget = static_cast<int>(brick_budget(n));
-    const int64_t nblk = (n + kScanBlock - 1) / kScanBlock + 1;
+    const int64_t nblk = (n + kFirstBlock - 1) / kFirstBlock + 1;
     char* p = static_cast<char*>(ws);
     w.t = reinterpret_cast<Slot*>(p);
     p += align_up(2 * w.cap * sizeof(Slot), 256);
@@ -690,7 +744,7 @@ cudaError_t launch_brick_build(const int4* c4, int n, const TopoWs& w, uint32_t*
 }  // namespace
 
 size_t topology_workspace_bytes(int64_t n) {
-    const int64_t nblk = (n + kScanBlock - 1) / kScanBlock + 1;
+    const int64_t nblk = (n + kFirstBlock - 1) / kFirstBlock + 1;
     return align_up(2 * table_capacity(n) * sizeof(Slot), 256) + align_up(static_cast<size_t>(n + 1) * 4, 256) +
            align_up(static_cast<size_t>(nblk) * 4, 256) + align_up(brick_capacity(n) * sizeof(Slot), 256) +
            align_up(static_cast<size_t>(brick_budget(n)) * kBrickVox * 4, 256) + 256 +
@@ -700,12 +754,18 @@ size_t topology_workspace_bytes(int64_t n) {
 namespace {
 
 // The neighbour map from a built brick table (or the per-voxel hash when
-// the bricks overflowed).
+// the bricks overflowed).  with_first: the brick path also runs the
+// first-child pass of the stride-2 maps (launch_stride2 then skips it).
 cudaError_t launch_map(const int4* c4, int64_t n, int32_t* nbr, const TopoWs& w, uint32_t* status,
-                       cudaStream_t st) {
+                       cudaStream_t st, bool with_first) {
     const int ni = static_cast<int>(n);
-    brick_neighbor_kernel<<<static_cast<unsigned>((n + kNbrThreads - 1) / kNbrThreads), kNbrThreads, 0, st>>>(
-        c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, nbr);
+    const unsigned grid = static_cast<unsigned>((n + kNbrThreads - 1) / kNbrThreads);
+    if (with_first)
+        brick_neighbor_kernel<true><<<grid, kNbrThreads, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget,
+                                                                  nbr, w.first, w.cell, w.excl, w.bsum);
+    else
+        brick_neighbor_kernel<false><<<grid, kNbrThreads, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget,
+                                                                   nbr, nullptr, nullptr, nullptr, nullptr);
     // too many bricks: the per-voxel hash (these return at once otherwise)
     table_clear_kernel<<<kStrideGrid, 256, 0, st>>>(w.t, w.cap, w.ctr, w.budget);
     insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, w.t, w.cap - 1, status, w.ctr, w.budget);
@@ -722,7 +782,7 @@ cudaError_t launch_make_level(const int32_t* coords, int64_t n, int32_t* nbr, vo
     const auto* c4 = reinterpret_cast<const int4*>(coords);
     cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
     if (e != cudaSuccess) return e;
-    return launch_map(c4, n, nbr, w, status, st);
+    return launch_map(c4, n, nbr, w, status, st, false);
 }
 
 size_t topology_table_bytes(int64_t n) { return table_capacity(n) * sizeof(Slot); }
@@ -744,11 +804,14 @@ cudaError_t launch_make_level_in_table(const int32_t* coords, int64_t n, int32_t
 namespace {
 
 // The stride-2 maps from a built brick table (or the per-voxel hashes).
+// first_done: the neighbour kernel already ran the brick path's first-child
+// pass (first_idx, cell ranks, flag scan).
 cudaError_t launch_stride2(const int4* c4, int64_t n, int32_t* parent, int32_t* np_dev, int32_t* pool_rows,
-                           float* inv_count, int32_t* up_rows, const TopoWs& w, uint32_t* status, cudaStream_t st) {
+                           float* inv_count, int32_t* up_rows, const TopoWs& w, uint32_t* status, cudaStream_t st,
+                           bool first_done) {
     Slot* tf = w.t;
     Slot* tp = w.t + w.cap;
-    const int nblk = static_cast<int>((n + kScanBlock - 1) / kScanBlock);
+    const int nblk = static_cast<int>((n + kFirstBlock - 1) / kFirstBlock);
     const int ni = static_cast<int>(n);
     auto* par = reinterpret_cast<int4*>(parent);
     // per-voxel tables only when the bricks overflowed (gated kernels)
@@ -756,9 +819,10 @@ cudaError_t launch_stride2(const int4* c4, int64_t n, int32_t* parent, int32_t* 
     insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tf, w.cap - 1, status, w.ctr, w.budget);
     parent_insert_kernel<<<kStrideGrid, 256, 0, st>>>(c4, ni, tp, w.cap - 1, status, w.ctr, w.budget);
     // first children: flags + per-block scan (one of the two runs)
-    brick_first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget, w.first,
-                                                         w.cell, w.excl, w.bsum);
-    first_scan_kernel<<<nblk, kScanBlock, 0, st>>>(c4, ni, tp, w.cap - 1, w.excl, w.bsum, w.ctr, w.budget);
+    if (!first_done)
+        brick_first_scan_kernel<<<nblk, kFirstBlock, 0, st>>>(c4, ni, w.bt, w.bcap - 1, w.rec, w.ctr, w.budget,
+                                                              w.first, w.cell, w.excl, w.bsum);
+    first_scan_kernel<<<nblk, kFirstBlock, 0, st>>>(c4, ni, tp, w.cap - 1, w.excl, w.bsum, w.ctr, w.budget);
     block_scan_kernel<<<1, kScanBlock, 0, st>>>(w.bsum, nblk, np_dev);
     pool_fill_kernel<<<kStrideGrid, 256, 0, st>>>(pool_rows, np_dev, ni);
     brick_assign_kernel<<<stride_grid(n, 256), 256, 0, st>>>(c4, ni, w.ctr, w.budget, w.first, w.cell, w.excl, w.bsum,
@@ -778,7 +842,7 @@ cudaError_t launch_downsample(const int32_t* coords, int64_t n, int32_t* parent,
     const auto* c4 = reinterpret_cast<const int4*>(coords);
     cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
     if (e != cudaSuccess) return e;
-    return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st);
+    return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st, false);
 }
 
 cudaError_t launch_octant_maps(const int32_t* coords, int64_t nfine, const int32_t* pool_rows,
@@ -801,9 +865,9 @@ cudaError_t launch_make_level_downsample(const int32_t* coords, int64_t n, int32
     const auto* c4 = reinterpret_cast<const int4*>(coords);
     cudaError_t e = launch_brick_build(c4, static_cast<int>(n), w, status, st);
     if (e != cudaSuccess) return e;
-    e = launch_map(c4, n, nbr, w, status, st);
+    e = launch_map(c4, n, nbr, w, status, st, true);
     if (e != cudaSuccess) return e;
-    return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st);
+    return launch_stride2(c4, n, parent, np_dev, pool_rows, inv_count, up_rows, w, status, st, true);
 }
 
 }  // namespace msc

@@ -142,16 +142,21 @@ def test_sparse_input_takes_the_per_voxel_hash(ex, oracle, spacing):
     np.testing.assert_array_equal(nbr, oracle.make_level(coords))
 
 
-@pytest.mark.parametrize("gen", ["golden", "topo_4m", "sparse"])
-def test_make_level_downsample_equals_the_two_calls(ex, golden_topology, gen):
-    """msc_make_level_downsample (one voxel table for both maps) gives the
-    neighbour map of msc_make_level and the stride-2 maps of
-    msc_downsample, bit for bit: the reference's shuffled golden set, the
-    4M-voxel stress set, and a lattice sparse enough for the per-voxel hash."""
+@pytest.mark.parametrize("gen", ["golden", "topo_4m", "res4_c128", "sparse"])
+def test_make_level_downsample_equals_the_two_calls(ex, oracle, golden_topology, gen):
+    """msc_make_level_downsample (one voxel table for both maps; the
+    neighbour kernel also runs the first-child pass) gives the neighbour map
+    of msc_make_level and the stride-2 maps of msc_downsample, bit for bit,
+    and both equal the oracle: the reference's shuffled golden set, the
+    4M-voxel stress set (against the two calls only), the 364,846-voxel
+    res4_c128 set (more than 1024 first-child scan blocks), and a lattice
+    sparse enough for the per-voxel hash."""
     if gen == "golden":
         c = golden_topology["topo_shuffled_coords"]
     elif gen == "topo_4m":
         c = synth.topo_4m_coords()
+    elif gen == "res4_c128":
+        c = synth.res4_c128_coords()
     else:
         g = np.arange(0, 22 * 5, 5)
         x, y, z = np.meshgrid(g, g, g[:12], indexing="ij")
@@ -167,3 +172,10 @@ def test_make_level_downsample_equals_the_two_calls(ex, golden_topology, gen):
     for a, b in ((tr_f.parent, tr.parent), (tr_f.pool_rows, tr.pool_rows), (tr_f.inv_count, tr.inv_count),
                  (tr_f.up_rows, tr.up_rows)):
         assert bool((a == b).all())
+    if gen != "topo_4m":
+        np.testing.assert_array_equal(host(nbr_f), oracle.make_level(c))
+        parent, pool, inv, up = oracle.downsample(c)
+        np.testing.assert_array_equal(host(tr_f.parent), parent)
+        np.testing.assert_array_equal(host(tr_f.pool_rows), pool)
+        np.testing.assert_array_equal(host(tr_f.inv_count), inv)
+        np.testing.assert_array_equal(host(tr_f.up_rows), up)
