@@ -245,25 +245,42 @@ __global__ void __launch_bounds__(kFirstBlock) first_scan_kernel(const int4* __r
 }
 
 // Single block: exclusive scan of the block totals in place; np -> *np_out.
-// Thread t takes the run of `per` consecutive totals starting at t * per:
-// its loads are independent (one memory round trip for the whole array),
-// then one block scan of the run sums.
+// Thread t takes the run of `per` consecutive totals starting at t * per,
+// then one block scan of the run sums.  Up to kRunRegs totals per thread
+// (nblocks <= 32768, n <= 8.4M voxels) the run is held in registers: all
+// its loads are issued together (one memory round trip for the array).
+constexpr int kRunRegs = 32;
 __global__ void __launch_bounds__(kScanBlock) block_scan_kernel(int* __restrict__ bsum, int nblocks,
                                                                 int* __restrict__ np_out) {
     __shared__ int warp_tot[kScanBlock / 32];
     __shared__ int total;
     const int per = (nblocks + kScanBlock - 1) / kScanBlock;
     const int64_t b0 = static_cast<int64_t>(threadIdx.x) * per;
-    int s = 0;
-#pragma unroll 4
-    for (int k = 0; k < per; ++k)
-        if (b0 + k < nblocks) s += bsum[b0 + k];
-    int run = block_exclusive_scan(s, warp_tot, &total);
-    for (int k = 0; k < per; ++k) {
-        if (b0 + k < nblocks) {
-            const int v = bsum[b0 + k];
-            bsum[b0 + k] = run;
-            run += v;
+    if (per <= kRunRegs) {
+        int v[kRunRegs];
+        int s = 0;
+#pragma unroll
+        for (int k = 0; k < kRunRegs; ++k) {
+            v[k] = (k < per && b0 + k < nblocks) ? bsum[b0 + k] : 0;
+            s += v[k];
+        }
+        int run = block_exclusive_scan(s, warp_tot, &total);
+#pragma unroll
+        for (int k = 0; k < kRunRegs; ++k) {
+            if (k < per && b0 + k < nblocks) bsum[b0 + k] = run;
+            run += v[k];
+        }
+    } else {
+        int s = 0;
+        for (int k = 0; k < per; ++k)
+            if (b0 + k < nblocks) s += bsum[b0 + k];
+        int run = block_exclusive_scan(s, warp_tot, &total);
+        for (int k = 0; k < per; ++k) {
+            if (b0 + k < nblocks) {
+                const int v = bsum[b0 + k];
+                bsum[b0 + k] = run;
+                run += v;
+            }
         }
     }
     if (threadIdx.x == 0) *np_out = total;
