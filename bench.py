@@ -9,7 +9,8 @@ Workloads (seeded synthetic surfaces, mogecpp_b200/synth.py):
 * ``res4_c128`` - 364,846 voxels on a 256^3 grid, 4 GroupNorm(32) residual
   blocks (conv -> GroupNorm -> SiLU -> conv -> +skip), C = 128, fp16, Q8_0.
 * ``topo_4m`` - topology only: hash build + 27-tap neighbour map + stride-2
-  maps over the union of 8 seeded surfaces (4.3M voxels) on a 1024^3 grid.
+  maps over the union of 8 seeded surfaces (4,026,477 voxels) on a 1024^3
+  grid.
 * ``conv_c64`` - one submanifold conv, C = 64, fp32 features and weights,
   77,507 voxels on a 128^3 grid.
 * ``unet_c64`` - one encoder-decoder level, batch 2 (two surfaces):
@@ -28,9 +29,12 @@ per second (topo_4m: voxels per second) with the inputs resident in HBM;
 inputs copied in and its result copied out inside the timed region.
 
 Multi-GPU (torchrun, one process per GPU; stack workloads): the voxels are
-split into z-slabs at voxel-count quantiles (mogecpp_b200/slab.py); each rank
-builds the topology of its slab plus a two-plane halo per side and, before
-every block, exchanges the boundary planes with its z-neighbours over NCCL.
+split into z-slabs whose owned + halo rows are balanced across the ranks
+(mogecpp_b200/slab.py); each rank builds the topology of its slab plus a
+two-plane halo per side and refreshes the halo once per block: by default
+conv2's epilogue stores the boundary planes straight into the neighbours'
+halo rows over CUDA IPC peer memory (``--exchange nccl``: NCCL send/recv
+before every block).
 Total work is fixed ("scaling": "strong"); timing is the max over ranks.
 After the timed region the owned rows are gathered on rank 0 and compared
 with the single-GPU stack over the whole set (``parity``).
