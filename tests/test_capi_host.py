@@ -135,3 +135,31 @@ def test_header_compiles_links_and_runs_from_plain_c(tmp_path, compiler, std):
     assert int(got["topology_ws_1000"]) == L.load().msc_topology_workspace_bytes(1000)
     assert int(got["null_ctx_rc"]) == -1
     assert got["null_ctx_error_has_context"] == "1"
+
+
+def test_cxx_seam_compiles_and_reports_no_device(tmp_path):
+    """include/moge_sparse_cuda.hpp, the C++17 seam mogecpp's refiner loop
+    calls (moge_cuda::Device, SparseConfig, SparseRefiner), compiles warning
+    free against the header alone and, without an sm_100 GPU, reports the
+    device unavailable and turns C ABI failures into moge_cuda::Error."""
+    import shutil
+    import subprocess
+    import torch
+    from mogecpp_b200 import lib as L
+    if shutil.which("g++") is None:
+        pytest.skip("g++ is not installed")
+    if not os.path.exists(L.LIB_PATH):
+        pytest.skip("library not built")
+    exe = tmp_path / "seam"
+    libdir = os.path.dirname(L.LIB_PATH)
+    cmd = ["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+           os.path.join(ROOT, "tests", "cxx_seam_probe.cpp"), "-o", str(exe), "-L", libdir,
+           "-l:" + os.path.basename(L.LIB_PATH), "-Wl,-rpath," + libdir]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True, timeout=60).stdout
+    lines = {ln.split()[0]: ln.split()[1:] for ln in out.splitlines()}
+    sm100 = torch.cuda.is_available() and torch.cuda.get_device_capability(0) == (10, 0)
+    assert lines["device"] == ["sm100" if sm100 else "none"]
+    assert lines["null_ctx_code"] == ["-1"]
+    assert lines["null_ctx_message"] == ["1"]
+    assert lines["default_config"] == ["0", "3", "16", "256.0"]
