@@ -96,24 +96,12 @@ class SparseRefiner {
 public:
     SparseRefiner(const Device& device, const void* mogg, size_t mogg_bytes, void* stream = nullptr) {
         check(msc_refiner_create(device.handle(), mogg, mogg_bytes, stream, &r_), "msc_refiner_create");
-        msc_sparse_config c{};
-        const int rc = msc_refiner_config(r_, &c);
-        if (rc != MSC_OK) {
+        try {
+            read_config();
+        } catch (...) {
             msc_refiner_destroy(r_);
-            check(rc, "msc_refiner_config");
+            throw;
         }
-        cfg_.present = true;
-        cfg_.in_channels = c.in_channels;
-        cfg_.out_channels = c.out_channels;
-        cfg_.encoder_channels = c.encoder_channels;
-        cfg_.model_channels.assign(c.model_channels, c.model_channels + c.num_levels);
-        cfg_.encoder_blocks.assign(c.encoder_blocks, c.encoder_blocks + c.num_levels);
-        const int inner = c.num_levels > 0 ? c.num_levels - 1 : 0;
-        cfg_.decoder_blocks.assign(c.decoder_blocks, c.decoder_blocks + inner);
-        cfg_.downsample_factors.assign(c.downsample_factors, c.downsample_factors + inner);
-        cfg_.bottleneck_blocks = c.bottleneck_blocks;
-        cfg_.encoder_downsample = c.encoder_downsample;
-        cfg_.depth_resolution = c.depth_resolution;
     }
     ~SparseRefiner() { msc_refiner_destroy(r_); }
     SparseRefiner(const SparseRefiner&) = delete;
@@ -150,6 +138,25 @@ public:
     }
 
 private:
+    void read_config() {
+        msc_sparse_config c{};
+        check(msc_refiner_config(r_, &c), "msc_refiner_config");
+        cfg_.present = true;
+        cfg_.in_channels = c.in_channels;
+        cfg_.out_channels = c.out_channels;
+        cfg_.encoder_channels = c.encoder_channels;
+        const int levels = c.num_levels < 0 ? 0 : (c.num_levels > MSC_REFINER_MAX_LEVELS ? MSC_REFINER_MAX_LEVELS
+                                                                                        : c.num_levels);
+        cfg_.model_channels.assign(c.model_channels, c.model_channels + levels);
+        cfg_.encoder_blocks.assign(c.encoder_blocks, c.encoder_blocks + levels);
+        const int inner = levels > 0 ? levels - 1 : 0;
+        cfg_.decoder_blocks.assign(c.decoder_blocks, c.decoder_blocks + inner);
+        cfg_.downsample_factors.assign(c.downsample_factors, c.downsample_factors + inner);
+        cfg_.bottleneck_blocks = c.bottleneck_blocks;
+        cfg_.encoder_downsample = c.encoder_downsample;
+        cfg_.depth_resolution = c.depth_resolution;
+    }
+
     msc_refiner_t r_ = nullptr;
     SparseConfig cfg_;
 };
