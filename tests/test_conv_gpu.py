@@ -115,7 +115,6 @@ def test_unsupported_channels_rejected(ex, oracle):
 
 def test_workspace_too_small_rejected(ex, oracle):
     import ctypes as C
-    from mogecpp_b200 import lib as L
     coords, x = _case(70, c=64)
     nbr = dev(oracle.make_level(coords))
     pw = ex.prepare_weight(weight_tensor(oracle, synth.conv_weight(71, 64, 64), "f32"), "f32", 64, 64, 27)
