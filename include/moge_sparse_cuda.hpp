@@ -57,8 +57,10 @@ public:
 
     msc_ctx_t handle() const noexcept { return ctx_; }
 
-    // Device-side status bits (MSC_DEV_*) raised since the last call; clears
-    // them.  Syncs the stream.
+    // Device-side status bits (MSC_DEV_*) raised since the last call, which
+    // it clears; throws Error (MSC_E_DEVICE) when any failure bit is set
+    // (MSC_DEV_DUP_COORD alone is informational and returned).  Syncs the
+    // stream.
     uint32_t status(void* stream = nullptr) const {
         uint32_t bits = 0;
         check(msc_check(ctx_, stream, &bits), "msc_check");
