@@ -97,8 +97,9 @@ PLAN_SORT_KERNELS = 6  # cub radix sort of 27-bit keys: histogram, scan, 4 digit
 # record clear, record fill), the neighbour map (brick kernel + the three
 # per-voxel fallback kernels, which return at once unless the bricks
 # overflow), the stride-2 maps (brick first-child scan, block scan, pool
-# fill, brick assign + six fallback kernels)
-TOPO_KERNELS = {"make_level": 8, "downsample": 14, "make_level_downsample": 18}
+# fill, brick assign + six fallback kernels); make_level_downsample's
+# neighbour kernel does the first-child scan, so it launches one fewer
+TOPO_KERNELS = {"make_level": 8, "downsample": 14, "make_level_downsample": 17}
 
 
 def load_peaks():
