@@ -92,7 +92,28 @@ CONV_DRAM_BYTES_PER_VOXEL = {("shell_4m", "ln"): 1302.0, ("res4_c128", "gn"): 86
 CONV_ALG_BYTES_PER_VOXEL = {"ln": ((144 + 112 + 144) + (144 + 112 + 256 + 256)) / 2.0,
                             "gn": ((144 + 112 + 512) + (144 + 112 + 256 + 256)) / 2.0}
 Q8_WEIGHT_BYTES = 27 * 128 * 128 + 27 * 4 * 128 * 4   # int8 codes + fp32 block scales per conv
-PLAN_SORT_KERNELS = 6  # cub radix sort of 27-bit keys: histogram, scan, 4 digit passes
+# cub::DeviceRadixSort on sm_100 (its Policy1000 tuning, 4-byte keys and
+# values): up to 256 x 19 items sort in one single-tile kernel; above that, a
+# histogram kernel, an exclusive-sum kernel and one onesweep kernel per 8-bit
+# digit
+CUB_SINGLE_TILE_ITEMS = 256 * 19
+PLAN_TILE_ROWS = 128
+
+
+def radix_sort_kernels(items, bits):
+    if items <= 0:
+        return 0
+    return 1 if items <= CUB_SINGLE_TILE_ITEMS else 2 + (bits + 7) // 8
+
+
+def plan_kernels(n):
+    """Kernels of one conv plan build over n output rows: header, mask keys,
+    the row sort (27-bit keys), tile lists, the tile schedule sort (8-bit
+    costs); the header alone for an empty level."""
+    if n <= 0:
+        return 1
+    tiles = (n + PLAN_TILE_ROWS - 1) // PLAN_TILE_ROWS
+    return 1 + 1 + radix_sort_kernels(n, 27) + 1 + radix_sort_kernels(tiles, 8)
 # kernels per topology call: the voxel table (table clear, brick insert,
 # record clear, record fill), the neighbour map (brick kernel + the three
 # per-voxel fallback kernels, which return at once unless the bricks
@@ -706,10 +727,11 @@ def build_refine(args, w, ex, dev):
                 "flops_note": "dense-equivalent 2*C*C*27*N per conv (the tap-skipping kernel does less)"}
 
     def launches(prof):
-        per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1}
+        # one plan per level and pass: the mean kernel count over the levels
+        per = {**TOPO_KERNELS, "plan_build": sum(plan_kernels(s) for s in sizes) / max(len(sizes), 1)}
         # + per pass: z quantisation (3), level-0 map, input rows, input_proj,
         # encoder rows, fuse_proj.0, SiLU, out_proj, log z update, key compare
-        return sum(per.get(k, 1) * v[0] for k, v in prof.items()) + 12 * args.steps
+        return round(sum(per.get(k, 1) * v[0] for k, v in prof.items())) + 12 * args.steps
 
     def cpu_baseline():
         threads = os.cpu_count() or 1
@@ -858,9 +880,9 @@ def build_stack(args, w, ex, dev, coords, rank, world):
 
     def launches(prof):
         # kernels per profiled family call: topology as TOPO_KERNELS;
-        # plan_build = header + mask keys + the radix sort's kernels + tile
-        # lists; gn_stats/finalize/act_prepare/conv_tc = 1
-        per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "halo": 0,
+        # plan_build over the rank's local rows (plan_kernels);
+        # gn_stats/finalize/act_prepare/conv_tc = 1
+        per = {**TOPO_KERNELS, "plan_build": plan_kernels(nl), "halo": 0,
                "halo_wait": 2 if peer else 1}  # wait + signal kernels per block
         return sum(per.get(k, 1) * v[0] for k, v in prof.items())
 
@@ -1044,7 +1066,7 @@ def build_other(args, w, ex, dev, coords):
 
         dtype = "fp32 (exact hi/lo fp16 split on tcgen05 kind::f16, fp32 accumulation)"
         cfg = {"step": "make_level + tap-order plan + 1 sparse conv", "channels": 64}
-        launches_per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1}
+        launches_per = {**TOPO_KERNELS, "plan_build": plan_kernels(n)}
     elif w.get("octant"):
         p = extra["p"]
         P = lambda k, ci, co, t: ex.prepare_weight(torch.from_numpy(p[k]).to(dev), "f32", ci, co, t)
@@ -1076,7 +1098,10 @@ def build_other(args, w, ex, dev, coords):
         dtype = "bf16 activations, fp32 weights (exact hi/lo fp16 split on tcgen05 kind::f16)"
         cfg = {"step": "make_level x2 + downsample + octant maps + conv 64 + octant strided conv 64->128 + conv 128 "
                        "+ octant transposed conv 128->64 + skip", "samples": 2, "coarse_voxels": int(n_coarse)}
-        launches_per = {**TOPO_KERNELS, "plan_build": 2 + PLAN_SORT_KERNELS + 1, "octant_maps": 2}
+        # two rectangular plans a step: the strided conv's (coarse rows) and
+        # the transposed conv's (fine rows)
+        launches_per = {**TOPO_KERNELS, "plan_build": (plan_kernels(n_coarse) + plan_kernels(n)) / 2,
+                        "octant_maps": 2}
     else:  # unet
         p = extra["p"]
         P = lambda k, ci, co, t: ex.prepare_weight(torch.from_numpy(p[k]).to(dev), "f32", ci, co, t)
@@ -1114,7 +1139,7 @@ def build_other(args, w, ex, dev, coords):
         return h_in, bufs, out_dev, h_out
 
     def launches(prof):
-        return sum(launches_per.get(k, 1) * v[0] for k, v in prof.items())
+        return round(sum(launches_per.get(k, 1) * v[0] for k, v in prof.items()))
 
     def cpu_baseline():
         if w.get("octant"):

@@ -79,3 +79,16 @@ def test_topology_kernel_counts_match_the_launch_code():
     assert (build, mp - 1, s2) == (4, 4, 10)
     assert bench.TOPO_KERNELS == {"make_level": build + mp - 1, "downsample": build + s2,
                                   "make_level_downsample": build + mp - 1 + s2 - 1}
+
+
+def test_plan_kernel_counts():
+    """A plan build launches header, mask keys, the 27-bit row sort, tile
+    lists and the 8-bit tile sort; cub sorts up to 256 x 19 items in one
+    kernel, else histogram + exclusive sum + one onesweep pass per 8 bits.
+    The launch lists agree: 5 onesweep launches per shell_4m step (24,576
+    tiles), 4 per res4_c128 step (2,851 tiles, single-tile schedule sort)."""
+    assert bench.plan_kernels(3145728) == 1 + 1 + 6 + 1 + 3
+    assert bench.plan_kernels(364846) == 1 + 1 + 6 + 1 + 1
+    assert bench.plan_kernels(4864) == 5 and bench.plan_kernels(4865) == 10
+    assert bench.plan_kernels(0) == 1
+    assert bench.radix_sort_kernels(24576, 8) - 2 == 1 and bench.radix_sort_kernels(3145728, 27) - 2 == 4
